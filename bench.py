@@ -1,0 +1,451 @@
+#!/usr/bin/env python
+"""Benchmark of the MXFP4 MoE hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload moe_decode|dequant] [--tokens T]
+
+Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
+  moe_decode  one MoE block forward over T tokens (default 8: the 8-token
+              gpt-oss-20b block — hidden 2880, 32 experts top-4, MXFP4
+              weights with E8M0 scales in [118, 126], bf16 activations).
+              Steps cycle over 4 uploaded layers (4 x 424 MB of packed
+              weights), so inputs are larger than L2 and no step finds the
+              previous step's weights cached. Metric: tokens/s.
+  dequant     standalone MXFP4 -> bf16 dequant of one layer's expert tensors
+              (32x5760x2880 + 32x2880x2880, E8M0 in [110, 135]). Metric: GB/s
+              of algorithmic traffic (423,014,400 B read + 1,592,524,800 B written).
+
+N > 1 runs one process per GPU (torchrun); every rank processes its own
+tokens through its own copy of the layer (replicas: no data-path collective),
+timing is max over ranks and ``value`` is the whole-job aggregate.
+
+``--impl reference`` times the reference's own CPU algorithm for the same
+workload (the oracle's REF-FAITHFUL restatement: f16 buffers, per-call
+weight conversion, sequential loops) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE tokens/s + HBM GB/s (decode), MXFP4 TFLOPS (prefill) at 1/2/4/8 B200"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel: str, key: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None."""
+    try:
+        with open(TRAFFIC_PATH) as f:
+            t = json.load(f)
+        return t[kernel][key]
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm, smax = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            sms.append(sm)
+            mx = smax
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sms)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def max_over_ranks(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws: int):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def emit(d: dict):
+    print(json.dumps(d), flush=True)
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle
+    from oxidized_gpt_oss_b200 import synth
+    threads = oracle.max_threads()
+    if args.workload == "dequant":
+        (w1, s1, r1, c1), _ = synth.dequant_tensors(seed=0)
+        rows = 5760 * 4  # bounded sample: 4 experts' mlp1 rows per step
+        blocks = w1.reshape(-1, c1 // 2)[:rows]
+        scales = s1.reshape(-1, c1 // 32)[:rows]
+        per_step_bytes = rows * c1 // 2 + rows * c1 // 32 + rows * c1 * 2
+        for _ in range(args.warmup):
+            oracle.dequantize_mxfp4_e8m0(blocks, scales, rows, c1)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            oracle.dequantize_mxfp4_e8m0(blocks, scales, rows, c1)
+        dt = time.perf_counter() - t0
+        value = per_step_bytes * args.steps / dt / 1e9
+        unit = "GB/s"
+        sample = f"{rows} rows x {c1} cols of mlp1 per step ({per_step_bytes} B algorithmic)"
+        config = {"workload": "dequant_layer", "rows": 32 * 5760 + 32 * 2880, "cols": 2880}
+    else:
+        T = args.tokens
+        d = synth.moe_layer(seed=0)
+        x = synth.activations(0, T, d["hidden"])
+        W = oracle.Weights(d)
+        L = oracle.RefLayer(W, x)
+        for _ in range(min(args.warmup, 1)):
+            L.forward(x, nthreads=threads)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            L.forward(x, nthreads=threads)
+        dt = time.perf_counter() - t0
+        value = T * args.steps / dt
+        unit = "tokens/s"
+        sample = f"{T} tokens of one MoE block per step (reference algorithm, OpenMP over tokens)"
+        config = moe_config(args, d)
+    emit({"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": ws,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic", "config": config,
+          "cpu_baseline": {"value": value, "unit": unit, "cores": min(threads, args.tokens)
+                           if args.workload != "dequant" else threads, "kind": "port", "sample": sample},
+          "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def moe_config(args, d):
+    return {"workload": "moe_block_decode", "tokens_per_gpu": args.tokens, "hidden": d["hidden"],
+            "intermediate": d["intermediate"], "experts": d["n_experts"], "top_k": d["top_k"],
+            "weights": "mxfp4 e2m1 + e8m0[118,126]", "layers_cycled": args.layers,
+            "l2": "inputs larger than L2: steps cycle over 4 layers x 424 MB of packed weights",
+            "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "single"}
+
+
+# --------------------------------------------------------------------------- our arm
+def cpu_baseline_moe(d, x, T):
+    from oracle import oracle
+    W = oracle.Weights(d)
+    L = oracle.RefLayer(W, x)
+    t0 = time.perf_counter()
+    L.forward(x, nthreads=1)
+    dt = time.perf_counter() - t0
+    L.close()
+    return {"value": T / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"one forward of {T} tokens through one MoE block, single thread (the reference's "
+                      f"algorithm as written), {dt:.2f} s"}
+
+
+def gpu_layers(args, d0, device):
+    """Layer 0 from the numpy generator; the rest from a seeded torch generator
+    on the device (same shapes and distributions)."""
+    import torch
+    layers = [d0]
+    H, I, E = d0["hidden"], d0["intermediate"], d0["n_experts"]
+    for li in range(1, args.layers):
+        g = torch.Generator(device=device)
+        g.manual_seed(1000 + li)
+        def u8(shape, lo, hi):
+            return torch.randint(lo, hi + 1, shape, generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+        def bf16(shape, std):
+            return (torch.randn(shape, generator=g, device=device) * std).to(torch.bfloat16).view(torch.int16)
+        layers.append(dict(d0, router_w=bf16((E, H), 0.02), router_b=bf16((E,), 0.01),
+                           w1_blocks=u8((E, 2 * I, H // 2), 0, 255), w1_scales=u8((E, 2 * I, H // 32), 118, 126),
+                           b1=bf16((E, 2 * I), 0.01), w2_blocks=u8((E, H, I // 2), 0, 255),
+                           w2_scales=u8((E, H, I // 32), 118, 126), b2=bf16((E, H), 0.01)))
+    return layers
+
+
+def run_moe(args, ws, rank, local):
+    import torch
+    from oxidized_gpt_oss_b200 import abi, synth
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    from oxidized_gpt_oss_b200.mxfp4 import context
+
+    device = torch.device("cuda", local)
+    T = args.tokens
+    d0 = synth.moe_layer(seed=0)
+    H, I, E, K = d0["hidden"], d0["intermediate"], d0["n_experts"], d0["top_k"]
+    ctx = context(None)
+    layers = [MoELayer(d, ctx=ctx, layer=i) for i, d in enumerate(gpu_layers(args, d0, device))]
+    for L in layers:
+        L.reserve(T)
+    n_x = 16
+    xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
+    xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
+    ys = [torch.empty((T, H), dtype=torch.float32, device=device) for _ in range(2)]
+
+    def step(i):
+        layers[i % len(layers)].forward(xs[i % n_x], out=ys[i % 2])
+
+    # distinct experts each step reads (routing is deterministic per (layer, x))
+    distinct = {}
+    for i in range(args.steps):
+        key = (i % len(layers), i % n_x)
+        if key not in distinct:
+            idx, _, _ = layers[key[0]].route(xs[key[1]])
+            distinct[key] = int(torch.unique(idx).numel())
+    hits = sum(distinct[(i % len(layers), i % n_x)] for i in range(args.steps))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ctx.profile(True)
+    ctx.profile_reset()
+    launches0 = ctx.launches()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+    ms = ev0.elapsed_time(ev1)
+    launches = ctx.launches() - launches0
+    k_ms = {n: ctx.profile_read(n) for n in ("router_topk", "permute", "moe_mlp1_decode", "moe_mlp2_decode",
+                                              "combine")}
+    ctx.profile(False)
+    ms_max = max_over_ranks(ms, ws)
+
+    # roofline of the dominant kernel (mlp1: gate/up projection + SwiGLU)
+    mlp1_w = 2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2
+    mlp2_w = H * I // 2 + H * I // 32 + H * 2
+    mlp1_bytes = hits * mlp1_w + args.steps * (T * H * 2 + T * K * I * 4)
+    mlp2_bytes = hits * mlp2_w + args.steps * (T * K * I * 4 + T * K * H * 4)
+    layer_bytes = mlp1_bytes + mlp2_bytes + args.steps * (E * H * 2 + T * H * 4)
+    hbm, hbm_kind = peaks()
+    m1_ms, m1_n = k_ms["moe_mlp1_decode"]
+    m2_ms, m2_n = k_ms["moe_mlp2_decode"]
+    achieved = mlp1_bytes / (m1_ms * 1e-3) / 1e9
+    traffic = ncu_traffic("moe_mlp1_decode", f"T{T}")
+
+    # end to end through the host-buffer API: pinned x in, y out, every step
+    xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
+    yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    for i in range(args.warmup):
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh)
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh)
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    barrier(ws)
+    e2e_ms = max_over_ranks(e2e_ms, ws)
+
+    out = {"metric": METRIC, "value": T * ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "mxfp4 weights x bf16 activations (exact f16 MMA operands), f32 accumulate",
+           "data": "synthetic", "config": moe_config(args, d0),
+           "roofline": {"bound": "hbm", "kernel": "moe_mlp1_decode", "achieved": achieved, "peak": hbm,
+                        "peak_kind": hbm_kind, "unit": "GB/s", "frac": achieved / hbm,
+                        "traffic": traffic,
+                        "algorithmic_bytes_per_launch": mlp1_bytes / max(m1_n, 1),
+                        "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3,
+                        "distinct_experts_per_step": hits / args.steps},
+           "layer": {"hbm_gbs": layer_bytes / (ms * 1e-3) / 1e9, "frac": layer_bytes / (ms * 1e-3) / 1e9 / hbm,
+                     "kernel_us_per_step": {n: v[0] / max(v[1], 1) * 1e3 for n, v in k_ms.items()},
+                     "mlp2_gbs": mlp2_bytes / (m2_ms * 1e-3) / 1e9},
+           "e2e": {"value": T * ws * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
+           "gpu_launches": launches,
+           "clocks": clk.summary()}
+    if rank == 0 and ws == 1:
+        out["cpu_baseline"] = cpu_baseline_moe(d0, xs_np[0], T)
+    return out
+
+
+def run_dequant(args, ws, rank, local):
+    import torch
+    from oxidized_gpt_oss_b200 import synth
+    from oxidized_gpt_oss_b200.mxfp4 import context, dequantize_mxfp4
+    device = torch.device("cuda", local)
+    (w1, s1, r1, c1), (w2, s2, r2, c2) = synth.dequant_tensors(seed=rank)
+    tens = [(torch.from_numpy(w).to(device), torch.from_numpy(s).to(device), r, c)
+            for w, s, r, c in ((w1, s1, r1, c1), (w2, s2, r2, c2))]
+    outs = [torch.empty(r * c, dtype=torch.int16, device=device) for _, _, r, c in tens]
+    read_b = sum(w.numel() + s.numel() for w, s, _, _ in tens)
+    write_b = sum(o.numel() * 2 for o in outs)
+    ctx = context(None)
+
+    def step():
+        for (b, s, r, c), o in zip(tens, outs):
+            dequantize_mxfp4(b, s, r, c, ctx=ctx, out=o)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.profile(True)
+    ctx.profile_reset()
+    launches0 = ctx.launches()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), ws)
+    k_ms, k_n = ctx.profile_read("dequant_mxfp4")
+    launches = ctx.launches() - launches0
+    ctx.profile(False)
+    hbm, hbm_kind = peaks()
+    total = (read_b + write_b) * args.steps
+    achieved = total / (k_ms * 1e-3) / 1e9
+    # e2e: host codes+scales in, bf16 out, every step
+    hb = [(w.cpu().pin_memory(), s.cpu().pin_memory()) for w, s, _, _ in tens]
+    ho = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for (b, s), (db, ds, r, c), o, h in zip(hb, tens, outs, ho):
+            db.copy_(b, non_blocking=True)
+            ds.copy_(s, non_blocking=True)
+            dequantize_mxfp4(db, ds, r, c, ctx=ctx, out=o)
+            h.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
+    out = {"metric": METRIC, "value": total * ws / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": ws,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8->bf16",
+           "data": "synthetic",
+           "config": {"workload": "dequant_layer", "elements": (r1 * c1 + r2 * c2),
+                      "l2": "inputs larger than L2 (423 MB in, 1.59 GB out per step)"},
+           "roofline": {"bound": "hbm", "kernel": "dequant_mxfp4", "achieved": achieved, "peak": hbm,
+                        "peak_kind": hbm_kind, "unit": "GB/s", "frac": achieved / hbm,
+                        "traffic": ncu_traffic("dequant_mxfp4", "layer"),
+                        "avg_launch_us": k_ms / max(k_n, 1) * 1e3},
+           "e2e": {"value": total * ws / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": read_b,
+                   "d2h_bytes_per_step": write_b},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    if rank == 0 and ws == 1:
+        from oracle import oracle
+        rows = 5760 * 2
+        t0 = time.perf_counter()
+        oracle.dequantize_mxfp4_e8m0(w1.reshape(-1, c1 // 2)[:rows], s1.reshape(-1, c1 // 32)[:rows], rows, c1)
+        dt = time.perf_counter() - t0
+        nb = rows * c1 // 2 + rows * c1 // 32 + rows * c1 * 2
+        out["cpu_baseline"] = {"value": nb / dt / 1e9, "unit": "GB/s", "cores": oracle.max_threads(),
+                               "kind": "port", "sample": f"{rows} rows of mlp1 ({nb} B algorithmic), OpenMP"}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["moe_decode", "dequant"], default="moe_decode")
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=4)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    try:
+        out = run_dequant(args, ws, rank, local) if args.workload == "dequant" else run_moe(args, ws, rank, local)
+        if rank == 0:
+            emit(out)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

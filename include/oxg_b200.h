@@ -1,0 +1,173 @@
+/*
+ * oxg_b200.h — C ABI of liboxg_b200.so, the B200 (sm_100a) MXFP4
+ * mixture-of-experts hot path of the gpt-oss runner cipher-rc5/oxidized_gpt_oss.
+ *
+ * The reference has no FFI: its "backend" is a compile-time module swap
+ * (src/backend/mod.rs:5-10) between a Metal implementation and a host-memory
+ * stub, and its hot path is host Rust (src/moe.rs, src/mxfp4.rs, src/ffn.rs,
+ * src/model.rs:1088-1184). Each entry point below names the reference
+ * interface it replaces. Conventions:
+ *
+ *  - Every function returns an int status: 0 (OXG_OK) or a negative
+ *    oxg_status. Nothing aborts the process where the reference panics on a
+ *    shape assert: the same condition returns OXG_ERR_SHAPE and
+ *    oxg_last_error() holds the reference's message text.
+ *  - Pointers named *_dev are device pointers (any CUDA allocation visible to
+ *    the context's device); *_host are host pointers; upload accepts either.
+ *  - Work is enqueued on the context's stream and is asynchronous unless the
+ *    function says otherwise; oxg_sync() waits for it.
+ *  - A context is used by one host thread at a time.
+ *  - bf16 values travel as uint16_t bit patterns.
+ */
+#ifndef OXG_B200_H
+#define OXG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OXG_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define OXG_API __attribute__((visibility("default")))
+#else
+#define OXG_API
+#endif
+
+typedef enum {
+  OXG_OK = 0,
+  OXG_ERR_INVALID_ARG = -1,
+  OXG_ERR_SHAPE = -2,
+  OXG_ERR_CUDA = -3,
+  OXG_ERR_NCCL = -4,
+  OXG_ERR_TIMEOUT = -5,
+  OXG_ERR_STATE = -6,
+  OXG_ERR_UNSUPPORTED = -7,
+  OXG_ERR_OOM = -8
+} oxg_status;
+
+enum { OXG_SCALE_E8M0 = 0, OXG_SCALE_BF16 = 1 };
+enum { OXG_MODE_AUTO = 0, OXG_MODE_DECODE = 1, OXG_MODE_PREFILL = 2 };
+enum { OXG_PRECISION_PARITY = 0 };
+
+typedef struct oxg_ctx oxg_ctx;
+
+/* ---- library / context --------------------------------------------------- */
+
+OXG_API int oxg_abi_version(void);
+OXG_API const char *oxg_status_string(int status);
+
+/* Replaces MetalDevice::new + MetalCompute::new (src/backend/metal_stub.rs:31-34,
+ * :92-95): binds a CUDA device and creates the context's stream. */
+OXG_API int oxg_ctx_create(int device, oxg_ctx **out);
+OXG_API int oxg_ctx_destroy(oxg_ctx *ctx);
+/* Message of the last failing call on ctx (or of the last failing
+ * context-less call on this thread when ctx is NULL). Never NULL. */
+OXG_API const char *oxg_last_error(const oxg_ctx *ctx);
+/* Runs the context's work on `stream` (a cudaStream_t) instead of its own;
+ * NULL restores the context's stream. */
+OXG_API int oxg_ctx_set_stream(oxg_ctx *ctx, void *stream);
+OXG_API void *oxg_ctx_get_stream(const oxg_ctx *ctx);
+/* Replaces MetalDevice::synchronize (src/backend/metal_stub.rs:46-48). */
+OXG_API int oxg_sync(oxg_ctx *ctx);
+
+/* ---- MXFP4 dequantisation ------------------------------------------------ */
+
+/* Replaces dequantize_mxfp4(blocks: &[u8], scales: &[u16], rows, cols) -> Vec<u16>
+ * (src/mxfp4.rs:15-54, called from src/loader.rs:66). Device pointers;
+ * n_block_bytes / n_scales are the slice lengths the reference asserts
+ * (rows*cols/2 and rows*cols/32). scale_fmt OXG_SCALE_BF16 takes bf16 bit
+ * patterns as the reference does; OXG_SCALE_E8M0 takes the checkpoint's
+ * uint8 E8M0 bytes (2^(e-127), 0 -> 0.0 as F8E8M0::to_f32, src/dtype.rs:245-252).
+ * out_dev receives rows*cols bf16 values, bit-exact with the reference. */
+OXG_API int oxg_dequant_mxfp4(oxg_ctx *ctx, const uint8_t *blocks_dev, size_t n_block_bytes,
+                              const void *scales_dev, size_t n_scales, int scale_fmt, size_t rows,
+                              size_t cols, uint16_t *out_dev);
+
+/* ---- SwiGLU -------------------------------------------------------------- */
+
+/* Replaces ffn::swiglu(gate, up) (src/ffn.rs:5-13) with the clamped gpt-oss
+ * form: g <- min(g, limit); u <- clamp(u, -limit, limit);
+ * out = g * sigmoid(alpha * g) * (u + 1). Device f32 arrays of n elements. */
+OXG_API int oxg_swiglu(oxg_ctx *ctx, const float *gate_dev, const float *up_dev, size_t n,
+                       float alpha, float limit, float *out_dev);
+
+/* ---- MoE layer ----------------------------------------------------------- */
+
+typedef struct {
+  int hidden;         /* H (2880 for gpt-oss-20b); multiple of 32 */
+  int intermediate;   /* I (2880); multiple of 32; mlp1 has 2*I rows */
+  int n_experts;      /* E (32); <= 256 */
+  int top_k;          /* k (4; the reference hard-codes 4, src/moe.rs:56); <= 16 */
+  float swiglu_alpha; /* 1.702 */
+  float swiglu_limit; /* 7.0; 0 < limit <= 128 */
+} oxg_moe_dims;
+
+typedef struct {
+  const uint16_t *router_w;  /* [E, H] bf16 ("mlp.router.weight", src/model.rs:239) */
+  const uint16_t *router_b;  /* [E] bf16, or NULL for no bias */
+  const uint8_t *w1_blocks;  /* [E, 2I, H/2] packed E2M1 ("mlp1_weight.blocks"), gate/up rows interleaved */
+  const uint8_t *w1_scales;  /* [E, 2I, H/32] E8M0 */
+  const uint16_t *b1;        /* [E, 2I] bf16 */
+  const uint8_t *w2_blocks;  /* [E, H, I/2] */
+  const uint8_t *w2_scales;  /* [E, H, I/32] */
+  const uint16_t *b2;        /* [E, H] bf16 */
+} oxg_moe_weights;
+
+/* Replaces the MoE branch of load_transformer_layer (src/model.rs:238-359)
+ * and the dequantising loader path (src/loader.rs:42-73): copies one layer's
+ * packed weights (host or device pointers) into library-owned device memory,
+ * still packed (no bf16 materialisation). Synchronous. Re-uploading a layer
+ * replaces it. */
+OXG_API int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims,
+                           const oxg_moe_weights *w);
+OXG_API int oxg_moe_release(oxg_ctx *ctx, int layer);
+
+/* Pre-sizes the context's scratch memory for n_tokens tokens of `layer`, so
+ * that later forwards of at most that many tokens allocate nothing. */
+OXG_API int oxg_moe_reserve(oxg_ctx *ctx, int layer, int n_tokens);
+
+/* Replaces MoELayer::forward(&self, hidden: &MetalBuffer, compute) -> Result<MetalBuffer>
+ * (src/moe.rs:16-100): router + top-k + softmax, permutation, expert MLPs
+ * with clamped SwiGLU, weighted combine. x_dev: [n_tokens, H] bf16;
+ * y_dev: [n_tokens, H] f32. mode: OXG_MODE_AUTO or OXG_MODE_DECODE (the
+ * in-register-dequant tensor-core path); precision: OXG_PRECISION_PARITY. */
+OXG_API int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_tokens,
+                            float *y_dev, int mode, int precision);
+
+/* The same from host memory (pinned for full speed): copies x in, runs the
+ * layer, copies y out and waits. This is the call a host-side runner makes. */
+OXG_API int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int n_tokens,
+                                 float *y_host, int mode, int precision);
+
+/* Routing tap (src/moe.rs:40-73): idx_dev [n_tokens, k] int32 expert ids in
+ * selection order, w_dev [n_tokens, k] f32 softmax weights; logits_dev
+ * [n_tokens, E] f32 may be NULL. */
+OXG_API int oxg_moe_route(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_tokens,
+                          int32_t *idx_dev, float *w_dev, float *logits_dev);
+
+/* Per-expert token counts of the last forward on this context (host array of
+ * E ints). Waits for the context's stream. */
+OXG_API int oxg_moe_last_counts(oxg_ctx *ctx, int32_t *counts_host, int n_experts);
+
+/* ---- measurement (no reference counterpart: the reference's only timing is
+ * the --bench wall clock of src/main.rs:159-164) --------------------------- */
+
+/* When on, every kernel this context launches is bracketed by CUDA events on
+ * the launching stream. */
+OXG_API int oxg_profile_enable(oxg_ctx *ctx, int on);
+/* Total device time (ms) and launch count of kernel `name` since the last
+ * reset (names: router_topk, permute, moe_mlp1_decode, moe_mlp2_decode,
+ * combine, dequant_mxfp4, swiglu). Waits for the context's stream. */
+OXG_API int oxg_profile_read(oxg_ctx *ctx, const char *name, double *total_ms, int *launches);
+OXG_API int oxg_profile_reset(oxg_ctx *ctx);
+/* Number of kernels this context has launched since it was created. */
+OXG_API int oxg_kernel_launches(const oxg_ctx *ctx, long long *count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OXG_B200_H */

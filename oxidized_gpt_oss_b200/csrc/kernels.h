@@ -1,0 +1,74 @@
+// kernels.h — host-side launchers of the sm_100a kernels (internal to the
+// library; the public surface is include/oxg_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace oxg {
+
+// ---- dequant (dequant.cu) ---------------------------------------------------
+// out[i] = bf16(e2m1(code_i) * scale[i / 32]) over n_blocks 32-element blocks.
+// scale_fmt: 0 = E8M0 bytes, 1 = bf16 bit patterns.
+cudaError_t launch_dequant_mxfp4(const uint8_t *codes, const void *scales, int scale_fmt,
+                                 size_t n_blocks, uint16_t *out, cudaStream_t stream);
+
+// ---- SwiGLU (swiglu.cu) -----------------------------------------------------
+cudaError_t launch_swiglu(const float *gate, const float *up, size_t n, float alpha, float limit,
+                          float *out, cudaStream_t stream);
+
+// ---- weight re-layout (relayout.cu) ----------------------------------------
+// Packed codes [rows, K/2] in the checkpoint order -> the "word-transposed"
+// order the MoE kernels read (see moe_layout.h). scales [rows, K/32] ->
+// [rows, kb_pad] with kb_pad = round_up(K/32, 4), padding bytes zero.
+cudaError_t launch_relayout_codes(const uint8_t *src, uint8_t *dst, size_t rows, int K,
+                                  cudaStream_t stream);
+cudaError_t launch_pad_scales(const uint8_t *src, uint8_t *dst, size_t rows, int K,
+                              cudaStream_t stream);
+
+// ---- routing (router.cu) ----------------------------------------------------
+// logits may be null. sigma[T] receives the per-token power-of-two exponent
+// that puts max|x| * 2^-sigma in [2^14, 2^15) (f16 operand range).
+cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
+                               int E, int k, int32_t *idx, float *wts, float *logits,
+                               int32_t *sigma, cudaStream_t stream);
+
+// ---- permutation (permute.cu) -------------------------------------------------
+// Stable counting sort of the T*k (token, j) slots by expert.
+//   counts[E], offsets[E+1], perm[T*k] (position -> slot), slot_pos[T*k]
+//   (slot -> position). expert_lo/expert_hi restrict to a local expert range
+//   (experts outside it are counted but are not "local").
+cudaError_t launch_permute(const int32_t *idx, int n_slots, int E, int32_t *counts,
+                           int32_t *offsets, int32_t *perm, int32_t *slot_pos,
+                           cudaStream_t stream);
+
+// ---- decode MoE (moe_decode.cu) ---------------------------------------------
+struct MoeDeviceWeights {
+  int H, I, E, k;
+  float alpha, limit;
+  const uint16_t *router_w, *router_b;
+  const uint8_t *w1, *s1;  // relaid codes [E, 2I, H/2], padded scales [E, 2I, kb1]
+  const uint16_t *b1;      // [E, 2I]
+  const uint8_t *w2, *s2;  // [E, H, I/2], [E, H, kb2]
+  const uint16_t *b2;      // [E, H]
+};
+
+// mlp1 + bias + clamped SwiGLU for every (expert, slot) -> h [n_slots, I] f32
+// (rows in expert-sorted position order). x_rows maps a position to the row
+// of x holding its token (i.e. perm[p] / k).
+cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
+                                   const int32_t *perm, const int32_t *sigma,
+                                   const int32_t *counts, const int32_t *offsets, int n_slots,
+                                   int expert_base, int n_local_experts, float *h,
+                                   cudaStream_t stream);
+// mlp2 + bias -> y_slot [n_slots, H] f32 (position order)
+cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
+                                   const int32_t *counts, const int32_t *offsets, int n_slots,
+                                   int expert_base, int n_local_experts, float *y_slot,
+                                   cudaStream_t stream);
+// out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
+cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,
+                           int H, int k, float *out, cudaStream_t stream);
+
+}  // namespace oxg

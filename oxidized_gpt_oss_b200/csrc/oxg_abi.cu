@@ -1,0 +1,648 @@
+// oxg_abi.cu — the C ABI of liboxg_b200.so (declared in include/oxg_b200.h).
+//
+// Host-side runtime: contexts (device + stream + scratch), the per-layer weight
+// registry, argument validation with the reference's error texts, and the
+// launch sequence of one MoE layer. No entry point throws across the ABI.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/oxg_b200.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_tls_error = "";
+
+struct Layer {
+  bool present = false;
+  oxg_moe_dims dims{};
+  void *block = nullptr;  // one allocation holding everything below
+  uint16_t *router_w = nullptr, *router_b = nullptr;
+  uint8_t *w1 = nullptr, *s1 = nullptr, *w2 = nullptr, *s2 = nullptr;
+  uint16_t *b1 = nullptr, *b2 = nullptr;
+};
+
+struct Scratch {
+  void *base = nullptr;
+  size_t bytes = 0;
+  int32_t *idx = nullptr, *sigma = nullptr, *counts = nullptr, *offsets = nullptr;
+  int32_t *perm = nullptr, *slot_pos = nullptr;
+  float *wts = nullptr, *logits = nullptr, *h = nullptr, *y_slot = nullptr;
+  uint16_t *x_stage = nullptr;
+  float *y_stage = nullptr;
+};
+
+// CUDA-event brackets around kernel launches, read back on demand.
+struct Profiler {
+  bool on = false;
+  struct Rec {
+    const char *name;
+    cudaEvent_t start, stop;
+  };
+  std::vector<Rec> recs;       // pending brackets since the last read/reset
+  std::vector<cudaEvent_t> pool;
+  struct Sum {
+    std::string name;
+    double ms = 0.0;
+    int launches = 0;
+  };
+  std::vector<Sum> sums;
+
+  cudaEvent_t get() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+  Sum &sum(const char *name) {
+    for (Sum &s : sums)
+      if (s.name == name) return s;
+    sums.push_back(Sum{name, 0.0, 0});
+    return sums.back();
+  }
+  // Folds finished brackets into the sums (the caller has synchronised).
+  void drain() {
+    for (Rec &r : recs) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, r.start, r.stop) == cudaSuccess) {
+        Sum &s = sum(r.name);
+        s.ms += ms;
+        s.launches += 1;
+      }
+      pool.push_back(r.start);
+      pool.push_back(r.stop);
+    }
+    recs.clear();
+  }
+  void destroy() {
+    drain();
+    for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    pool.clear();
+  }
+};
+
+}  // namespace
+
+struct oxg_ctx {
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string error;
+  std::vector<Layer> layers;
+  Scratch ws;
+  int last_layer = -1;
+  long long launches = 0;
+  Profiler prof;
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int fail(oxg_ctx *ctx, int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (ctx)
+    ctx->error = buf;
+  else
+    g_tls_error = buf;
+  return status;
+}
+
+int cuda_fail(oxg_ctx *ctx, cudaError_t st, const char *what) {
+  return fail(ctx, st == cudaErrorMemoryAllocation ? OXG_ERR_OOM : OXG_ERR_CUDA, "%s: %s (%s)",
+              what, cudaGetErrorName(st), cudaGetErrorString(st));
+}
+
+#define OXG_CUDA(ctx, call, what)                      \
+  do {                                                 \
+    cudaError_t st_ = (call);                          \
+    if (st_ != cudaSuccess) return cuda_fail(ctx, st_, what); \
+  } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int check_dims(oxg_ctx *ctx, const oxg_moe_dims *d) {
+  if (!d) return fail(ctx, OXG_ERR_INVALID_ARG, "dims is NULL");
+  if (d->hidden <= 0 || d->hidden % 32)
+    return fail(ctx, OXG_ERR_SHAPE, "hidden must be a positive multiple of 32, got %d", d->hidden);
+  if (d->intermediate <= 0 || d->intermediate % 32)
+    return fail(ctx, OXG_ERR_SHAPE, "intermediate must be a positive multiple of 32, got %d",
+                d->intermediate);
+  if (d->n_experts <= 0 || d->n_experts > 256)
+    return fail(ctx, OXG_ERR_SHAPE, "n_experts must be in [1, 256], got %d", d->n_experts);
+  if (d->top_k <= 0 || d->top_k > 16 || d->top_k > d->n_experts)
+    return fail(ctx, OXG_ERR_SHAPE, "top_k must be in [1, min(16, n_experts)], got %d", d->top_k);
+  if (!(d->swiglu_limit > 0.f) || d->swiglu_limit > 128.f)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "swiglu_limit must be in (0, 128], got %g",
+                (double)d->swiglu_limit);
+  return OXG_OK;
+}
+
+// Scratch layout for T tokens of a layer with dims d.
+size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
+  const size_t S = (size_t)T * d.top_k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes, 256);
+    return base ? base + o : nullptr;
+  };
+  char *p_idx = take(S * 4), *p_wts = take(S * 4), *p_sigma = take((size_t)T * 4);
+  char *p_logits = take((size_t)T * d.n_experts * 4);
+  char *p_counts = take((size_t)d.n_experts * 4), *p_offsets = take(((size_t)d.n_experts + 1) * 4);
+  char *p_perm = take(S * 4), *p_slot = take(S * 4);
+  char *p_h = take(S * d.intermediate * 4), *p_y = take(S * d.hidden * 4);
+  char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
+  if (s && base) {
+    s->idx = (int32_t *)p_idx;
+    s->wts = (float *)p_wts;
+    s->sigma = (int32_t *)p_sigma;
+    s->logits = (float *)p_logits;
+    s->counts = (int32_t *)p_counts;
+    s->offsets = (int32_t *)p_offsets;
+    s->perm = (int32_t *)p_perm;
+    s->slot_pos = (int32_t *)p_slot;
+    s->h = (float *)p_h;
+    s->y_slot = (float *)p_y;
+    s->x_stage = (uint16_t *)p_xs;
+    s->y_stage = (float *)p_ys;
+  }
+  return off;
+}
+
+int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
+  const int Tc = T < 1 ? 1 : T;
+  const size_t need = scratch_bytes(d, Tc, nullptr, nullptr);
+  if (need <= ctx->ws.bytes) {
+    scratch_bytes(d, Tc, &ctx->ws, (char *)ctx->ws.base);
+    return OXG_OK;
+  }
+  if (ctx->ws.base) {
+    OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    cudaFree(ctx->ws.base);
+    ctx->ws = Scratch{};
+  }
+  void *p = nullptr;
+  OXG_CUDA(ctx, cudaMalloc(&p, need), "cudaMalloc(scratch)");
+  ctx->ws.base = p;
+  ctx->ws.bytes = need;
+  scratch_bytes(d, Tc, &ctx->ws, (char *)p);
+  return OXG_OK;
+}
+
+Layer *get_layer(oxg_ctx *ctx, int layer) {
+  if (layer < 0 || layer >= (int)ctx->layers.size() || !ctx->layers[layer].present) return nullptr;
+  return &ctx->layers[layer];
+}
+
+void free_layer(Layer &L) {
+  if (L.block) cudaFree(L.block);
+  L = Layer{};
+}
+
+oxg::MoeDeviceWeights device_weights(const Layer &L) {
+  oxg::MoeDeviceWeights w{};
+  w.H = L.dims.hidden;
+  w.I = L.dims.intermediate;
+  w.E = L.dims.n_experts;
+  w.k = L.dims.top_k;
+  w.alpha = L.dims.swiglu_alpha;
+  w.limit = L.dims.swiglu_limit;
+  w.router_w = L.router_w;
+  w.router_b = L.router_b;
+  w.w1 = L.w1;
+  w.s1 = L.s1;
+  w.b1 = L.b1;
+  w.w2 = L.w2;
+  w.s2 = L.s2;
+  w.b2 = L.b2;
+  return w;
+}
+
+// Runs one kernel launcher, counting the launch and, when profiling is on,
+// bracketing it with CUDA events on the context's stream.
+template <class F>
+cudaError_t launch(oxg_ctx *ctx, const char *name, F &&fn) {
+  cudaEvent_t a = nullptr;
+  if (ctx->prof.on) {
+    a = ctx->prof.get();
+    cudaEventRecord(a, ctx->stream);
+  }
+  cudaError_t st = fn();
+  if (st == cudaSuccess) ctx->launches += 1;
+  if (ctx->prof.on) {
+    cudaEvent_t b = ctx->prof.get();
+    cudaEventRecord(b, ctx->stream);
+    ctx->prof.recs.push_back(Profiler::Rec{name, a, b});
+  }
+  return st;
+}
+
+int route(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, int32_t *idx, float *wts,
+          float *logits) {
+  const oxg_moe_dims &d = L.dims;
+  OXG_CUDA(ctx, launch(ctx, "router_topk", [&] {
+             return oxg::launch_router_topk(x, L.router_w, L.router_b, T, d.hidden, d.n_experts,
+                                            d.top_k, idx, wts, logits, ctx->ws.sigma, ctx->stream);
+           }),
+           "router_topk launch");
+  return OXG_OK;
+}
+
+int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
+  const oxg_moe_dims &d = L.dims;
+  const int S = T * d.top_k;
+  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
+  if (rc) return rc;
+  OXG_CUDA(ctx, launch(ctx, "permute", [&] {
+             return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts,
+                                        ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos,
+                                        ctx->stream);
+           }),
+           "permute launch");
+  const oxg::MoeDeviceWeights w = device_weights(L);
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp1_decode", [&] {
+             return oxg::launch_moe_mlp1_decode(w, x, ctx->ws.perm, ctx->ws.sigma, ctx->ws.counts,
+                                                ctx->ws.offsets, S, 0, d.n_experts, ctx->ws.h,
+                                                ctx->stream);
+           }),
+           "mlp1 launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp2_decode", [&] {
+             return oxg::launch_moe_mlp2_decode(w, ctx->ws.h, ctx->ws.counts, ctx->ws.offsets, S,
+                                                0, d.n_experts, ctx->ws.y_slot, ctx->stream);
+           }),
+           "mlp2 launch");
+  OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+             return oxg::launch_combine(ctx->ws.y_slot, ctx->ws.slot_pos, ctx->ws.wts, T,
+                                        d.hidden, d.top_k, y, ctx->stream);
+           }),
+           "combine launch");
+  return OXG_OK;
+}
+
+int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void *y, int mode,
+                       int precision, Layer **out) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
+  if (T > 0 && (!x || !y)) return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be non-NULL");
+  if (mode != OXG_MODE_AUTO && mode != OXG_MODE_DECODE && mode != OXG_MODE_PREFILL)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "unknown mode %d", mode);
+  if (mode == OXG_MODE_PREFILL)
+    return fail(ctx, OXG_ERR_UNSUPPORTED, "prefill mode is not available in this build");
+  if (precision != OXG_PRECISION_PARITY)
+    return fail(ctx, OXG_ERR_UNSUPPORTED, "unknown precision %d", precision);
+  *out = L;
+  return OXG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int oxg_abi_version(void) { return OXG_ABI_VERSION; }
+
+const char *oxg_status_string(int status) {
+  switch (status) {
+    case OXG_OK: return "ok";
+    case OXG_ERR_INVALID_ARG: return "invalid argument";
+    case OXG_ERR_SHAPE: return "shape mismatch";
+    case OXG_ERR_CUDA: return "CUDA error";
+    case OXG_ERR_NCCL: return "NCCL error";
+    case OXG_ERR_TIMEOUT: return "timeout";
+    case OXG_ERR_STATE: return "invalid state";
+    case OXG_ERR_UNSUPPORTED: return "unsupported";
+    case OXG_ERR_OOM: return "out of device memory";
+    default: return "unknown status";
+  }
+}
+
+int oxg_ctx_create(int device, oxg_ctx **out) {
+  if (!out) return fail(nullptr, OXG_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t st = cudaGetDeviceCount(&n);
+  if (st != cudaSuccess) return cuda_fail(nullptr, st, "cudaGetDeviceCount");
+  if (device < 0 || device >= n)
+    return fail(nullptr, OXG_ERR_INVALID_ARG, "device %d out of range (%d devices)", device, n);
+  DeviceGuard g(device);
+  if (!g.ok) return fail(nullptr, OXG_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  cudaDeviceProp prop;
+  st = cudaGetDeviceProperties(&prop, device);
+  if (st != cudaSuccess) return cuda_fail(nullptr, st, "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(nullptr, OXG_ERR_UNSUPPORTED,
+                "device %d is sm_%d%d; this library is built for sm_100a (B200) only", device,
+                prop.major, prop.minor);
+  oxg_ctx *ctx = new (std::nothrow) oxg_ctx();
+  if (!ctx) return fail(nullptr, OXG_ERR_OOM, "host allocation failed");
+  ctx->device = device;
+  st = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+  if (st != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(nullptr, st, "cudaStreamCreate");
+  }
+  ctx->stream = ctx->own_stream;
+  *out = ctx;
+  return OXG_OK;
+}
+
+int oxg_ctx_destroy(oxg_ctx *ctx) {
+  if (!ctx) return OXG_OK;
+  DeviceGuard g(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (Layer &L : ctx->layers) free_layer(L);
+  if (ctx->ws.base) cudaFree(ctx->ws.base);
+  ctx->prof.destroy();
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return OXG_OK;
+}
+
+const char *oxg_last_error(const oxg_ctx *ctx) {
+  return ctx ? ctx->error.c_str() : g_tls_error.c_str();
+}
+
+int oxg_ctx_set_stream(oxg_ctx *ctx, void *stream) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+  return OXG_OK;
+}
+
+void *oxg_ctx_get_stream(const oxg_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int oxg_sync(oxg_ctx *ctx) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return OXG_OK;
+}
+
+int oxg_dequant_mxfp4(oxg_ctx *ctx, const uint8_t *blocks, size_t n_block_bytes,
+                      const void *scales, size_t n_scales, int scale_fmt, size_t rows, size_t cols,
+                      uint16_t *out) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  // Same checks, order and wording as src/mxfp4.rs:16-33.
+  if (cols % 32 != 0) return fail(ctx, OXG_ERR_SHAPE, "cols must be divisible by 32, got %zu", cols);
+  if (cols != 0 && rows > SIZE_MAX / cols)
+    return fail(ctx, OXG_ERR_SHAPE, "rows * cols overflows: %zu x %zu", rows, cols);
+  const size_t expected_blocks = rows * cols / 2;
+  if (n_block_bytes != expected_blocks)
+    return fail(ctx, OXG_ERR_SHAPE, "blocks length mismatch: expected %zu, got %zu",
+                expected_blocks, n_block_bytes);
+  const size_t expected_scales = rows * (cols / 32);
+  if (n_scales != expected_scales)
+    return fail(ctx, OXG_ERR_SHAPE, "scales length mismatch: expected %zu, got %zu",
+                expected_scales, n_scales);
+  if (scale_fmt != OXG_SCALE_E8M0 && scale_fmt != OXG_SCALE_BF16)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "unknown scale format %d", scale_fmt);
+  if (expected_scales == 0) return OXG_OK;
+  if (!blocks || !scales || !out)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "blocks, scales and out must be non-NULL");
+  if (scale_fmt == OXG_SCALE_BF16 && ((uintptr_t)scales & 1))
+    return fail(ctx, OXG_ERR_INVALID_ARG, "bf16 scales must be 2-byte aligned");
+  if ((uintptr_t)out & 1) return fail(ctx, OXG_ERR_INVALID_ARG, "out must be 2-byte aligned");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, launch(ctx, "dequant_mxfp4", [&] {
+             return oxg::launch_dequant_mxfp4(blocks, scales, scale_fmt, expected_scales, out,
+                                              ctx->stream);
+           }),
+           "dequant launch");
+  return OXG_OK;
+}
+
+int oxg_swiglu(oxg_ctx *ctx, const float *gate, const float *up, size_t n, float alpha,
+               float limit, float *out) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  if (n == 0) return OXG_OK;
+  if (!gate || !up || !out) return fail(ctx, OXG_ERR_INVALID_ARG, "gate, up and out must be non-NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, launch(ctx, "swiglu", [&] {
+             return oxg::launch_swiglu(gate, up, n, alpha, limit, out, ctx->stream);
+           }),
+           "swiglu launch");
+  return OXG_OK;
+}
+
+int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe_weights *w) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  if (layer < 0 || layer > 4096) return fail(ctx, OXG_ERR_INVALID_ARG, "layer %d out of range", layer);
+  int rc = check_dims(ctx, dims);
+  if (rc) return rc;
+  if (!w || !w->router_w || !w->w1_blocks || !w->w1_scales || !w->b1 || !w->w2_blocks ||
+      !w->w2_scales || !w->b2)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "all weight pointers except router_b must be non-NULL");
+  DeviceGuard g(ctx->device);
+  const oxg_moe_dims d = *dims;
+  const size_t E = d.n_experts, H = d.hidden, I = d.intermediate;
+  const size_t kb1 = (H / 32 + 3) / 4 * 4, kb2 = (I / 32 + 3) / 4 * 4;
+  const size_t n_rw = E * H * 2, n_rb = E * 2;
+  const size_t n_w1 = E * 2 * I * (H / 2), n_s1 = E * 2 * I * kb1, n_b1 = E * 2 * I * 2;
+  const size_t n_w2 = E * H * (I / 2), n_s2 = E * H * kb2, n_b2 = E * H * 2;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t o_rw = take(n_rw), o_rb = take(n_rb), o_w1 = take(n_w1), o_s1 = take(n_s1),
+               o_b1 = take(n_b1), o_w2 = take(n_w2), o_s2 = take(n_s2), o_b2 = take(n_b2);
+  const size_t stage_bytes = n_w1 > n_w2 ? n_w1 : n_w2;
+
+  if ((size_t)layer >= ctx->layers.size()) ctx->layers.resize(layer + 1);
+  free_layer(ctx->layers[layer]);
+  Layer L;
+  L.dims = d;
+  void *block = nullptr, *stage = nullptr;
+  OXG_CUDA(ctx, cudaMalloc(&block, off), "cudaMalloc(layer weights)");
+  cudaError_t st = cudaMalloc(&stage, stage_bytes);
+  if (st != cudaSuccess) {
+    cudaFree(block);
+    return cuda_fail(ctx, st, "cudaMalloc(upload staging)");
+  }
+  char *base = (char *)block;
+  L.block = block;
+  L.router_w = (uint16_t *)(base + o_rw);
+  L.router_b = w->router_b ? (uint16_t *)(base + o_rb) : nullptr;
+  L.w1 = (uint8_t *)(base + o_w1);
+  L.s1 = (uint8_t *)(base + o_s1);
+  L.b1 = (uint16_t *)(base + o_b1);
+  L.w2 = (uint8_t *)(base + o_w2);
+  L.s2 = (uint8_t *)(base + o_s2);
+  L.b2 = (uint16_t *)(base + o_b2);
+  cudaStream_t s = ctx->stream;
+  auto body = [&]() -> cudaError_t {
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(L.router_w, w->router_w, n_rw, cudaMemcpyDefault, s))) return e;
+    if (w->router_b && (e = cudaMemcpyAsync(L.router_b, w->router_b, n_rb, cudaMemcpyDefault, s)))
+      return e;
+    if ((e = cudaMemcpyAsync(L.b1, w->b1, n_b1, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(L.b2, w->b2, n_b2, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w->w1_blocks, n_w1, cudaMemcpyDefault, s))) return e;
+    if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w1, E * 2 * I, (int)H, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w->w1_scales, E * 2 * I * (H / 32), cudaMemcpyDefault, s))) return e;
+    if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s1, E * 2 * I, (int)H, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w->w2_blocks, n_w2, cudaMemcpyDefault, s))) return e;
+    if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w2, E * H, (int)I, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w->w2_scales, E * H * (I / 32), cudaMemcpyDefault, s))) return e;
+    if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s2, E * H, (int)I, s))) return e;
+    return cudaStreamSynchronize(s);
+  };
+  st = body();
+  cudaFree(stage);
+  if (st != cudaSuccess) {
+    cudaFree(block);
+    return cuda_fail(ctx, st, "weight upload");
+  }
+  L.present = true;
+  ctx->layers[layer] = L;
+  return OXG_OK;
+}
+
+int oxg_moe_release(oxg_ctx *ctx, int layer) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  free_layer(*L);
+  return OXG_OK;
+}
+
+int oxg_moe_reserve(oxg_ctx *ctx, int layer, int n_tokens) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  if (n_tokens < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", n_tokens);
+  DeviceGuard g(ctx->device);
+  return ensure_scratch(ctx, L->dims, n_tokens);
+}
+
+int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y, int mode,
+                    int precision) {
+  Layer *L = nullptr;
+  int rc = check_forward_args(ctx, layer, x, T, y, mode, precision, &L);
+  if (rc) return rc;
+  if (T == 0) return OXG_OK;
+  if (((uintptr_t)x & 15) || ((uintptr_t)y & 15))
+    return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  rc = ensure_scratch(ctx, L->dims, T);
+  if (rc) return rc;
+  ctx->last_layer = layer;
+  return forward_device(ctx, *L, x, T, y);
+}
+
+int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T, float *y_host,
+                         int mode, int precision) {
+  Layer *L = nullptr;
+  int rc = check_forward_args(ctx, layer, x_host, T, y_host, mode, precision, &L);
+  if (rc) return rc;
+  if (T == 0) return OXG_OK;
+  DeviceGuard g(ctx->device);
+  rc = ensure_scratch(ctx, L->dims, T);
+  if (rc) return rc;
+  ctx->last_layer = layer;
+  const size_t H = L->dims.hidden;
+  OXG_CUDA(ctx, cudaMemcpyAsync(ctx->ws.x_stage, x_host, (size_t)T * H * 2, cudaMemcpyDefault, ctx->stream),
+           "copy x to device");
+  rc = forward_device(ctx, *L, ctx->ws.x_stage, T, ctx->ws.y_stage);
+  if (rc) return rc;
+  OXG_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->ws.y_stage, (size_t)T * H * 4, cudaMemcpyDefault, ctx->stream),
+           "copy y to host");
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return OXG_OK;
+}
+
+int oxg_moe_route(oxg_ctx *ctx, int layer, const uint16_t *x, int T, int32_t *idx, float *wts,
+                  float *logits) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
+  if (T == 0) return OXG_OK;
+  if (!x || !idx || !wts) return fail(ctx, OXG_ERR_INVALID_ARG, "x, idx and w must be non-NULL");
+  if ((uintptr_t)x & 15) return fail(ctx, OXG_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  int rc = ensure_scratch(ctx, L->dims, T);
+  if (rc) return rc;
+  return route(ctx, *L, x, T, idx, wts, logits);
+}
+
+int oxg_moe_last_counts(oxg_ctx *ctx, int32_t *counts_host, int n_experts) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, ctx->last_layer);
+  if (!L || !ctx->ws.counts) return fail(ctx, OXG_ERR_STATE, "no forward has run on this context");
+  if (!counts_host || n_experts != L->dims.n_experts)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "counts_host must hold n_experts = %d ints",
+                L->dims.n_experts);
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaMemcpyAsync(counts_host, ctx->ws.counts, (size_t)n_experts * 4, cudaMemcpyDefault, ctx->stream),
+           "copy counts");
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return OXG_OK;
+}
+
+int oxg_profile_enable(oxg_ctx *ctx, int on) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ctx->prof.on = on != 0;
+  return OXG_OK;
+}
+
+int oxg_profile_read(oxg_ctx *ctx, const char *name, double *total_ms, int *launches) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  if (!name || !total_ms || !launches)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "name, total_ms and launches must be non-NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  ctx->prof.drain();
+  *total_ms = 0.0;
+  *launches = 0;
+  for (const Profiler::Sum &s : ctx->prof.sums)
+    if (s.name == name) {
+      *total_ms = s.ms;
+      *launches = s.launches;
+    }
+  return OXG_OK;
+}
+
+int oxg_profile_reset(oxg_ctx *ctx) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  ctx->prof.drain();
+  ctx->prof.sums.clear();
+  return OXG_OK;
+}
+
+int oxg_kernel_launches(const oxg_ctx *ctx, long long *count) {
+  if (!ctx || !count) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx and count must be non-NULL");
+  *count = ctx->launches;
+  return OXG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,151 @@
+"""MoE layer forward on the GPU through the C ABI against the SPEC oracle.
+
+Tolerance (the layer-parity bar): max |y_gpu - y_oracle| <= 2e-2 and
+mean relative error sum|y_gpu - y_oracle| / sum|y_oracle| <= 1e-3, with the
+oracle accumulating in fp64. Routing is compared exactly, except where the
+oracle's own gap between the k-th and (k+1)-th logit is below 1e-4 (a tie the
+fp32 summation order may decide either way); there the GPU's routing is fed
+to the oracle for the output comparison.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from oxidized_gpt_oss_b200 import synth
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+MAX_ABS = 2e-2
+MEAN_REL = 1e-3
+TIE_GAP = 1e-4
+
+
+def _layer(d):
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    return MoELayer(d)
+
+
+def _forward(layer, x_np):
+    import torch
+    x = torch.from_numpy(x_np.view(np.int16)).cuda()
+    y = layer.forward(x)
+    idx, w, logits = layer.route(x)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy()
+
+
+def _check_layer(d, x, y, idx, w, logits):
+    W = oracle.Weights(d)
+    K = d["top_k"]
+    ref_logits = oracle.router_logits(W, x)
+    assert np.max(np.abs(logits - ref_logits)) < 1e-4 * max(1.0, np.abs(ref_logits).max())
+    ref_idx, ref_w = oracle.topk_softmax(ref_logits, K)
+    srt = -np.sort(-ref_logits, axis=1)
+    gap = srt[:, K - 1] - srt[:, K] if ref_logits.shape[1] > K else np.full(len(x), np.inf)
+    near_tie = gap < TIE_GAP
+    same = np.all(idx == ref_idx, axis=1)
+    assert np.all(same | near_tie), f"routing differs on tokens {np.nonzero(~(same | near_tie))[0]}"
+    assert np.allclose(w[same], ref_w[same], rtol=1e-5, atol=1e-6)
+    y_ref = oracle.moe_forward_spec(W, x, idx=idx, wts=w, acc64=True)
+    err = np.abs(y - y_ref)
+    max_abs = float(err.max()) if err.size else 0.0
+    mean_rel = float(err.sum() / max(np.abs(y_ref).sum(), 1e-30)) if err.size else 0.0
+    assert max_abs <= MAX_ABS, f"max abs error {max_abs}"
+    assert mean_rel <= MEAN_REL, f"mean relative error {mean_rel}"
+    return max_abs, mean_rel
+
+
+def test_small_golden_fixture(cuda_ctx):
+    f = np.load(os.path.join(GOLDEN, "moe_small_seed1.npz"))
+    H, I, E, K = f["dims"].tolist()
+    alpha, limit = f["act"].tolist()
+    d = dict(hidden=H, intermediate=I, n_experts=E, top_k=K, alpha=alpha, limit=limit)
+    for k in ("router_w", "router_b", "w1_blocks", "w1_scales", "b1", "w2_blocks", "w2_scales", "b2"):
+        d[k] = f[k]
+    layer = _layer(d)
+    y, idx, w, logits = _forward(layer, f["x"])
+    assert np.array_equal(idx, f["idx"])
+    err = np.abs(y - f["y"])
+    assert err.max() <= MAX_ABS and err.sum() / np.abs(f["y"]).sum() <= MEAN_REL
+
+
+@pytest.mark.parametrize("H,I,E,K,T", [
+    (96, 160, 8, 4, 1),     # tail-only groups (3 blocks) and 1 full + 1-block tail
+    (128, 64, 4, 2, 13),    # full groups only
+    (2880, 2880, 32, 4, 3),
+    (256, 224, 16, 4, 40),  # experts with > 8 tokens: several token passes
+])
+def test_shapes(cuda_ctx, H, I, E, K, T):
+    d = synth.moe_layer(seed=H + I + T, hidden=H, intermediate=I, n_experts=E, top_k=K)
+    x = synth.activations(7, T, H)
+    y, idx, w, logits = _forward(_layer(d), x)
+    _check_layer(d, x, y, idx, w, logits)
+
+
+def test_config0_full_size(cuda_ctx):
+    """One gpt-oss-20b MoE block, 8 tokens, seed 0 (the reference's CPU-runnable case)."""
+    d = synth.moe_layer(seed=0)
+    x = synth.activations(0, 8, 2880)
+    layer = _layer(d)
+    y, idx, w, logits = _forward(layer, x)
+    max_abs, mean_rel = _check_layer(d, x, y, idx, w, logits)
+    counts = layer.last_counts()
+    assert counts.sum() == 8 * 4
+    print(f"config0: max_abs={max_abs:.3e} mean_rel={mean_rel:.3e} distinct_experts={(counts > 0).sum()}")
+
+
+def test_no_router_bias_and_empty_batch(cuda_ctx):
+    import torch
+    d = synth.moe_layer(seed=5, hidden=64, intermediate=96, n_experts=8, top_k=4, router_bias=False)
+    layer = _layer(d)
+    x = synth.activations(5, 6, 64)
+    y, idx, w, logits = _forward(layer, x)
+    _check_layer(d, x, y, idx, w, logits)
+    out = layer.forward(torch.empty((0, 64), dtype=torch.int16, device="cuda"))
+    assert out.shape == (0, 64)
+
+
+def test_large_activation_range_uses_exponent_shift(cuda_ctx):
+    # activations beyond the f16 range exercise the per-token 2^-sigma staging
+    d = synth.moe_layer(seed=9, hidden=128, intermediate=96, n_experts=8, top_k=4)
+    x = synth.activations(9, 4, 128)
+    xf = synth.bf16_bits_to_f32(x).copy()
+    xf[1] *= 2.0 ** 20
+    xf[2] *= 2.0 ** -20
+    x = synth.f32_to_bf16_bits(xf)
+    y, idx, w, logits = _forward(_layer(d), x)
+    W = oracle.Weights(d)
+    y_ref = oracle.moe_forward_spec(W, x, idx=idx, wts=w, acc64=True)
+    rel = np.abs(y - y_ref).max(axis=1) / np.maximum(np.abs(y_ref).max(axis=1), 1e-30)
+    assert np.all(rel < 1e-4), rel
+
+
+def test_deterministic_and_host_path_matches(cuda_ctx):
+    import torch
+    d = synth.moe_layer(seed=3, hidden=256, intermediate=256, n_experts=16, top_k=4)
+    layer = _layer(d)
+    x = synth.activations(3, 24, 256)
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    y1 = layer.forward(xt).cpu()
+    y2 = layer.forward(xt).cpu()
+    assert torch.equal(y1, y2)
+    xh = torch.from_numpy(x.view(np.int16)).pin_memory()
+    yh = layer.forward_host(xh)
+    assert torch.equal(yh, y1)
+
+
+def test_bad_arguments_are_errors(cuda_ctx):
+    import torch
+    from oxidized_gpt_oss_b200 import abi
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    d = synth.moe_layer(seed=1, hidden=64, intermediate=64, n_experts=4, top_k=2)
+    with pytest.raises(abi.OxgError, match="hidden must be a positive multiple of 32"):
+        MoELayer(dict(d, hidden=48))
+    layer = MoELayer(d)
+    with pytest.raises(abi.OxgError, match="prefill mode is not available"):
+        layer.forward(torch.zeros((2, 64), dtype=torch.int16, device="cuda"), mode=abi.OXG_MODE_PREFILL)
+    lib = abi.load()
+    st = lib.oxg_moe_forward(cuda_ctx.handle, 999, None, 1, None, 0, 0)
+    assert st == abi.OXG_ERR_STATE
