@@ -67,8 +67,8 @@ OXG_API int oxg_ctx_destroy(oxg_ctx *ctx);
 /* Message of the last failing call on ctx (or of the last failing
  * context-less call on this thread when ctx is NULL). Never NULL. */
 OXG_API const char *oxg_last_error(const oxg_ctx *ctx);
-/* Runs the context's work on `stream` (a cudaStream_t) instead of its own;
- * NULL restores the context's stream. */
+/* Runs the context's work on `stream` (a cudaStream_t) from now on, instead
+ * of the stream the context created; NULL is CUDA's legacy default stream. */
 OXG_API int oxg_ctx_set_stream(oxg_ctx *ctx, void *stream);
 OXG_API void *oxg_ctx_get_stream(const oxg_ctx *ctx);
 /* Replaces MetalDevice::synchronize (src/backend/metal_stub.rs:46-48). */

@@ -127,9 +127,10 @@ class Context:
             self.set_stream(stream)
 
     def set_stream(self, stream) -> None:
-        """stream: a torch.cuda.Stream, a raw cudaStream_t int, or None."""
+        """stream: a torch.cuda.Stream or a raw cudaStream_t int (0 / None:
+        CUDA's legacy default stream, which is torch's default stream)."""
         raw = getattr(stream, "cuda_stream", stream)
-        check(self.lib.oxg_ctx_set_stream(self.handle, raw), self.handle)
+        check(self.lib.oxg_ctx_set_stream(self.handle, raw or None), self.handle)
 
     def sync(self) -> None:
         check(self.lib.oxg_sync(self.handle), self.handle)

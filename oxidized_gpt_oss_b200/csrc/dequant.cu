@@ -25,12 +25,26 @@ __device__ __forceinline__ float load_scale(const void *scales, size_t blk) {
   return bf16_to_f32(__ldg(static_cast<const uint16_t *>(scales) + blk));
 }
 
+// e2m1(n) * s in f32 with the NaN results of an x86-64 host (the reference's
+// f32 multiply there): a NaN scale propagates quieted with its sign and
+// payload; inf * 0 gives the default NaN 0xFFC00000. The GPU multiply alone
+// returns the canonical 0x7FFFFFFF for both. (An AArch64 host agrees on the
+// first rule and returns 0x7FC00000 for the second.)
+__device__ __forceinline__ float scaled_code(uint32_t n, float s) {
+  const float v = __fmul_rn(e2m1_to_f32(n), s);
+  if (__builtin_expect(v != v, 0)) {
+    const uint32_t sb = __float_as_uint(s);
+    return __uint_as_float(s != s ? (sb | 0x00400000u) : 0xFFC00000u);
+  }
+  return v;
+}
+
 __device__ __forceinline__ uint4 decode8(uint32_t w, float s) {
   uint32_t o[4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    float lo = __fmul_rn(e2m1_to_f32(w >> (8 * p)), s);
-    float hi = __fmul_rn(e2m1_to_f32(w >> (8 * p + 4)), s);
+    const float lo = scaled_code(w >> (8 * p), s);
+    const float hi = scaled_code(w >> (8 * p + 4), s);
     o[p] = f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
@@ -69,8 +83,8 @@ __global__ void __launch_bounds__(256) dequant_byte_kernel(const uint8_t *__rest
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_bytes; i += stride) {
     uint32_t b = __ldg(codes + i);
     float s = load_scale<FMT>(scales, i >> 4);
-    out[2 * i] = (uint16_t)f32_to_bf16_bits(__fmul_rn(e2m1_to_f32(b), s));
-    out[2 * i + 1] = (uint16_t)f32_to_bf16_bits(__fmul_rn(e2m1_to_f32(b >> 4), s));
+    out[2 * i] = (uint16_t)f32_to_bf16_bits(scaled_code(b, s));
+    out[2 * i + 1] = (uint16_t)f32_to_bf16_bits(scaled_code(b >> 4, s));
   }
 }
 

@@ -389,7 +389,7 @@ const char *oxg_last_error(const oxg_ctx *ctx) {
 
 int oxg_ctx_set_stream(oxg_ctx *ctx, void *stream) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
-  ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+  ctx->stream = (cudaStream_t)stream;  // NULL is the legacy default stream
   return OXG_OK;
 }
 

@@ -136,6 +136,25 @@ def test_deterministic_and_host_path_matches(cuda_ctx):
     assert torch.equal(yh, y1)
 
 
+def test_runs_on_torch_current_stream(cuda_ctx):
+    """The library enqueues on torch's current stream (default or side stream),
+    so torch ops after a forward see its result without a device-wide sync."""
+    import torch
+    d = synth.moe_layer(seed=8, hidden=128, intermediate=128, n_experts=8, top_k=4)
+    layer = _layer(d)
+    x = torch.from_numpy(synth.activations(8, 16, 128).view(np.int16)).cuda()
+    torch.cuda.synchronize()
+    ref = layer.forward(x).clone()
+    assert (layer.ctx.lib.oxg_ctx_get_stream(layer.ctx.handle) or 0) == torch.cuda.current_stream().cuda_stream
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        outs = [layer.forward(x) for _ in range(4)]
+        got = torch.stack(outs).sum(0)
+        assert (layer.ctx.lib.oxg_ctx_get_stream(layer.ctx.handle) or 0) == s.cuda_stream
+    s.synchronize()
+    assert torch.allclose(got, ref * 4, rtol=1e-6, atol=1e-4)
+
+
 def test_bad_arguments_are_errors(cuda_ctx):
     import torch
     from oxidized_gpt_oss_b200 import abi
