@@ -153,6 +153,28 @@ OXG_API int oxg_moe_route(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_
  * E ints). Waits for the context's stream. */
 OXG_API int oxg_moe_last_counts(oxg_ctx *ctx, int32_t *counts_host, int n_experts);
 
+/* Has no counterpart in the reference. The same layer forward as
+ * oxg_moe_forward (same kernels, same results), for callers that must not
+ * have the library allocate device memory during a forward: serving runtimes
+ * that reserve the whole GPU for their own memory pool, decode loops that
+ * cannot absorb the synchronisation a cudaMalloc/cudaFree may cause, and
+ * embedders that forbid foreign code from allocating. This call allocates
+ * nothing (no cudaMalloc, cudaFree or allocating library routine): its
+ * working memory is one fixed 4 MiB array compiled into the library, which
+ * every GPU that loads the library holds until the process exits. The layer
+ * must have been uploaded before (the upload allocates, once); x_dev/y_dev are
+ * as for oxg_moe_forward. Batches whose scratch exceeds 4 MiB are refused with
+ * OXG_ERR_SHAPE and a message giving the largest token count that fits (45
+ * tokens of a gpt-oss-20b layer). The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, done once per device), so make
+ * that first call before any stream capture. All calls share the one array and
+ * it keeps the last call's contents (every part is rewritten before it is read,
+ * so nothing is cleared); calls that overlap on the GPU — concurrent streams,
+ * contexts or threads on the same device — race on it and must be serialised
+ * by the caller. */
+OXG_API int oxg_moe_forward_noalloc(oxg_ctx *ctx, int layer, const uint16_t *x_dev,
+                                    int n_tokens, float *y_dev);
+
 /* ---- measurement (no reference counterpart: the reference's only timing is
  * the --bench wall clock of src/main.rs:159-164) --------------------------- */
 

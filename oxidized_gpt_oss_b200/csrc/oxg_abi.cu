@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/oxg_b200.h"
+#include "ctx_internal.h"
 #include "kernels.h"
 
 namespace {
@@ -321,6 +322,24 @@ int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void
 }
 
 }  // namespace
+
+namespace oxg {
+
+bool ctx_layer(oxg_ctx *ctx, int layer, MoeDeviceWeights *w, int *device, cudaStream_t *stream) {
+  Layer *L = get_layer(ctx, layer);
+  if (!L) {
+    fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+    return false;
+  }
+  *w = device_weights(*L);
+  *device = ctx->device;
+  *stream = ctx->stream;
+  return true;
+}
+
+int ctx_error(oxg_ctx *ctx, int status, const char *msg) { return fail(ctx, status, "%s", msg); }
+
+}  // namespace oxg
 
 extern "C" {
 
