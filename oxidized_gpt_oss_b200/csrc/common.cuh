@@ -84,6 +84,25 @@ __device__ __forceinline__ void stg_stream_v4(void *p, uint4 v) {
                : "memory");
 }
 
+// Asynchronous global -> shared copies (per thread; completion tracked per
+// thread with commit/wait groups, no register staging).
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void cp_async_16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // Warp MMA: D(16x8 f32) = A(16x16 f16, row) * B(16x8 f16, col) + C.
 // ----------------------------------------------------------------------------

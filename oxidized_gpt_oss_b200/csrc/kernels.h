@@ -20,8 +20,8 @@ cudaError_t launch_swiglu(const float *gate, const float *up, size_t n, float al
 
 // ---- weight re-layout (relayout.cu) ----------------------------------------
 // Packed codes [rows, K/2] in the checkpoint order -> the "word-transposed"
-// order the MoE kernels read (see moe_layout.h). scales [rows, K/32] ->
-// [rows, kb_pad] with kb_pad = round_up(K/32, 4), padding bytes zero.
+// order the MoE kernels read (described in relayout.cu). scales [rows, K/32]
+// -> [rows, kb_pad] with kb_pad = round_up(K/32, 4), padding bytes zero.
 cudaError_t launch_relayout_codes(const uint8_t *src, uint8_t *dst, size_t rows, int K,
                                   cudaStream_t stream);
 cudaError_t launch_pad_scales(const uint8_t *src, uint8_t *dst, size_t rows, int K,
@@ -37,11 +37,30 @@ cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint1
 // ---- permutation (permute.cu) -------------------------------------------------
 // Stable counting sort of the T*k (token, j) slots by expert.
 //   counts[E], offsets[E+1], perm[T*k] (position -> slot), slot_pos[T*k]
-//   (slot -> position). expert_lo/expert_hi restrict to a local expert range
-//   (experts outside it are counted but are not "local").
+//   (slot -> position).
 cudaError_t launch_permute(const int32_t *idx, int n_slots, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
                            cudaStream_t stream);
+
+// ---- fused routing for small batches (route_small.cu) -------------------------
+constexpr int kMaxRouteTokens = 64;
+
+struct RouteSmallArgs {
+  const uint16_t *x, *router_w, *router_b;
+  int T, H, E, k;
+  float *logits;   // [T, E]
+  int32_t *sigma;  // [T]
+  int32_t *idx;    // [T, k]
+  float *wts;      // [T, k]
+  int32_t *counts, *offsets, *perm, *slot_pos;
+  int32_t *active, *n_active;  // active expert ids (ascending) and their number
+  uint32_t *done;              // CTA completion counter (zero between calls)
+  uint32_t *band_done;         // per-band counters of the mlp2 kernel, zeroed here
+  int n_bands;
+};
+// pdl: launch with programmatic stream serialisation (overlaps the previous
+// kernel's tail; the kernel waits for it before touching memory).
+cudaError_t launch_route_small(const RouteSmallArgs &a, cudaStream_t stream, bool pdl);
 
 // ---- decode MoE (moe_decode.cu) ---------------------------------------------
 struct MoeDeviceWeights {
@@ -55,8 +74,8 @@ struct MoeDeviceWeights {
 };
 
 // mlp1 + bias + clamped SwiGLU for every (expert, slot) -> h [n_slots, I] f32
-// (rows in expert-sorted position order). x_rows maps a position to the row
-// of x holding its token (i.e. perm[p] / k).
+// (rows in expert-sorted position order; the token of position p is
+// perm[p] / k).
 cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
                                    const int32_t *perm, const int32_t *sigma,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
@@ -67,6 +86,35 @@ cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
                                    int expert_base, int n_local_experts, float *y_slot,
                                    cudaStream_t stream);
+// Scheduled variants (decode fast path): blockIdx.y walks the active-expert
+// list written by the routing kernel, the grid is sized to one resident
+// wave, pdl chains the launches.
+struct DecodeSched {
+  const int32_t *active, *n_active;
+  int max_active;  // grid.y: upper bound on the number of active experts
+  int bands1;      // per-expert bands of the mlp1 kernel (when not all-token)
+  int bands2;      // per-expert bands of the mlp2 kernel
+  int n_sms;       // persistent grid of the all-token mlp1 kernel
+  bool pdl;
+};
+// Bands (CTAs per expert) so that expected_active experts fill n_sms SMs.
+int decode_bands(int rows, int expected_active, int n_sms);
+// mlp1 + bias + clamped SwiGLU. With T <= 8 all tokens are staged once per
+// CTA and a persistent grid of n_sms CTAs walks (active expert, tile) pairs;
+// idx is the routing [T, k]. Otherwise one CTA per (active expert, band).
+cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
+                                  const int32_t *perm, const int32_t *sigma, const int32_t *idx,
+                                  const int32_t *counts, const int32_t *offsets,
+                                  const DecodeSched &s, int T, float *h, cudaStream_t stream);
+// mlp2 + bias into y_slot, then, per band of rows, the CTA of the last expert
+// to finish writes y[t, band] = sum_j wts[t, j] * y_slot[slot_pos[t, j], band]
+// (band_done: one zeroed counter per band).
+cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
+                                  const int32_t *counts, const int32_t *offsets,
+                                  const DecodeSched &s, uint32_t *band_done, int T,
+                                  const int32_t *slot_pos, const float *wts, float *y_slot,
+                                  float *y, cudaStream_t stream);
+
 // out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,
                            int H, int k, float *out, cudaStream_t stream);

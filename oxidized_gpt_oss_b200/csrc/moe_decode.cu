@@ -9,33 +9,46 @@
 //   y  = h . W2^T + b2          W2 [H, I]
 //
 // Design (HBM-bound: every expert weight byte is read once per step):
-//  * Each CTA owns one expert (blockIdx.y) and a band of 16-row tiles; a warp
-//    computes a 16-row x 8-token tile with mma.m16n8k16 (f16 in, f32 out).
-//  * Weight codes stream from HBM with 16-byte loads in the word-transposed
-//    order of relayout.cu, so one load gives a lane the A-operand codes of all
-//    four blocks of a 128-element group. cvt.rn.f16x2.e2m1x2 turns two codes
-//    into two exact f16 values; the E8M0 scale of each 32-element block is
-//    applied to the f32 MMA result of that block (exact power of two).
+//  * A warp computes 16 weight rows x 8 token columns with mma.m16n8k16
+//    (f16 in, f32 out); CTAs are 16 warps, one per SM.
+//  * Weight codes stream from HBM in the word-transposed order of
+//    relayout.cu, so one 16-byte copy gives a lane the A-operand codes of all
+//    four blocks of a 128-element group. Each warp runs one continuous
+//    cp.async pipeline through a shared-memory ring (6 groups in flight per
+//    lane, ~120 KB per SM) across all the tiles it processes, so HBM latency
+//    is covered without holding registers and without a refill gap between
+//    tiles. cvt.rn.f16x2.e2m1x2 turns two codes into two exact f16 values;
+//    the E8M0 scale of each 32-element block multiplies that block's f32 MMA
+//    result (an exact power of two).
 //  * The per-lane K order inside a block is permuted consistently on A (by the
 //    byte order of the code word) and B (by the shared-memory "fragment order"
 //    of the activations), so no shuffles are needed.
 //  * mlp1: A rows g and g+8 of a tile are the gate and up rows of one
 //    intermediate unit, so a lane holds both and applies bias + clamped SwiGLU
-//    in registers; the activation is staged once per CTA as f16 x * 2^-sigma
-//    (exact for bf16 input) and the products are scaled back by 2^sigma.
+//    in registers. x enters as f16 x * 2^-sigma (exact for bf16 input) and the
+//    products are scaled back by 2^sigma. With at most 8 tokens, all tokens
+//    are staged once per CTA and every tile computes all 8 columns (the MMA
+//    has 8 columns either way), so any warp can take any (expert, tile) and a
+//    persistent grid keeps every SM busy; the epilogue keeps the columns of
+//    the tokens routed to the tile's expert.
 //  * mlp2: the f32 SwiGLU output is split into f16 hi + lo (h = hi + lo to
-//    ~2^-22 relative), and each block takes two MMAs per operand half, so the
-//    intermediate is not rounded to 16 bits.
+//    ~2^-22 relative), so the intermediate is not rounded to 16 bits. For an
+//    expert with at most 4 tokens, hi and lo of token j sit in MMA columns 2j
+//    and 2j+1 (one MMA per k-step); otherwise each half takes its own MMA.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace oxg {
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr int kTilesPerWarp = 2;
-constexpr int kTilesPerCta = kWarps * kTilesPerWarp;
+// Per-warp ring of weight groups in flight: kStages slots of
+// 2 rows x 32 lanes x 16 B of codes + 2 x 32 x 4 B of scales.
+constexpr int kStages = 6;
+constexpr int kStageBytes = 1280;
+constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
 struct DecodeArgs {
   const uint8_t *codes;   // relaid codes [E, rows, K/2]
@@ -46,6 +59,7 @@ struct DecodeArgs {
   const uint16_t *x;
   const int32_t *perm;
   const int32_t *sigma;
+  const int32_t *idx;  // routing [T, topk] (all-token mlp1)
   int topk;
   // mlp2 input: h [n_slots, K] f32 in position order
   const float *h;
@@ -54,7 +68,22 @@ struct DecodeArgs {
   float *out;  // mlp1: h [n_slots, I]; mlp2: y_slot [n_slots, H]
   int out_ld;
   float alpha, limit;
+  // scheduling: blockIdx.y indexes `active` (ids of experts with tokens,
+  // *n_active of them) when it is set, else expert_base + blockIdx.y;
+  // blockIdx.x is one of `bands` equal bands of an expert's 16-row tiles
+  const int32_t *active, *n_active;
+  int bands;
+  int pdl;  // launched as a programmatic dependent: wait before reading inputs
+  int T;
+  // mlp2 only: fused weighted combine when band_done is set
+  uint32_t *band_done;
+  const int32_t *slot_pos;
+  const float *wts;
+  float *y;
 };
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Byte offset of the 8-element group (n-tile nt, block blk, half s, token g,
 // lane-in-quad q) in the fragment-ordered activation buffer.
@@ -62,48 +91,236 @@ __device__ __forceinline__ int frag_off(int nt, int nb, int blk, int s, int g, i
   return ((((nt * nb + blk) * 2 + s) * 8 + g) * 4 + q) * bytes;
 }
 
-template <int MODE, int NT>
-__global__ void __launch_bounds__(kThreads) moe_decode_kernel(const DecodeArgs a) {
+struct TileRows {
+  const uint8_t *ca, *cb, *sa, *sb;  // codes and scales of the lane's rows a and b
+};
+
+// Streams the weight rows of n_items 16-row tiles through the warp's ring.
+// item_rows(i) gives the lane's two rows of item i; block_fn(blk, wa, wb,
+// s_a, s_b) consumes one 32-element block (code words of rows a/b, their
+// scales); done_fn(i) runs after the last block of item i.
+template <class ItemRows, class BlockFn, class DoneFn>
+__device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, ItemRows item_rows,
+                                             BlockFn block_fn, DoneFn done_fn) {
+  if (n_items <= 0) return;
+  const int lane = threadIdx.x & 31, q = lane & 3;
+  const int nb = K / 32, full = nb / 4, tail = nb % 4, ngroups = full + (tail ? 1 : 0);
+  // Issue side: runs kStages groups ahead of the consumer; the rows of the
+  // item being issued are computed once per item.
+  int i_item = 0, i_grp = 0, i_slot = 0;
+  TileRows ir = item_rows(0);
+  auto issue_next = [&]() {
+    if (i_item < n_items) {
+      uint8_t *st = ring + i_slot * kStageBytes;
+      if (i_grp < full) {
+        cp_async_16(st + lane * 16, ir.ca + i_grp * 64 + q * 16);
+        cp_async_16(st + 512 + lane * 16, ir.cb + i_grp * 64 + q * 16);
+      } else {
+        for (int b = 0; b < tail; ++b) {
+          cp_async_4(st + lane * 16 + b * 4, ir.ca + i_grp * 64 + (q * tail + b) * 4);
+          cp_async_4(st + 512 + lane * 16 + b * 4, ir.cb + i_grp * 64 + (q * tail + b) * 4);
+        }
+      }
+      cp_async_4(st + 1024 + lane * 4, ir.sa + i_grp * 4);
+      cp_async_4(st + 1152 + lane * 4, ir.sb + i_grp * 4);
+      if (++i_grp == ngroups) {
+        i_grp = 0;
+        if (++i_item < n_items) ir = item_rows(i_item);
+      }
+    }
+    cp_async_commit();
+    if (++i_slot == kStages) i_slot = 0;
+  };
+#pragma unroll
+  for (int u = 0; u < kStages; ++u) issue_next();
+  int c_item = 0, c_grp = 0, c_slot = 0;
+#pragma unroll 1
+  while (c_item < n_items) {
+    cp_async_wait<kStages - 1>();
+    const uint8_t *st = ring + c_slot * kStageBytes;
+    const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
+    const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
+    const uint32_t sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + lane * 4);
+    const uint32_t sxb = *reinterpret_cast<const uint32_t *>(st + 1152 + lane * 4);
+    issue_next();
+    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+    if (c_grp < full) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        block_fn(c_grp * 4 + b, wa[b], wb[b], e8m0_to_f32(sxa >> (8 * b)), e8m0_to_f32(sxb >> (8 * b)));
+    } else {
+#pragma unroll
+      for (int b = 0; b < 3; ++b)
+        if (b < tail)
+          block_fn(c_grp * 4 + b, wa[b], wb[b], e8m0_to_f32(sxa >> (8 * b)), e8m0_to_f32(sxb >> (8 * b)));
+    }
+    if (++c_grp == ngroups) {
+      done_fn(c_item);
+      c_grp = 0;
+      ++c_item;
+    }
+    if (++c_slot == kStages) c_slot = 0;
+  }
+  cp_async_wait<0>();
+}
+
+// Decodes two rows' code words into the m16n8k16 A operands of the block's
+// two k-steps.
+__device__ __forceinline__ void a_operands(uint32_t wa, uint32_t wb, uint32_t (&A0)[4],
+                                           uint32_t (&A1)[4]) {
+  uint32_t fa[4], fb[4];
+  e2m1x8_to_f16x8(wa, fa);
+  e2m1x8_to_f16x8(wb, fb);
+  A0[0] = fa[0]; A0[1] = fb[0]; A0[2] = fa[1]; A0[3] = fb[1];
+  A1[0] = fa[2]; A1[1] = fb[2]; A1[2] = fa[3]; A1[3] = fb[3];
+}
+
+// Stages tokens [tok0, tok0 + n) of x (rows of `x` given by row_of(tok))
+// as f16 x * 2^-sigma into fragment order, 8 tokens per n-tile; tokens
+// beyond `valid` are zero.
+template <int NT, class RowOf>
+__device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int nb, int valid,
+                                        RowOf row_of) {
+  const int K = a.K;
+  const int units = NT * 8 * (K / 8);
+  for (int u = threadIdx.x; u < units; u += kThreads) {
+    const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
+    const int blk = k0 >> 5, qq = (k0 & 31) >> 3, nt = tok >> 3, gg = tok & 7;
+    uint32_t o0 = 0, o1 = 0, o2 = 0, o3 = 0;
+    if (tok < valid) {
+      const int t = row_of(tok);
+      const float inv = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
+      const uint4 v = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + k0);
+      o0 = pack_f16x2(bf16_to_f32(v.x & 0xFFFFu) * inv, bf16_to_f32(v.x >> 16) * inv);
+      o1 = pack_f16x2(bf16_to_f32(v.y & 0xFFFFu) * inv, bf16_to_f32(v.y >> 16) * inv);
+      o2 = pack_f16x2(bf16_to_f32(v.z & 0xFFFFu) * inv, bf16_to_f32(v.z >> 16) * inv);
+      o3 = pack_f16x2(bf16_to_f32(v.w & 0xFFFFu) * inv, bf16_to_f32(v.w >> 16) * inv);
+    }
+    *reinterpret_cast<uint2 *>(smem + frag_off(nt, nb, blk, 0, gg, qq, 8)) = make_uint2(o0, o1);
+    *reinterpret_cast<uint2 *>(smem + frag_off(nt, nb, blk, 1, gg, qq, 8)) = make_uint2(o2, o3);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// mlp1 over all tokens (T <= 8): persistent grid over (active expert, tile).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ float tok_scale[NT * 8];
+  __shared__ float tok_scale[8];
+  __shared__ int act_s[kMaxAllTokActive];
+  __shared__ int act_of[256];
+  __shared__ int col_pos[kMaxAllTokActive * 8];  // position of (active expert, token), or -1
 
-  const int e = a.expert_base + blockIdx.y;
-  const int n_e = a.counts[e];
-  if (n_e == 0) return;
-  const int pos0 = a.offsets[e];
-  const int K = a.K, nb = K / 32, ngroups_full = nb / 4, tail = nb % 4;
+  if (a.pdl) pdl_wait();
+  const int K = a.K, nb = K / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int T = a.T, k = a.topk;
+  const int n_act = *a.n_active;
   const int n_tiles = a.rows / 16;
-  const int tile0 = blockIdx.x * kTilesPerCta;
-  if (tile0 >= n_tiles) return;
 
+  for (int i = tid; i < n_act; i += kThreads) {
+    act_s[i] = a.active[i];
+    act_of[a.active[i]] = i;
+  }
+  for (int i = tid; i < n_act * 8; i += kThreads) col_pos[i] = -1;
+  stage_x<1>(a, smem, nb, T, [](int tok) { return tok; });
+  if (tid < 8) tok_scale[tid] = tid < T ? __uint_as_float((uint32_t)(127 + a.sigma[tid]) << 23) : 1.f;
+  __syncthreads();
+  for (int p = tid; p < T * k; p += kThreads) {
+    const int s = a.perm[p];
+    col_pos[act_of[a.idx[s]] * 8 + s / k] = p;
+  }
+  __syncthreads();
+  if (a.pdl) pdl_launch();
+
+  const int W = gridDim.x * kWarps, wg = blockIdx.x * kWarps + warp;
+  const int total = n_act * n_tiles;
+  const int n_items = wg < total ? (total - wg + W - 1) / W : 0;
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  auto item_rows = [&](int i) {
+    const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
+    const size_t r_a = (size_t)act_s[ai] * a.rows + 2 * (tile * 8 + g);
+    return TileRows{a.codes + r_a * (K / 2), a.codes + (r_a + 1) * (K / 2),
+                    a.scales + r_a * a.kb_pad, a.scales + (r_a + 1) * a.kb_pad};
+  };
+  auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
+    uint32_t A0[4], A1[4];
+    a_operands(wa, wb, A0, A1);
+    const uint2 b0 = *reinterpret_cast<const uint2 *>(smem + frag_off(0, nb, blk, 0, g, q, 8));
+    const uint2 b1 = *reinterpret_cast<const uint2 *>(smem + frag_off(0, nb, blk, 1, g, q, 8));
+    float d[4];
+    mma_f16_16816(d, A0, b0.x, b0.y, zero4);
+    mma_f16_16816(d, A1, b1.x, b1.y, d);
+    acc[0] = fmaf(s_a, d[0], acc[0]);
+    acc[1] = fmaf(s_a, d[1], acc[1]);
+    acc[2] = fmaf(s_b, d[2], acc[2]);
+    acc[3] = fmaf(s_b, d[3], acc[3]);
+  };
+  auto done_fn = [&](int i) {
+    const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
+    const int e = act_s[ai];
+    const int pr = tile * 8 + g;  // intermediate unit (gate row 2pr, up row 2pr + 1)
+    const float bg = bf16_to_f32(a.bias[(size_t)e * a.rows + 2 * pr]);
+    const float bu = bf16_to_f32(a.bias[(size_t)e * a.rows + 2 * pr + 1]);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int t = 2 * q + c;
+      const int p = col_pos[ai * 8 + t];
+      if (p >= 0) {
+        const float gate = fmaf(acc[c], tok_scale[t], bg);
+        const float up = fmaf(acc[2 + c], tok_scale[t], bu);
+        a.out[(size_t)p * a.out_ld + pr] = swiglu_clamped(gate, up, a.alpha, a.limit);
+      }
+    }
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  };
+  uint8_t *ring = smem + nb * 2 * 32 * 8 + warp * (kStages * kStageBytes);
+  stream_items(n_items, K, ring, item_rows, block_fn, done_fn);
+}
+
+// ---------------------------------------------------------------------------
+// Per-expert kernel: CTA = (expert, band of tiles); tokens staged per expert.
+// ---------------------------------------------------------------------------
+
+// One band of one expert's tiles x its n_e tokens.
+//   MODE 1: mlp1 + bias + clamped SwiGLU -> a.out = h
+//   MODE 2: mlp2 + bias -> a.out = y_slot
+// PACKED (MODE 2, n_e <= 4): f16 hi/lo of token j in MMA columns 2j / 2j+1.
+template <int MODE, int NT, bool PACKED>
+__device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, float *tok_scale,
+                                            int e, int n_e, int pos0, int t_begin, int t_end) {
+  constexpr int kTokPerPass = PACKED ? 4 : NT * 8;
+  constexpr int kFrag = (MODE == 1 || PACKED) ? 8 : 16;  // bytes per staged fragment
+  constexpr int kNT = PACKED ? 1 : NT;
+  const int K = a.K, nb = K / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const size_t rbase = (size_t)e * a.rows;
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  uint8_t *ring = smem + NT * nb * 2 * 32 * (MODE == 1 ? 8 : 16) + warp * (kStages * kStageBytes);
+  // tiles of this warp: t_begin + warp, t_begin + warp + kWarps, ...
+  const int n_items = t_begin + warp < t_end ? (t_end - t_begin - warp + kWarps - 1) / kWarps : 0;
 
-  for (int tok0 = 0; tok0 < n_e; tok0 += NT * 8) {
+  for (int tok0 = 0; tok0 < n_e; tok0 += kTokPerPass) {
     // ---- stage this pass's activations in fragment order ----
-    const int units = NT * 8 * (K / 8);
-    for (int u = tid; u < units; u += kThreads) {
-      const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
-      const int nt = tok >> 3, gg = tok & 7, blk = k0 >> 5, qq = (k0 & 31) >> 3;
-      const bool valid = tok0 + tok < n_e;
-      if (MODE == 1) {
-        uint32_t o0 = 0, o1 = 0, o2 = 0, o3 = 0;
-        if (valid) {
-          const int t = a.perm[pos0 + tok0 + tok] / a.topk;
-          const float inv = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
-          const uint4 v = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + k0);
-          o0 = pack_f16x2(bf16_to_f32(v.x & 0xFFFFu) * inv, bf16_to_f32(v.x >> 16) * inv);
-          o1 = pack_f16x2(bf16_to_f32(v.y & 0xFFFFu) * inv, bf16_to_f32(v.y >> 16) * inv);
-          o2 = pack_f16x2(bf16_to_f32(v.z & 0xFFFFu) * inv, bf16_to_f32(v.z >> 16) * inv);
-          o3 = pack_f16x2(bf16_to_f32(v.w & 0xFFFFu) * inv, bf16_to_f32(v.w >> 16) * inv);
-        }
-        *reinterpret_cast<uint2 *>(smem + frag_off(nt, nb, blk, 0, gg, qq, 8)) = make_uint2(o0, o1);
-        *reinterpret_cast<uint2 *>(smem + frag_off(nt, nb, blk, 1, gg, qq, 8)) = make_uint2(o2, o3);
-      } else {
+    if (MODE == 1) {
+      stage_x<NT>(a, smem, nb, n_e - tok0, [&](int tok) { return a.perm[pos0 + tok0 + tok] / a.topk; });
+      if (tid < NT * 8) {
+        float sc = 1.f;
+        if (tok0 + tid < n_e)
+          sc = __uint_as_float((uint32_t)(127 + a.sigma[a.perm[pos0 + tok0 + tid] / a.topk]) << 23);
+        tok_scale[tid] = sc;
+      }
+    } else {
+      const int units = kTokPerPass * (K / 8);
+      for (int u = tid; u < units; u += kThreads) {
+        const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
+        const int blk = k0 >> 5, qq = (k0 & 31) >> 3;
         float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (valid) {
+        if (tok0 + tok < n_e) {
           const float4 *src = reinterpret_cast<const float4 *>(a.h + (size_t)(pos0 + tok0 + tok) * K + k0);
           const float4 v0 = src[0], v1 = src[1];
           f[0] = v0.x; f[1] = v0.y; f[2] = v0.z; f[3] = v0.w;
@@ -116,127 +333,151 @@ __global__ void __launch_bounds__(kThreads) moe_decode_kernel(const DecodeArgs a
           const float2 r01 = unpack_f16x2(h01), r23 = unpack_f16x2(h23);
           const uint32_t l01 = pack_f16x2(f[4 * s] - r01.x, f[4 * s + 1] - r01.y);
           const uint32_t l23 = pack_f16x2(f[4 * s + 2] - r23.x, f[4 * s + 3] - r23.y);
-          *reinterpret_cast<uint4 *>(smem + frag_off(nt, nb, blk, s, gg, qq, 16)) =
-              make_uint4(h01, h23, l01, l23);
+          if (PACKED) {
+            *reinterpret_cast<uint2 *>(smem + frag_off(0, nb, blk, s, 2 * tok, qq, 8)) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2 *>(smem + frag_off(0, nb, blk, s, 2 * tok + 1, qq, 8)) = make_uint2(l01, l23);
+          } else {
+            *reinterpret_cast<uint4 *>(smem + frag_off(tok >> 3, nb, blk, s, tok & 7, qq, 16)) =
+                make_uint4(h01, h23, l01, l23);
+          }
         }
       }
     }
-    if (MODE == 1 && tid < NT * 8) {
-      float sc = 1.f;
-      if (tok0 + tid < n_e) {
-        const int t = a.perm[pos0 + tok0 + tid] / a.topk;
-        sc = __uint_as_float((uint32_t)(127 + a.sigma[t]) << 23);
-      }
-      tok_scale[tid] = sc;
-    }
     __syncthreads();
+    // Once every CTA of this grid has passed here, the next kernel in the
+    // stream may start taking the SM slots that free up; it waits for this
+    // grid's results before it reads them.
+    if (a.pdl && tok0 == 0) pdl_launch();
 
-    // ---- tiles ----
-    for (int ti = 0; ti < kTilesPerWarp; ++ti) {
-      const int tile = tile0 + warp * kTilesPerWarp + ti;
-      if (tile >= n_tiles) break;
+    float acc[kNT][4];
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    auto tile_of = [&](int i) { return t_begin + warp + i * kWarps; };
+    auto item_rows = [&](int i) {
+      const int tile = tile_of(i);
       const int row_a = MODE == 1 ? 2 * (tile * 8 + g) : tile * 16 + g;
       const int row_b = MODE == 1 ? row_a + 1 : row_a + 8;
-      const uint8_t *ca = a.codes + (rbase + row_a) * (size_t)(K / 2);
-      const uint8_t *cb = a.codes + (rbase + row_b) * (size_t)(K / 2);
-      const uint8_t *sa = a.scales + (rbase + row_a) * (size_t)a.kb_pad;
-      const uint8_t *sb = a.scales + (rbase + row_b) * (size_t)a.kb_pad;
-
-      float acc[NT][4];
+      return TileRows{a.codes + (rbase + row_a) * (size_t)(K / 2),
+                      a.codes + (rbase + row_b) * (size_t)(K / 2),
+                      a.scales + (rbase + row_a) * (size_t)a.kb_pad,
+                      a.scales + (rbase + row_b) * (size_t)a.kb_pad};
+    };
+    auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
+      uint32_t A0[4], A1[4];
+      a_operands(wa, wb, A0, A1);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-
-      auto block_step = [&](uint32_t wa, uint32_t wb, float s_a, float s_b, int blk) {
-        uint32_t fa[4], fb[4];
-        e2m1x8_to_f16x8(wa, fa);
-        e2m1x8_to_f16x8(wb, fb);
-        const uint32_t A0[4] = {fa[0], fb[0], fa[1], fb[1]};
-        const uint32_t A1[4] = {fa[2], fb[2], fa[3], fb[3]};
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          float d[4];
-          if (MODE == 1) {
-            const uint2 b0 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 0, g, q, 8));
-            const uint2 b1 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 1, g, q, 8));
-            mma_f16_16816(d, A0, b0.x, b0.y, zero4);
-            mma_f16_16816(d, A1, b1.x, b1.y, d);
-          } else {
-            const uint4 b0 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 0, g, q, 16));
-            const uint4 b1 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 1, g, q, 16));
-            mma_f16_16816(d, A0, b0.x, b0.y, zero4);
-            mma_f16_16816(d, A0, b0.z, b0.w, d);
-            mma_f16_16816(d, A1, b1.x, b1.y, d);
-            mma_f16_16816(d, A1, b1.z, b1.w, d);
-          }
-          acc[nt][0] = fmaf(s_a, d[0], acc[nt][0]);
-          acc[nt][1] = fmaf(s_a, d[1], acc[nt][1]);
-          acc[nt][2] = fmaf(s_b, d[2], acc[nt][2]);
-          acc[nt][3] = fmaf(s_b, d[3], acc[nt][3]);
+      for (int nt = 0; nt < kNT; ++nt) {
+        float d[4];
+        if (kFrag == 8) {
+          const uint2 b0 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 0, g, q, 8));
+          const uint2 b1 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 1, g, q, 8));
+          mma_f16_16816(d, A0, b0.x, b0.y, zero4);
+          mma_f16_16816(d, A1, b1.x, b1.y, d);
+        } else {
+          const uint4 b0 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 0, g, q, 16));
+          const uint4 b1 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 1, g, q, 16));
+          mma_f16_16816(d, A0, b0.x, b0.y, zero4);
+          mma_f16_16816(d, A0, b0.z, b0.w, d);
+          mma_f16_16816(d, A1, b1.x, b1.y, d);
+          mma_f16_16816(d, A1, b1.z, b1.w, d);
         }
-      };
-
-      // full groups, one group of loads kept in flight ahead of the math
-      if (ngroups_full > 0) {
-        uint4 va = ldg_stream_v4(ca + q * 16);
-        uint4 vb = ldg_stream_v4(cb + q * 16);
-        uint32_t xa = ldg_stream_u32(sa);
-        uint32_t xb = ldg_stream_u32(sb);
-#pragma unroll 1
-        for (int grp = 0; grp < ngroups_full; ++grp) {
-          uint4 na = va, nb4 = vb;
-          uint32_t nxa = xa, nxb = xb;
-          if (grp + 1 < ngroups_full) {
-            na = ldg_stream_v4(ca + (grp + 1) * 64 + q * 16);
-            nb4 = ldg_stream_v4(cb + (grp + 1) * 64 + q * 16);
-            nxa = ldg_stream_u32(sa + (grp + 1) * 4);
-            nxb = ldg_stream_u32(sb + (grp + 1) * 4);
-          }
-          const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
-          const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-          for (int b = 0; b < 4; ++b)
-            block_step(wa[b], wb[b], e8m0_to_f32(xa >> (8 * b)), e8m0_to_f32(xb >> (8 * b)),
-                       grp * 4 + b);
-          va = na;
-          vb = nb4;
-          xa = nxa;
-          xb = nxb;
-        }
+        acc[nt][0] = fmaf(s_a, d[0], acc[nt][0]);
+        acc[nt][1] = fmaf(s_a, d[1], acc[nt][1]);
+        acc[nt][2] = fmaf(s_b, d[2], acc[nt][2]);
+        acc[nt][3] = fmaf(s_b, d[3], acc[nt][3]);
       }
-      if (tail) {
-        const int grp = ngroups_full;
-        const uint32_t xa = ldg_stream_u32(sa + grp * 4);
-        const uint32_t xb = ldg_stream_u32(sb + grp * 4);
-        for (int b = 0; b < tail; ++b) {
-          const uint32_t wa = ldg_stream_u32(ca + grp * 64 + (q * tail + b) * 4);
-          const uint32_t wb = ldg_stream_u32(cb + grp * 64 + (q * tail + b) * 4);
-          block_step(wa, wb, e8m0_to_f32(xa >> (8 * b)), e8m0_to_f32(xb >> (8 * b)), grp * 4 + b);
-        }
-      }
-
-      // ---- epilogue ----
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int col = nt * 8 + 2 * q + c;
-          const int tok = tok0 + col;
-          if (tok >= n_e) continue;
+    };
+    auto done_fn = [&](int i) {
+      const int tile = tile_of(i);
+      const int row_a = MODE == 1 ? 2 * (tile * 8 + g) : tile * 16 + g;
+      const int row_b = MODE == 1 ? row_a + 1 : row_a + 8;
+      const float ba = bf16_to_f32(a.bias[rbase + row_a]), bb = bf16_to_f32(a.bias[rbase + row_b]);
+      if (PACKED) {
+        const int tok = tok0 + q;  // columns 2q (hi) and 2q + 1 (lo)
+        if (tok < n_e) {
           const size_t pos = (size_t)(pos0 + tok);
-          if (MODE == 1) {
-            const int p = tile * 8 + g;
-            const float sc = tok_scale[col];
-            const float gate = fmaf(acc[nt][c], sc, bf16_to_f32(a.bias[rbase + row_a]));
-            const float up = fmaf(acc[nt][2 + c], sc, bf16_to_f32(a.bias[rbase + row_b]));
-            a.out[pos * a.out_ld + p] = swiglu_clamped(gate, up, a.alpha, a.limit);
-          } else {
-            a.out[pos * a.out_ld + row_a] = acc[nt][c] + bf16_to_f32(a.bias[rbase + row_a]);
-            a.out[pos * a.out_ld + row_b] = acc[nt][2 + c] + bf16_to_f32(a.bias[rbase + row_b]);
+          a.out[pos * a.out_ld + row_a] = (acc[0][0] + acc[0][1]) + ba;
+          a.out[pos * a.out_ld + row_b] = (acc[0][2] + acc[0][3]) + bb;
+        }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int col = nt * 8 + 2 * q + c;
+            const int tok = tok0 + col;
+            if (tok >= n_e) continue;
+            const size_t pos = (size_t)(pos0 + tok);
+            if (MODE == 1) {
+              const float sc = tok_scale[col];
+              a.out[pos * a.out_ld + tile * 8 + g] =
+                  swiglu_clamped(fmaf(acc[nt][c], sc, ba), fmaf(acc[nt][2 + c], sc, bb), a.alpha, a.limit);
+            } else {
+              a.out[pos * a.out_ld + row_a] = acc[nt][c] + ba;
+              a.out[pos * a.out_ld + row_b] = acc[nt][2 + c] + bb;
+            }
           }
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    };
+    stream_items(n_items, K, ring, item_rows, block_fn, done_fn);
+    __syncthreads();
+  }
+}
+
+template <int MODE, int NT>
+__global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float tok_scale[NT * 8];
+  __shared__ int band_last;
+
+  if (a.pdl) pdl_wait();
+  int e;
+  if (a.active) {
+    if ((int)blockIdx.y >= *a.n_active) return;
+    e = a.active[blockIdx.y];
+  } else {
+    e = a.expert_base + blockIdx.y;
+  }
+  const int n_e = a.counts[e];
+  if (n_e == 0) return;
+  const int pos0 = a.offsets[e];
+  const int n_tiles = a.rows / 16;
+  const int t_begin = (int)(((long long)blockIdx.x * n_tiles) / a.bands);
+  const int t_end = (int)(((long long)(blockIdx.x + 1) * n_tiles) / a.bands);
+  const int tid = threadIdx.x;
+
+  if (MODE == 2 && n_e <= 4)
+    expert_band<MODE, NT, true>(a, smem, tok_scale, e, n_e, pos0, t_begin, t_end);
+  else
+    expert_band<MODE, NT, false>(a, smem, tok_scale, e, n_e, pos0, t_begin, t_end);
+
+  // ---- mlp2: the last expert to finish a band of rows combines it ----
+  // out[t, r] = sum_j wts[t, j] * y_slot[slot_pos[t, j], r], j in order (the
+  // same expression as combine_kernel), so the result does not depend on
+  // which CTA finishes last.
+  if (MODE == 2 && a.band_done) {
+    if (tid == 0) {
+      __threadfence();
+      band_last = atomicAdd(&a.band_done[blockIdx.x], 1u) == (unsigned)(*a.n_active - 1);
     }
     __syncthreads();
+    if (band_last) {
+      __threadfence();
+      const int r0 = t_begin * 16, nr = (t_end - t_begin) * 16;
+      for (int i = tid; i < nr * a.T; i += kThreads) {
+        const int t = i / nr, r = r0 + i % nr;
+        float acc = 0.f;
+        for (int j = 0; j < a.topk; ++j) {
+          const int p = a.slot_pos[t * a.topk + j];
+          if (p < 0) continue;
+          acc = fmaf(a.wts[t * a.topk + j], __ldcg(a.out + (size_t)p * a.out_ld + r), acc);
+        }
+        a.y[(size_t)t * a.out_ld + r] = acc;
+      }
+    }
   }
 }
 
@@ -264,32 +505,38 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
   }
 }
 
-template <int MODE, int NT>
-cudaError_t launch_decode(const DecodeArgs &a, int n_local_experts, cudaStream_t stream) {
-  const int nb = a.K / 32;
-  const size_t smem = (size_t)NT * nb * 2 * 32 * (MODE == 1 ? 8 : 16);
-  auto fn = moe_decode_kernel<MODE, NT>;
+template <class Kern>
+cudaError_t launch_ex(Kern fn, dim3 grid, size_t smem, bool pdl, cudaStream_t stream,
+                      const DecodeArgs &a) {
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
-  const int n_tiles = a.rows / 16;
-  dim3 grid((n_tiles + kTilesPerCta - 1) / kTilesPerCta, n_local_experts);
-  fn<<<grid, kThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
-}  // namespace
+template <int MODE, int NT>
+cudaError_t launch_decode(const DecodeArgs &a, int grid_y, cudaStream_t stream) {
+  const int nb = a.K / 32;
+  const size_t smem = (size_t)NT * nb * 2 * 32 * (MODE == 1 ? 8 : 16) + kRingBytes;
+  return launch_ex(moe_decode_kernel<MODE, NT>, dim3(a.bands, grid_y), smem, a.pdl, stream, a);
+}
 
-// Shared memory of the activation stage, per token n-tile: nb * 2 * 32 * 8 (mlp1)
-// or * 16 (mlp2) bytes. One n-tile (8 tokens) per pass keeps several CTAs
-// resident per SM; larger groups of tokens take several passes.
-cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
-                                   const int32_t *perm, const int32_t *sigma,
-                                   const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *h,
-                                   cudaStream_t stream) {
-  if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
+int bands_for_tpw(int rows, int tpw) { return (rows / 16 + kWarps * tpw - 1) / (kWarps * tpw); }
+
+DecodeArgs mlp1_args(const MoeDeviceWeights &w, const uint16_t *x, const int32_t *perm,
+                     const int32_t *sigma, const int32_t *counts, const int32_t *offsets,
+                     float *h) {
   DecodeArgs a{};
   a.codes = w.w1;
   a.scales = w.s1;
@@ -303,19 +550,16 @@ cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
   a.topk = w.k;
   a.counts = counts;
   a.offsets = offsets;
-  a.expert_base = expert_base;
   a.out = h;
   a.out_ld = w.I;
   a.alpha = w.alpha;
   a.limit = w.limit;
-  return launch_decode<1, 1>(a, n_local_experts, stream);
+  a.bands = bands_for_tpw(a.rows, 2);
+  return a;
 }
 
-cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
-                                   const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *y_slot,
-                                   cudaStream_t stream) {
-  if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
+DecodeArgs mlp2_args(const MoeDeviceWeights &w, const float *h, const int32_t *counts,
+                     const int32_t *offsets, float *y_slot) {
   DecodeArgs a{};
   a.codes = w.w2;
   a.scales = w.s2;
@@ -327,10 +571,82 @@ cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
   a.topk = w.k;
   a.counts = counts;
   a.offsets = offsets;
-  a.expert_base = expert_base;
   a.out = y_slot;
   a.out_ld = w.H;
+  a.bands = bands_for_tpw(a.rows, 2);
+  return a;
+}
+
+}  // namespace
+
+// Shared memory of the activation stage, per token n-tile: nb * 2 * 32 * 8 (mlp1)
+// or * 16 (mlp2) bytes, plus the warps' cp.async rings. One n-tile (8 tokens)
+// per pass; larger groups of tokens take several passes.
+cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
+                                   const int32_t *perm, const int32_t *sigma,
+                                   const int32_t *counts, const int32_t *offsets, int n_slots,
+                                   int expert_base, int n_local_experts, float *h,
+                                   cudaStream_t stream) {
+  if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
+  DecodeArgs a = mlp1_args(w, x, perm, sigma, counts, offsets, h);
+  a.expert_base = expert_base;
+  return launch_decode<1, 1>(a, n_local_experts, stream);
+}
+
+cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
+                                   const int32_t *counts, const int32_t *offsets, int n_slots,
+                                   int expert_base, int n_local_experts, float *y_slot,
+                                   cudaStream_t stream) {
+  if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
+  DecodeArgs a = mlp2_args(w, h, counts, offsets, y_slot);
+  a.expert_base = expert_base;
   return launch_decode<2, 1>(a, n_local_experts, stream);
+}
+
+int decode_bands(int rows, int expected_active, int n_sms) {
+  const int tiles = rows / 16;
+  int bands = n_sms / (expected_active > 0 ? expected_active : 1);
+  if (bands < 1) bands = 1;
+  if (bands > tiles) bands = tiles;
+  return bands;
+}
+
+cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
+                                  const int32_t *perm, const int32_t *sigma, const int32_t *idx,
+                                  const int32_t *counts, const int32_t *offsets,
+                                  const DecodeSched &s, int T, float *h, cudaStream_t stream) {
+  if (s.max_active == 0 || T == 0) return cudaSuccess;
+  DecodeArgs a = mlp1_args(w, x, perm, sigma, counts, offsets, h);
+  a.active = s.active;
+  a.n_active = s.n_active;
+  a.pdl = s.pdl;
+  a.T = T;
+  a.idx = idx;
+  if (T <= 8 && T * w.k <= kMaxAllTokActive && w.E <= 256) {
+    const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + kRingBytes;
+    return launch_ex(mlp1_alltok_kernel, dim3(s.n_sms), smem, a.pdl, stream, a);
+  }
+  a.bands = s.bands1;
+  return launch_decode<1, 1>(a, s.max_active, stream);
+}
+
+cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
+                                  const int32_t *counts, const int32_t *offsets,
+                                  const DecodeSched &s, uint32_t *band_done, int T,
+                                  const int32_t *slot_pos, const float *wts, float *y_slot,
+                                  float *y, cudaStream_t stream) {
+  if (s.max_active == 0) return cudaSuccess;
+  DecodeArgs a = mlp2_args(w, h, counts, offsets, y_slot);
+  a.active = s.active;
+  a.n_active = s.n_active;
+  a.bands = s.bands2;
+  a.pdl = s.pdl;
+  a.band_done = band_done;
+  a.T = T;
+  a.slot_pos = slot_pos;
+  a.wts = wts;
+  a.y = y;
+  return launch_decode<2, 1>(a, s.max_active, stream);
 }
 
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,

@@ -9,6 +9,8 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <algorithm>
+#include <cmath>
 #include <vector>
 
 #include "../../include/oxg_b200.h"
@@ -28,9 +30,16 @@ struct Layer {
   uint16_t *b1 = nullptr, *b2 = nullptr;
 };
 
+// Completion counters at the start of the scratch: zeroed when the scratch is
+// allocated and left at zero by every forward that uses them.
+constexpr int kMaxBands = 1024;
+constexpr size_t kCounterBytes = (1 + kMaxBands) * sizeof(uint32_t);
+
 struct Scratch {
   void *base = nullptr;
   size_t bytes = 0;
+  uint32_t *done = nullptr, *band_done = nullptr;
+  int32_t *active = nullptr, *n_active = nullptr;
   int32_t *idx = nullptr, *sigma = nullptr, *counts = nullptr, *offsets = nullptr;
   int32_t *perm = nullptr, *slot_pos = nullptr;
   float *wts = nullptr, *logits = nullptr, *h = nullptr, *y_slot = nullptr;
@@ -101,6 +110,7 @@ struct oxg_ctx {
   std::vector<Layer> layers;
   Scratch ws;
   int last_layer = -1;
+  int n_sms = 148;
   long long launches = 0;
   Profiler prof;
 };
@@ -171,6 +181,8 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
     off = align_up(off + bytes, 256);
     return base ? base + o : nullptr;
   };
+  char *p_cnt = take(kCounterBytes);
+  char *p_active = take((size_t)d.n_experts * 4), *p_nactive = take(4);
   char *p_idx = take(S * 4), *p_wts = take(S * 4), *p_sigma = take((size_t)T * 4);
   char *p_logits = take((size_t)T * d.n_experts * 4);
   char *p_counts = take((size_t)d.n_experts * 4), *p_offsets = take(((size_t)d.n_experts + 1) * 4);
@@ -178,6 +190,10 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_h = take(S * d.intermediate * 4), *p_y = take(S * d.hidden * 4);
   char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
   if (s && base) {
+    s->done = (uint32_t *)p_cnt;
+    s->band_done = s->done + 1;
+    s->active = (int32_t *)p_active;
+    s->n_active = (int32_t *)p_nactive;
     s->idx = (int32_t *)p_idx;
     s->wts = (float *)p_wts;
     s->sigma = (int32_t *)p_sigma;
@@ -211,6 +227,7 @@ int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
   ctx->ws.base = p;
   ctx->ws.bytes = need;
   scratch_bytes(d, Tc, &ctx->ws, (char *)p);
+  OXG_CUDA(ctx, cudaMemsetAsync(p, 0, kCounterBytes, ctx->stream), "cudaMemsetAsync(counters)");
   return OXG_OK;
 }
 
@@ -273,9 +290,75 @@ int route(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, int32_t *idx, float 
   return OXG_OK;
 }
 
+// Expected number of distinct experts T tokens route to with uniform routing:
+// E * (1 - (1 - k/E)^T), at least 1 and at most min(E, T*k).
+int expected_active(int E, int k, int T) {
+  const double p = 1.0 - (double)k / (double)E;
+  double v = (double)E * (1.0 - std::pow(p, (double)T));
+  int n = (int)std::ceil(v - 1e-9);
+  const int mx = std::min(E, T * k);
+  return std::max(1, std::min(n, mx));
+}
+
+// Decode fast path (T <= kMaxRouteTokens): fused routing + permutation, then
+// the two expert kernels, all chained with programmatic dependent launch; the
+// weighted combine is done by the mlp2 kernel.
+int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
+  const oxg_moe_dims &d = L.dims;
+  const oxg::MoeDeviceWeights w = device_weights(L);
+  const int exp_active = expected_active(d.n_experts, d.top_k, T);
+  oxg::DecodeSched sched{};
+  sched.active = ctx->ws.active;
+  sched.n_active = ctx->ws.n_active;
+  sched.max_active = std::min(d.n_experts, T * d.top_k);
+  sched.bands1 = oxg::decode_bands(2 * d.intermediate, exp_active, ctx->n_sms);
+  sched.bands2 = oxg::decode_bands(d.hidden, exp_active, ctx->n_sms);
+  sched.n_sms = ctx->n_sms;
+  sched.pdl = true;
+  const int n_bands = sched.bands2;
+  if (n_bands > kMaxBands) return fail(ctx, OXG_ERR_UNSUPPORTED, "too many row bands (%d)", n_bands);
+  oxg::RouteSmallArgs ra{};
+  ra.x = x;
+  ra.router_w = L.router_w;
+  ra.router_b = L.router_b;
+  ra.T = T;
+  ra.H = d.hidden;
+  ra.E = d.n_experts;
+  ra.k = d.top_k;
+  ra.logits = ctx->ws.logits;
+  ra.sigma = ctx->ws.sigma;
+  ra.idx = ctx->ws.idx;
+  ra.wts = ctx->ws.wts;
+  ra.counts = ctx->ws.counts;
+  ra.offsets = ctx->ws.offsets;
+  ra.perm = ctx->ws.perm;
+  ra.slot_pos = ctx->ws.slot_pos;
+  ra.active = ctx->ws.active;
+  ra.n_active = ctx->ws.n_active;
+  ra.done = ctx->ws.done;
+  ra.band_done = ctx->ws.band_done;
+  ra.n_bands = n_bands;
+  OXG_CUDA(ctx, launch(ctx, "route_small", [&] { return oxg::launch_route_small(ra, ctx->stream, true); }),
+           "route_small launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp1_decode", [&] {
+             return oxg::launch_moe_mlp1_sched(w, x, ctx->ws.perm, ctx->ws.sigma, ctx->ws.idx,
+                                               ctx->ws.counts, ctx->ws.offsets, sched, T, ctx->ws.h,
+                                               ctx->stream);
+           }),
+           "mlp1 launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp2_decode", [&] {
+             return oxg::launch_moe_mlp2_sched(w, ctx->ws.h, ctx->ws.counts, ctx->ws.offsets, sched,
+                                               ctx->ws.band_done, T, ctx->ws.slot_pos,
+                                               ctx->ws.wts, ctx->ws.y_slot, y, ctx->stream);
+           }),
+           "mlp2 launch");
+  return OXG_OK;
+}
+
 int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
+  if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y);
   int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
   if (rc) return rc;
   OXG_CUDA(ctx, launch(ctx, "permute", [&] {
@@ -380,6 +463,7 @@ int oxg_ctx_create(int device, oxg_ctx **out) {
   oxg_ctx *ctx = new (std::nothrow) oxg_ctx();
   if (!ctx) return fail(nullptr, OXG_ERR_OOM, "host allocation failed");
   ctx->device = device;
+  ctx->n_sms = prop.multiProcessorCount;
   st = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
   if (st != cudaSuccess) {
     delete ctx;

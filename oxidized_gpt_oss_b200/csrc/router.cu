@@ -145,11 +145,10 @@ cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint1
   if (T == 0) return cudaSuccess;
   if (E > kMaxExperts || k > kMaxTopK || k > E || H % 8) return cudaErrorInvalidValue;
   const size_t smem = (size_t)H * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t st = cudaFuncSetAttribute(router_topk_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (st != cudaSuccess) return st;
-  }
+  // opt in unconditionally: static plus dynamic shared memory is what counts
+  cudaError_t st = cudaFuncSetAttribute(router_topk_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (st != cudaSuccess) return st;
   router_topk_kernel<<<T, kRouterThreads, smem, stream>>>(x, w, b, H, E, k, idx, wts, logits,
                                                           sigma);
   return cudaGetLastError();

@@ -76,6 +76,7 @@ def test_small_golden_fixture(cuda_ctx):
     (128, 64, 4, 2, 13),    # full groups only
     (2880, 2880, 32, 4, 3),
     (256, 224, 16, 4, 40),  # experts with > 8 tokens: several token passes
+    (128, 96, 8, 4, 80),    # beyond the fused-routing batch size: separate router/permute/combine
 ])
 def test_shapes(cuda_ctx, H, I, E, K, T):
     d = synth.moe_layer(seed=H + I + T, hidden=H, intermediate=I, n_experts=E, top_k=K)
