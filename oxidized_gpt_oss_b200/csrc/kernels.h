@@ -115,6 +115,32 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
                                   const int32_t *slot_pos, const float *wts, float *y_slot,
                                   float *y, cudaStream_t stream);
 
+// ---- prefill MoE (moe_prefill.cu) -------------------------------------------
+// Buffers of one prefill pass over S expert-sorted slots.
+struct PrefillIO {
+  int S;
+  const int32_t *counts, *offsets;  // per expert (global ids)
+  int expert_base, n_local_experts;
+  const uint16_t *xp;               // [S, H] f16 x * 2^-sigma in slot order (gather)
+  const float *pos_scale;           // [S] 2^sigma of each slot's token
+  uint16_t *h_hi, *h_lo;            // [S, I] f16 SwiGLU output, hi + lo
+  float *y_slot;                    // [S, H] f32 expert outputs
+  int *err;                         // pipeline timeout code (0 = none)
+};
+// min over non-zero and max of E8M0 scale bytes into minmax[0..1] (which
+// must hold 255 and 0 on entry).
+cudaError_t launch_scale_range(const uint8_t *scales, size_t n, unsigned *minmax,
+                               cudaStream_t stream);
+cudaError_t launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *sigma, int S,
+                              int H, int topk, uint16_t *xp, float *pos_scale, int *err,
+                              cudaStream_t stream);
+// tcgen05 grouped GEMMs (persistent grid of n_sms CTAs). Need H and I
+// multiples of 64 and every E8M0 scale 0 or in [104, 141].
+cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
+                                cudaStream_t stream);
+cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
+                                cudaStream_t stream);
+
 // out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,
                            int H, int k, float *out, cudaStream_t stream);

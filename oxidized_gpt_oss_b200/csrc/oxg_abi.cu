@@ -28,17 +28,24 @@ struct Layer {
   uint16_t *router_w = nullptr, *router_b = nullptr;
   uint8_t *w1 = nullptr, *s1 = nullptr, *w2 = nullptr, *s2 = nullptr;
   uint16_t *b1 = nullptr, *b2 = nullptr;
+  // Every E8M0 scale is 0 or in [104, 141], so scale * E2M1 is exact in f16
+  // and the tensor-core prefill path applies (H and I multiples of 64 too).
+  bool prefill_ok = false;
+  unsigned scale_min = 0, scale_max = 0;
 };
 
 // Completion counters at the start of the scratch: zeroed when the scratch is
 // allocated and left at zero by every forward that uses them.
 constexpr int kMaxBands = 1024;
-constexpr size_t kCounterBytes = (1 + kMaxBands) * sizeof(uint32_t);
+constexpr size_t kCounterBytes = (2 + kMaxBands) * sizeof(uint32_t);  // done, err, bands
 
 struct Scratch {
   void *base = nullptr;
   size_t bytes = 0;
   uint32_t *done = nullptr, *band_done = nullptr;
+  int *err = nullptr;  // prefill pipeline timeout code
+  uint16_t *xp = nullptr, *h_hi = nullptr, *h_lo = nullptr;
+  float *pos_scale = nullptr;
   int32_t *active = nullptr, *n_active = nullptr;
   int32_t *idx = nullptr, *sigma = nullptr, *counts = nullptr, *offsets = nullptr;
   int32_t *perm = nullptr, *slot_pos = nullptr;
@@ -112,6 +119,7 @@ struct oxg_ctx {
   int last_layer = -1;
   int n_sms = 148;
   long long launches = 0;
+  bool prefill_pending = false;  // a prefill ran since the error word was last read
   Profiler prof;
 };
 
@@ -189,9 +197,16 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_perm = take(S * 4), *p_slot = take(S * 4);
   char *p_h = take(S * d.intermediate * 4), *p_y = take(S * d.hidden * 4);
   char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
+  char *p_xp = take(S * d.hidden * 2), *p_hhi = take(S * d.intermediate * 2);
+  char *p_hlo = take(S * d.intermediate * 2), *p_psc = take(S * 4);
   if (s && base) {
     s->done = (uint32_t *)p_cnt;
-    s->band_done = s->done + 1;
+    s->err = (int *)(s->done + 1);
+    s->band_done = s->done + 2;
+    s->xp = (uint16_t *)p_xp;
+    s->h_hi = (uint16_t *)p_hhi;
+    s->h_lo = (uint16_t *)p_hlo;
+    s->pos_scale = (float *)p_psc;
     s->active = (int32_t *)p_active;
     s->n_active = (int32_t *)p_nactive;
     s->idx = (int32_t *)p_idx;
@@ -355,9 +370,60 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   return OXG_OK;
 }
 
-int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
+// Prefill path: routing and permutation, the slot-ordered f16 activations,
+// the two tcgen05 grouped GEMMs and the weighted combine.
+int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
+  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
+  if (rc) return rc;
+  OXG_CUDA(ctx, launch(ctx, "permute", [&] {
+             return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts,
+                                        ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos,
+                                        ctx->stream);
+           }),
+           "permute launch");
+  OXG_CUDA(ctx, launch(ctx, "gather_f16", [&] {
+             return oxg::launch_gather_f16(x, ctx->ws.perm, ctx->ws.sigma, S, d.hidden, d.top_k,
+                                           ctx->ws.xp, ctx->ws.pos_scale, ctx->ws.err,
+                                           ctx->stream);
+           }),
+           "gather launch");
+  const oxg::MoeDeviceWeights w = device_weights(L);
+  oxg::PrefillIO io{};
+  io.S = S;
+  io.counts = ctx->ws.counts;
+  io.offsets = ctx->ws.offsets;
+  io.expert_base = 0;
+  io.n_local_experts = d.n_experts;
+  io.xp = ctx->ws.xp;
+  io.pos_scale = ctx->ws.pos_scale;
+  io.h_hi = ctx->ws.h_hi;
+  io.h_lo = ctx->ws.h_lo;
+  io.y_slot = ctx->ws.y_slot;
+  io.err = ctx->ws.err;
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp1_prefill", [&] {
+             return oxg::launch_prefill_mlp1(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp1 launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp2_prefill", [&] {
+             return oxg::launch_prefill_mlp2(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp2 launch");
+  OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+             return oxg::launch_combine(ctx->ws.y_slot, ctx->ws.slot_pos, ctx->ws.wts, T,
+                                        d.hidden, d.top_k, y, ctx->stream);
+           }),
+           "combine launch");
+  ctx->prefill_pending = true;
+  return OXG_OK;
+}
+
+int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, int mode) {
+  const oxg_moe_dims &d = L.dims;
+  const int S = T * d.top_k;
+  if (mode == OXG_MODE_PREFILL || (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && L.prefill_ok))
+    return forward_prefill(ctx, L, x, T, y);
   if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y);
   int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
   if (rc) return rc;
@@ -387,6 +453,22 @@ int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   return OXG_OK;
 }
 
+// Reads (and clears) the prefill kernels' timeout code after the work has run.
+int read_pipeline_error(oxg_ctx *ctx) {
+  if (!ctx->prefill_pending || !ctx->ws.err) return OXG_OK;
+  int h = 0;
+  OXG_CUDA(ctx, cudaMemcpyAsync(&h, ctx->ws.err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream),
+           "read pipeline status");
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  ctx->prefill_pending = false;
+  if (h) {
+    cudaMemsetAsync(ctx->ws.err, 0, sizeof(int), ctx->stream);
+    return fail(ctx, h >= 100 ? OXG_ERR_CUDA : OXG_ERR_TIMEOUT,
+                h >= 100 ? "prefill self-check failed (code %d)" : "prefill pipeline wait timed out (stage %d)", h);
+  }
+  return OXG_OK;
+}
+
 int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void *y, int mode,
                        int precision, Layer **out) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
@@ -396,8 +478,11 @@ int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void
   if (T > 0 && (!x || !y)) return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be non-NULL");
   if (mode != OXG_MODE_AUTO && mode != OXG_MODE_DECODE && mode != OXG_MODE_PREFILL)
     return fail(ctx, OXG_ERR_INVALID_ARG, "unknown mode %d", mode);
-  if (mode == OXG_MODE_PREFILL)
-    return fail(ctx, OXG_ERR_UNSUPPORTED, "prefill mode is not available in this build");
+  if (mode == OXG_MODE_PREFILL && !L->prefill_ok)
+    return fail(ctx, OXG_ERR_UNSUPPORTED,
+                "prefill mode needs hidden and intermediate multiples of 64 and E8M0 scales "
+                "0 or in [104, 141]; this layer has scales in [%u, %u]",
+                L->scale_min, L->scale_max);
   if (precision != OXG_PRECISION_PARITY)
     return fail(ctx, OXG_ERR_UNSUPPORTED, "unknown precision %d", precision);
   *out = L;
@@ -502,7 +587,7 @@ int oxg_sync(oxg_ctx *ctx) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
   DeviceGuard g(ctx->device);
   OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
-  return OXG_OK;
+  return read_pipeline_error(ctx);
 }
 
 int oxg_dequant_mxfp4(oxg_ctx *ctx, const uint8_t *blocks, size_t n_block_bytes,
@@ -613,7 +698,19 @@ int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_
     if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w2, E * H, (int)I, s))) return e;
     if ((e = cudaMemcpyAsync(stage, w->w2_scales, E * H * (I / 32), cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s2, E * H, (int)I, s))) return e;
-    return cudaStreamSynchronize(s);
+    // scale range over both matrices (padding bytes are zero and ignored)
+    const unsigned init[2] = {255u, 0u};
+    if ((e = cudaMemcpyAsync(stage, init, sizeof(init), cudaMemcpyHostToDevice, s))) return e;
+    if ((e = oxg::launch_scale_range(L.s1, n_s1, (unsigned *)stage, s))) return e;
+    if ((e = oxg::launch_scale_range(L.s2, n_s2, (unsigned *)stage, s))) return e;
+    unsigned mm[2] = {0u, 0u};
+    if ((e = cudaMemcpyAsync(mm, stage, sizeof(mm), cudaMemcpyDeviceToHost, s))) return e;
+    if ((e = cudaStreamSynchronize(s))) return e;
+    L.scale_min = mm[0];
+    L.scale_max = mm[1];
+    L.prefill_ok = H % 64 == 0 && I % 64 == 0 &&
+                   (mm[1] == 0u || (mm[0] >= 104u && mm[1] <= 141u));
+    return cudaSuccess;
   };
   st = body();
   cudaFree(stage);
@@ -657,7 +754,7 @@ int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y,
   rc = ensure_scratch(ctx, L->dims, T);
   if (rc) return rc;
   ctx->last_layer = layer;
-  return forward_device(ctx, *L, x, T, y);
+  return forward_device(ctx, *L, x, T, y, mode);
 }
 
 int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T, float *y_host,
@@ -673,12 +770,12 @@ int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T,
   const size_t H = L->dims.hidden;
   OXG_CUDA(ctx, cudaMemcpyAsync(ctx->ws.x_stage, x_host, (size_t)T * H * 2, cudaMemcpyDefault, ctx->stream),
            "copy x to device");
-  rc = forward_device(ctx, *L, ctx->ws.x_stage, T, ctx->ws.y_stage);
+  rc = forward_device(ctx, *L, ctx->ws.x_stage, T, ctx->ws.y_stage, mode);
   if (rc) return rc;
   OXG_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->ws.y_stage, (size_t)T * H * 4, cudaMemcpyDefault, ctx->stream),
            "copy y to host");
   OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
-  return OXG_OK;
+  return read_pipeline_error(ctx);
 }
 
 int oxg_moe_route(oxg_ctx *ctx, int layer, const uint16_t *x, int T, int32_t *idx, float *wts,

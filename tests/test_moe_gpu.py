@@ -164,8 +164,8 @@ def test_bad_arguments_are_errors(cuda_ctx):
     with pytest.raises(abi.OxgError, match="hidden must be a positive multiple of 32"):
         MoELayer(dict(d, hidden=48))
     layer = MoELayer(d)
-    with pytest.raises(abi.OxgError, match="prefill mode is not available"):
-        layer.forward(torch.zeros((2, 64), dtype=torch.int16, device="cuda"), mode=abi.OXG_MODE_PREFILL)
+    with pytest.raises(abi.OxgError, match="unknown mode 7"):
+        layer.forward(torch.zeros((2, 64), dtype=torch.int16, device="cuda"), mode=7)
     lib = abi.load()
     st = lib.oxg_moe_forward(cuda_ctx.handle, 999, None, 1, None, 0, 0)
     assert st == abi.OXG_ERR_STATE
