@@ -2,7 +2,7 @@
 """Benchmark of the MXFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_decode|dequant] [--tokens T]
+                    [--workload moe_decode|moe_prefill|dequant] [--tokens T]
 
 Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
   moe_decode  one MoE block forward over T tokens (default 8: the 8-token
@@ -11,6 +11,10 @@ Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
               Steps cycle over 4 uploaded layers (4 x 424 MB of packed
               weights), so inputs are larger than L2 and no step finds the
               previous step's weights cached. Metric: tokens/s.
+  moe_prefill 8192 tokens per GPU through one MoE block on the tcgen05
+              grouped-GEMM path (router logits ~N(0, 1), so expert loads are
+              roughly uniform). Metric: tokens/s; roofline: TFLOP/s of the
+              gate/up GEMM against the measured dense 16-bit tensor peak.
   dequant     standalone MXFP4 -> bf16 dequant of one layer's expert tensors
               (32x5760x2880 + 32x2880x2880, E8M0 in [110, 135]). Metric: GB/s
               of algorithmic traffic (423,014,400 B read + 1,592,524,800 B written).
@@ -50,6 +54,19 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+FALLBACK_TFLOPS = 1590.0
+
+
+def tensor_peak():
+    """Dense 16-bit tensor-core peak (burst figure: each kernel is timed alone)."""
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_TFLOPS, "fallback"
 
 
 def ncu_traffic(kernel: str, key: str):
@@ -167,7 +184,8 @@ def run_reference(args):
         sample = f"{rows} rows x {c1} cols of mlp1 per step ({per_step_bytes} B algorithmic)"
         config = {"workload": "dequant_layer", "rows": 32 * 5760 + 32 * 2880, "cols": 2880}
     else:
-        T = args.tokens
+        # bounded sample of the workload's tokens: one per host thread
+        T = min(args.tokens, max(threads, 1))
         d = synth.moe_layer(seed=0)
         x = synth.activations(0, T, d["hidden"])
         W = oracle.Weights(d)
@@ -180,8 +198,11 @@ def run_reference(args):
         dt = time.perf_counter() - t0
         value = T * args.steps / dt
         unit = "tokens/s"
-        sample = f"{T} tokens of one MoE block per step (reference algorithm, OpenMP over tokens)"
+        sample = (f"{T} of the workload's {args.tokens} tokens per step through one MoE block "
+                  f"(reference algorithm, OpenMP over tokens)")
         config = moe_config(args, d)
+        if args.workload == "moe_prefill":
+            config["workload"] = "moe_prefill"
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": ws,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -344,6 +365,120 @@ def run_moe(args, ws, rank, local):
     return out
 
 
+def run_prefill(args, ws, rank, local):
+    """8192 tokens per GPU through one gpt-oss-20b MoE layer on the tcgen05
+    grouped-GEMM path (router logits ~N(0, 1): x ~N(0, 1), W_router ~N(0, 0.02))."""
+    import torch
+    from oxidized_gpt_oss_b200 import abi, synth
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    from oxidized_gpt_oss_b200.mxfp4 import context
+
+    device = torch.device("cuda", local)
+    T = args.tokens
+    d0 = synth.moe_layer(seed=0)
+    H, I, E, K = d0["hidden"], d0["intermediate"], d0["n_experts"], d0["top_k"]
+    ctx = context(None)
+    layers = [MoELayer(d, ctx=ctx, layer=i) for i, d in enumerate(gpu_layers(args, d0, device))]
+    for L in layers:
+        L.reserve(T)
+    n_x = 2
+    xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
+    xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
+    y = torch.empty((T, H), dtype=torch.float32, device=device)
+    mode = abi.OXG_MODE_PREFILL
+
+    def step(i):
+        layers[i % len(layers)].forward(xs[i % n_x], out=y, mode=mode)
+
+    for i in range(args.warmup):
+        step(i)
+    ctx.sync()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+    ms = ev0.elapsed_time(ev1)
+    launches = ctx.launches() - launches0
+    ctx.sync()
+    ctx.profile(True)
+    ctx.profile_reset()
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    names = ("router_topk", "permute", "gather_f16", "moe_mlp1_prefill", "moe_mlp2_prefill", "combine")
+    k_ms = {n: ctx.profile_read(n) for n in names}
+    k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
+    ctx.profile(False)
+    ms_max = max_over_ranks(ms, ws)
+
+    S = T * K
+    flop1 = 2.0 * S * (2 * I) * H          # GEMM1 algorithmic FLOPs per step
+    flop2 = 2.0 * S * H * I                # GEMM2 (the f16 hi/lo split executes it twice)
+    peak, peak_kind = tensor_peak()
+    m1_ms, m1_n = k_ms["moe_mlp1_prefill"]
+    m2_ms, m2_n = k_ms["moe_mlp2_prefill"]
+    achieved = flop1 * m1_n / (m1_ms * 1e-3) / 1e12
+    layer_tflops = (flop1 + flop2) * args.steps / (ms * 1e-3) / 1e12
+
+    # end to end through the host-buffer API
+    xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
+    yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    for i in range(min(args.warmup, 2)):
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, ws)
+
+    out = {"metric": METRIC, "value": T * ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "mxfp4 weights x bf16 activations (exact f16 tcgen05 operands), f32 accumulate",
+           "data": "synthetic",
+           "config": {"workload": "moe_prefill", "tokens_per_gpu": T, "hidden": H, "intermediate": I,
+                      "experts": E, "top_k": K, "weights": "mxfp4 e2m1 + e8m0[118,126]",
+                      "layers_cycled": args.layers,
+                      "l2": "inputs larger than L2 (424 MB of packed weights and 189 MB of slot "
+                            "activations per step)",
+                      "parallelism": "replicas" if ws > 1 else "single"},
+           "roofline": {"bound": "tensor", "kernel": "moe_mlp1_prefill", "achieved": achieved, "peak": peak,
+                        "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
+                        "traffic": ncu_traffic("moe_mlp1_prefill", f"T{T}"),
+                        "algorithmic_flop_per_launch": flop1,
+                        "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3},
+           "layer": {"tflops": layer_tflops, "frac": layer_tflops / peak,
+                     "kernel_us_per_step": {n: v[0] / max(v[1], 1) * 1e3 for n, v in k_ms.items()},
+                     "mlp2_tflops": flop2 * m2_n / (m2_ms * 1e-3) / 1e12},
+           "e2e": {"value": T * ws * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
+           "gpu_launches": launches,
+           "clocks": clk.summary()}
+    if rank == 0 and ws == 1:
+        from oracle import oracle
+        n_cpu = 2
+        W = oracle.Weights(d0)
+        L = oracle.RefLayer(W, xs_np[0][:n_cpu])
+        t0 = time.perf_counter()
+        L.forward(xs_np[0][:n_cpu], nthreads=1)
+        dt = time.perf_counter() - t0
+        L.close()
+        out["cpu_baseline"] = {"value": n_cpu / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+                               "sample": f"{n_cpu} of the {T} tokens through the reference's algorithm, "
+                                         f"single thread, {dt:.2f} s"}
+    return out
+
+
 def run_dequant(args, ws, rank, local):
     import torch
     from oxidized_gpt_oss_b200 import synth
@@ -429,10 +564,13 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["moe_decode", "dequant"], default="moe_decode")
-    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant"], default="moe_decode")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
     args = ap.parse_args()
+    if args.tokens is None:
+        args.tokens = 8192 if args.workload == "moe_prefill" else 8
     if args.impl == "reference":
         run_reference(args)
         return
@@ -445,7 +583,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        out = run_dequant(args, ws, rank, local) if args.workload == "dequant" else run_moe(args, ws, rank, local)
+        run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe}[args.workload]
+        out = run(args, ws, rank, local)
         if rank == 0:
             emit(out)
     finally:

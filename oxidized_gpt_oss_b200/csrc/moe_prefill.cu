@@ -17,12 +17,12 @@
 //   warp 1      TMEM owner and MMA issuer: one thread issues
 //               tcgen05.mma.kind::f16 (f16 x f16 -> f32) into a double-buffered
 //               TMEM accumulator and commits to the stage / accumulator barriers;
-//   warps 2-5   converters: stream the MXFP4 codes and E8M0 scales through a
+//   warps 2-9   converters: stream the MXFP4 codes and E8M0 scales through a
 //               per-thread cp.async ring, decode with cvt.rn.f16x2.e2m1x2,
 //               multiply each 32-element block by its scale in f16 (exact for
 //               scales 2^-23..2^14, which the upload checks) and store the
 //               weight tile in the tensor cores' swizzled K-major layout;
-//   warps 6-9   epilogue: tcgen05.ld of the accumulator (one TMEM lane per
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator (one TMEM lane per
 //               weight row), bias, then for GEMM1 the gate/up pairing across
 //               adjacent lanes, the 2^sigma token scale and the clamped SwiGLU
 //               (h split into f16 hi + lo), for GEMM2 the f32 slot rows.
@@ -43,9 +43,9 @@ constexpr int BM = 128;             // weight rows per tile (MMA M)
 constexpr int BK = 64;              // K per stage (one 128-byte swizzle atom of f16)
 constexpr int kStagesP = 3;         // A/B stage ring
 constexpr int kCodeStages = 6;      // converter cp.async ring (k-steps in flight)
-constexpr int kConvWarps = 4;
+constexpr int kConvWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kThreadsP = (2 + kConvWarps + kEpiWarps) * 32;  // 320
+constexpr int kThreadsP = (2 + kConvWarps + kEpiWarps) * 32;  // 448
 constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kTasks = BM * 4 / kConvThreads;  // (row, lane-in-quad) tasks per converter thread
 constexpr int kTmemCols = 512;
@@ -313,11 +313,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             e2m1x8_to_f16x8(cw[t].y, f);
             o1 = make_uint4(hmul2(f[0], h1), hmul2(f[1], h1), hmul2(f[2], h1), hmul2(f[3], h1));
           }
-          // chunks q (block 2hf) and 4 + q (block 2hf + 1), 128-byte swizzle
+          // chunks q (block 2hf) and 4 + q (block 2hf + 1), 128-byte swizzle.
+          // Odd rows store their two chunks in the opposite order, so the 8
+          // lanes (two rows) of each store wavefront hit 8 different banks.
           const int x7 = r_ & 7;
           uint8_t *rowp = atile + (r_ >> 3) * 1024 + x7 * 128;
-          *reinterpret_cast<uint4 *>(rowp + ((q ^ x7) << 4)) = o0;
-          *reinterpret_cast<uint4 *>(rowp + (((4 + q) ^ x7) << 4)) = o1;
+          const bool odd = r_ & 1;
+          *reinterpret_cast<uint4 *>(rowp + (((odd ? 4 + q : q) ^ x7) << 4)) = odd ? o1 : o0;
+          *reinterpret_cast<uint4 *>(rowp + (((odd ? q : 4 + q) ^ x7) << 4)) = odd ? o0 : o1;
         }
         fence_proxy_async_smem();
         __syncwarp();
