@@ -135,7 +135,7 @@ cudaError_t launch_gather_f16(const uint16_t *x, const int32_t *perm, const int3
                               int H, int topk, uint16_t *xp, float *pos_scale, int *err,
                               cudaStream_t stream);
 // tcgen05 grouped GEMMs (persistent grid of n_sms CTAs). Need H and I
-// multiples of 64 and every E8M0 scale 0 or in [104, 141].
+// multiples of 64 and every E8M0 scale 0 or in [104, 140].
 cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream);
 cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,

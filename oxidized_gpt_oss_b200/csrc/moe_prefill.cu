@@ -39,17 +39,21 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;             // weight rows per tile (MMA M)
+constexpr int BM = 128;             // weight rows per CTA (the pair's MMA has M = 256)
+constexpr int BN = 256;             // token columns per tile (MMA N)
+constexpr int BNH = BN / 2;         // token rows of the tile each CTA loads
 constexpr int BK = 64;              // K per stage (one 128-byte swizzle atom of f16)
-constexpr int kStagesP = 3;         // A/B stage ring
-constexpr int kCodeStages = 6;      // converter cp.async ring (k-steps in flight)
 constexpr int kConvWarps = 8;
-constexpr int kEpiWarps = 4;
-constexpr int kThreadsP = (2 + kConvWarps + kEpiWarps) * 32;  // 448
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, alternating 32-column chunks
+constexpr int kThreadsP = (2 + kConvWarps + kEpiWarps) * 32;  // 576
 constexpr int kConvThreads = kConvWarps * 32;
-constexpr int kTasks = BM * 4 / kConvThreads;  // (row, lane-in-quad) tasks per converter thread
+// The converter warps form kGroups groups; group g fills the A tiles of the
+// k-steps it with it % kGroups == g, so each warp pays the per-step waits and
+// fences once per kGroups k-steps and decodes kTasks (row, q) tasks per step.
+constexpr int kGroups = 2;
+constexpr int kGroupThreads = kConvThreads / kGroups;
+constexpr int kTasks = BM * 4 / kGroupThreads;
 constexpr int kTmemCols = 512;
-constexpr int kCodeStageBytes = kTasks * kConvThreads * 12;  // 8 B codes + 4 B scales per task
 constexpr int kMaxExpertsP = 256;
 
 struct PrefillArgs {
@@ -75,10 +79,6 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
-__device__ __forceinline__ void cp_async_8(void *smem, const void *gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(smem)), "l"(gmem)
-               : "memory");
-}
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -100,39 +100,43 @@ struct Coords {
   int m0;      // first weight row of the tile
 };
 
-template <int GEMM, int BN>
+template <int GEMM, int STAGES>
 __global__ void __launch_bounds__(kThreadsP, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap tm0,
                         const __grid_constant__ CUtensorMap tm1, const PrefillArgs a) {
   constexpr int NB = GEMM == 1 ? 1 : 2;  // token tiles per stage (GEMM2: h hi and lo)
-  constexpr int A_BYTES = BM * BK * 2;
-  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int A_BYTES = BM * BK * 2;   // this CTA's 128 weight rows
+  constexpr int B_BYTES = BNH * BK * 2;  // this CTA's half of the token tile
   constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  constexpr int kLead = 2;  // a converter group's own k-steps whose codes are in registers
+  static_assert(STAGES % kGroups == 0, "every converter group owns the same stages");
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the shared-space offset (the swizzle atoms of the
-  // TMA tiles and the MMA descriptors assume it)
+  // TMA tiles and the MMA descriptors assume it); the same in both CTAs
   uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint8_t *tiles = smem;
-  uint8_t *code_ring = tiles + kStagesP * STAGE_BYTES;
-  uint8_t *epi = code_ring + kCodeStages * kCodeStageBytes;  // GEMM1 output staging
 
-  __shared__ uint64_t full_a[kStagesP], full_b[kStagesP], empty_[kStagesP];
+  // full_, acc_empty and mma_done are used in rank 0 only; empty_ and
+  // acc_full in both CTAs
+  __shared__ uint64_t full_[STAGES], empty_[STAGES];
   __shared__ uint64_t acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_slot;
   __shared__ int ntile_prefix[kMaxExpertsP + 1];
   __shared__ int epi_ok;
+  __shared__ float col_scale[BN];  // GEMM1: 2^sigma of each column of the current item
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
   const int E = a.n_experts;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStagesP; ++s) {
-      mbar_init(&full_a[s], kConvWarps);
-      mbar_init(&full_b[s], 1);
+    for (int s = 0; s < STAGES; ++s) {
+      // both CTAs' converter groups + rank 0's expect_tx arrival
+      mbar_init(&full_[s], 2 * (kConvWarps / kGroups) + 1);
       mbar_init(&empty_[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);
     }
     mbar_init(&mma_done, 1);
     fence_mbar_init();
@@ -144,21 +148,23 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     ntile_prefix[E] = run;
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(&tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  const int MT = (a.rows + BM - 1) / BM;
+  const int MT = (a.rows + 2 * BM - 1) / (2 * BM);  // 256-row tiles of the pair
   const int total = ntile_prefix[E] * MT;
   const int KSTEPS = a.K / BK;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   auto coords = [&](int item) {
     Coords c;
     const int ntg = item / MT;
-    c.m0 = (item - ntg * MT) * BM;
+    c.m0 = (item - ntg * MT) * 2 * BM;
     int e = 0;
     while (e + 1 < E && ntile_prefix[e + 1] <= ntg) ++e;
     c.e = e;
@@ -166,252 +172,278 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     c.nvalid = min(BN, a.counts[a.expert_base + e] - c.n0);
     return c;
   };
+  // rank 0's full barriers as seen from either CTA
+  auto full_cl = [&](int s) { return mapa_shared(smem_addr(&full_[s]), 0); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // Each CTA loads its half of the token tile: rank 0 columns [0, n/2),
+    // rank 1 [n/2, n) of the n-column MMA (n = valid columns rounded up to
+    // 16); the bytes of both are counted on rank 0's full barrier.
     if (lane == 0) {
       prefetch_tmap(&tm0);
       if (NB == 2) prefetch_tmap(&tm1);
       int it = 0;
-      int last_round[kStagesP] = {-1, -1, -1};
+      int last_round[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_round[s] = -1;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+      for (int item = pair; ok && item < total; item += n_pairs) {
         const Coords c = coords(item);
-        const int row0 = a.offsets[a.expert_base + c.e] + c.n0;
+        const int n_mma = (c.nvalid + 15) / 16 * 16;
+        const int row0 = a.offsets[a.expert_base + c.e] + c.n0 + (rank ? n_mma / 2 : 0);
         for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
-          const int s = it % kStagesP, r = it / kStagesP;
-          if (r > 0 && !(ok = mbar_wait(&empty_[s], (r - 1) & 1, a.err, 1))) break;
+          const int s = it % STAGES, r = it / STAGES;
+          if (r > 0 && !(ok = mbar_wait_cl(&empty_[s], (r - 1) & 1, a.err, 1))) break;
           uint8_t *st = tiles + s * STAGE_BYTES;
           if (misaligned(smem_addr(st + A_BYTES), 1024, a.err, 101) ||
               misaligned((uint64_t)&tm0, 64, a.err, 102)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_b[s], NB * B_BYTES);
-          tma_load_2d(st + A_BYTES, &tm0, &full_b[s], ks * BK, row0);
-          if (NB == 2) tma_load_2d(st + A_BYTES + B_BYTES, &tm1, &full_b[s], ks * BK, row0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_[s], 2 * NB * B_BYTES);
+          tma_load_2d_pair(st + A_BYTES, &tm0, full_cl(s), ks * BK, row0);
+          if (NB == 2) tma_load_2d_pair(st + A_BYTES + B_BYTES, &tm1, full_cl(s), ks * BK, row0);
           last_round[s] = r;
         }
       }
-      if (!ok) {  // let copies still in flight land before the CTA exits
-        for (int s = 0; s < kStagesP; ++s)
-          if (last_round[s] >= 0) mbar_wait(&full_b[s], last_round[s] & 1, a.err, 1);
+      if (!ok && rank == 0) {  // let copies still in flight land before the pair exits
+        for (int s = 0; s < STAGES; ++s)
+          if (last_round[s] >= 0) mbar_wait_cl(&full_[s], last_round[s] & 1, a.err, 1);
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (lane == 0 && rank == 0) {
       int it = 0, j = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
+      // stage s's A tile starts at tiles + s * STAGE_BYTES, its B tile(s) A_BYTES
+      // later; shared addresses stay below 2^18, so adding to the 14-bit start
+      // field of the descriptor never carries into the next field
+      const uint64_t desc_a0 = desc_sw128_kmajor(smem_addr(tiles));
+      for (int item = pair; ok && item < total; item += n_pairs, ++j) {
         const Coords c = coords(item);
         const int buf = j & 1, rr = j >> 1;
-        if (rr > 0 && !(ok = mbar_wait(&acc_empty[buf], (rr - 1) & 1, a.err, 3))) break;
+        if (rr > 0 && !(ok = mbar_wait_cl(&acc_empty[buf], (rr - 1) & 1, a.err, 3))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
         const int n_mma = (c.nvalid + 15) / 16 * 16;
-        const uint32_t idesc = idesc_f16_f32(BM, n_mma);
+        const uint32_t idesc = idesc_f16_f32(2 * BM, n_mma);
         for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
-          const int s = it % kStagesP, r = it / kStagesP;
-          if (!(ok = mbar_wait(&full_a[s], r & 1, a.err, 2))) break;
-          if (!(ok = mbar_wait(&full_b[s], r & 1, a.err, 2))) break;
+          const int s = it % STAGES, r = it / STAGES;
+          if (!(ok = mbar_wait_cl(&full_[s], r & 1, a.err, 2))) break;
           tc_fence_after();
-          const uint32_t sa = smem_addr(tiles + s * STAGE_BYTES);
-          const uint32_t sb = sa + A_BYTES;
+          // descriptors of k16 slice 0; slice kk starts 32 B (2 units) further
+          const uint64_t ad = desc_a0 + (uint64_t)(s * (STAGE_BYTES >> 4));
+          const uint64_t bd = ad + (uint64_t)(A_BYTES >> 4);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = desc_sw128_kmajor(sa + kk * 32);
-            umma_f16(d, ad, desc_sw128_kmajor(sb + kk * 32), idesc, (ks | kk) != 0);
-            if (NB == 2) umma_f16(d, ad, desc_sw128_kmajor(sb + B_BYTES + kk * 32), idesc, 1);
+            umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+            if (NB == 2) umma_f16_pair(d, ad + 2 * kk, bd + (B_BYTES >> 4) + 2 * kk, idesc, 1);
           }
-          umma_commit(&empty_[s]);
+          const uint32_t e_own = smem_addr(&empty_[s]);
+          umma_commit_pair(mapa_shared(e_own, 0));
+          umma_commit_pair(mapa_shared(e_own, 1));
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok) {
+          const uint32_t f_own = smem_addr(&acc_full[buf]);
+          umma_commit_pair(mapa_shared(f_own, 0));
+          umma_commit_pair(mapa_shared(f_own, 1));
+        }
       }
       // nothing may be left in flight when TMEM is released
-      umma_commit(&mma_done);
-      mbar_wait(&mma_done, 0, a.err, 2);
+      umma_commit_pair(mapa_shared(smem_addr(&mma_done), 0));
+      mbar_wait_cl(&mma_done, 0, a.err, 2);
     }
   } else if (warp < 2 + kConvWarps) {
     // ------------------------------------------------------------ converters
+    // Thread gt of group grp owns kTasks (row, q) pairs of each of its weight
+    // tiles: row (gt + t * kGroupThreads) / 4, 16-byte chunks q (block 2hf of
+    // the k-step pair) and 4 + q (block 2hf + 1). Its codes (8 B: word q of
+    // the two blocks, adjacent in the relaid order) and the two scale bytes
+    // are loaded into registers kLead of its k-steps before use.
     const int ct = threadIdx.x - 64;
-    const int q = ct & 3;
-    const int nb = a.K / 32, full = nb / 4;
-    // issue side of the per-thread code ring: runs kCodeStages k-steps ahead
-    int i_item = blockIdx.x, i_ks = 0, i_slot = 0;
-    Coords ic = i_item < total ? coords(i_item) : Coords{0, 0, 0, 0};
-    auto issue_next = [&]() {
-      if (i_item < total) {
-        uint8_t *slot = code_ring + i_slot * kCodeStageBytes;
-        const int G = i_ks >> 1, hf = i_ks & 1;
-        const size_t ebase = (size_t)(a.expert_base + ic.e) * a.rows;
+    const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
+    const int q = gt & 3;
+    const int full = a.K / 128;  // complete 4-block groups per row
+    const int row_bytes = a.K / 2;
+    // issue cursor: this group's k-steps as (item, ks), kGroups steps apart
+    int i_item = pair, i_ks = grp;
+    // task t's row is row0 + t * (kGroupThreads / 4): codes at crow + t * cstep
+    const uint8_t *crow = a.codes, *srow = a.scales;
+    const int cstep = (kGroupThreads / 4) * row_bytes, sstep = (kGroupThreads / 4) * a.kb_pad;
+    int n_rows_ok = 0;  // tasks 0 .. n_rows_ok - 1 lie inside the matrix
+    auto set_rows = [&](int item) {
+      const Coords c = coords(item);
+      const int R0 = c.m0 + (int)rank * BM + (gt >> 2);
+      const size_t erow = (size_t)(a.expert_base + c.e) * a.rows + R0;
+      crow = a.codes + erow * row_bytes;
+      srow = a.scales + erow * a.kb_pad;
+      n_rows_ok = R0 < a.rows ? min(kTasks, (a.rows - R0 + kGroupThreads / 4 - 1) / (kGroupThreads / 4)) : 0;
+    };
+    auto normalise = [&]() {
+      while (i_item < total && i_ks >= KSTEPS) {
+        i_ks -= KSTEPS;
+        i_item += n_pairs;
+      }
+    };
+    normalise();
+    if (i_item < total) set_rows(i_item);
+    auto load_step = [&](uint2 (&cw)[kTasks], uint32_t (&sw)[kTasks]) {
+      const int G = i_ks >> 1, hf = i_ks & 1;
+      const int off = G < full ? G * 64 + q * 16 + hf * 8 : G * 64 + q * 8;
 #pragma unroll
-        for (int t = 0; t < kTasks; ++t) {
-          const int r = (ct + t * kConvThreads) >> 2;
-          const int R = ic.m0 + r;
-          if (R < a.rows) {
-            const uint8_t *row = a.codes + (ebase + R) * (size_t)(a.K / 2);
-            const int off = G < full ? G * 64 + q * 16 + hf * 8 : G * 64 + q * 8;
-            uint8_t *d8 = slot + (t * kConvThreads + ct) * 8;
-            uint8_t *d4 = slot + kTasks * kConvThreads * 8 + (t * kConvThreads + ct) * 4;
-            const uint8_t *s4 = a.scales + (ebase + R) * (size_t)a.kb_pad + G * 4;
-            if (!misaligned((uint64_t)(row + off), 8, a.err, 103) &&
-                !misaligned(smem_addr(d8), 8, a.err, 104))
-              cp_async_8(d8, row + off);
-            if (!misaligned((uint64_t)s4, 4, a.err, 105) && !misaligned(smem_addr(d4), 4, a.err, 106))
-              cp_async_4(d4, s4);
-          }
-        }
-        if (++i_ks == KSTEPS) {
-          i_ks = 0;
-          i_item += gridDim.x;
-          if (i_item < total) ic = coords(i_item);
+      for (int t = 0; t < kTasks; ++t) {
+        cw[t] = make_uint2(0u, 0u);
+        sw[t] = 0u;
+        if (i_item < total && t < n_rows_ok) {
+          cw[t] = __ldg(reinterpret_cast<const uint2 *>(crow + t * cstep + off));
+          sw[t] = __ldg(reinterpret_cast<const unsigned short *>(srow + t * sstep + G * 4 + 2 * hf));
         }
       }
-      cp_async_commit();
-      if (++i_slot == kCodeStages) i_slot = 0;
+      if (i_item < total) {
+        const int prev = i_item;
+        i_ks += kGroups;
+        normalise();
+        if (i_item != prev && i_item < total) set_rows(i_item);
+      }
     };
-#pragma unroll 1
-    for (int u = 0; u < kCodeStages; ++u) issue_next();
-    int it = 0, c_slot = 0;
+    uint2 rc[kLead][kTasks];
+    uint32_t rs[kLead][kTasks];
+#pragma unroll
+    for (int u = 0; u < kLead; ++u) load_step(rc[u], rs[u]);
+
+    const int my_items = pair < total ? (total - 1 - pair) / n_pairs + 1 : 0;
+    const int n_steps = my_items * KSTEPS;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
-      const Coords c = coords(item);
-      for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
-        const int s = it % kStagesP, r = it / kStagesP;
-        cp_async_wait<kCodeStages - 1>();
-        const uint8_t *slot = code_ring + c_slot * kCodeStageBytes;
-        uint2 cw[kTasks];
-        uint32_t sw[kTasks];
+    for (int m0 = 0; ok && grp + m0 * kGroups < n_steps; m0 += kLead) {
+#pragma unroll
+      for (int u = 0; u < kLead; ++u) {
+        const int it = grp + (m0 + u) * kGroups;
+        if (it >= n_steps) break;
+        const int s = it % STAGES, r = it / STAGES;
+        // decode first (rows beyond the matrix load zero codes and scales)
+        uint4 o[kTasks][2];
 #pragma unroll
         for (int t = 0; t < kTasks; ++t) {
-          cw[t] = *reinterpret_cast<const uint2 *>(slot + (t * kConvThreads + ct) * 8);
-          sw[t] = *reinterpret_cast<const uint32_t *>(slot + kTasks * kConvThreads * 8 +
-                                                      (t * kConvThreads + ct) * 4);
+          const uint32_t s0 = rs[u][t] & 0xFFu, s1 = rs[u][t] >> 8;
+          const uint32_t h0 = pack_f16x2(e8m0_to_f32(s0), e8m0_to_f32(s0));
+          const uint32_t h1 = pack_f16x2(e8m0_to_f32(s1), e8m0_to_f32(s1));
+          uint32_t f[4];
+          e2m1x8_to_f16x8(rc[u][t].x, f);
+          o[t][0] = make_uint4(hmul2(f[0], h0), hmul2(f[1], h0), hmul2(f[2], h0), hmul2(f[3], h0));
+          e2m1x8_to_f16x8(rc[u][t].y, f);
+          o[t][1] = make_uint4(hmul2(f[0], h1), hmul2(f[1], h1), hmul2(f[2], h1), hmul2(f[3], h1));
         }
-        issue_next();
-        if (++c_slot == kCodeStages) c_slot = 0;
-        if (r > 0) {  // one lane waits, the warp follows its verdict
+        load_step(rc[u], rs[u]);  // this group's step kLead ahead
+        if (r > 0) {  // one lane waits for the MMAs to free the stage; the warp follows
           int w_ok = 1;
-          if (lane == 0) w_ok = mbar_wait(&empty_[s], (r - 1) & 1, a.err, 5);
+          if (lane == 0) w_ok = mbar_wait_cl(&empty_[s], (r - 1) & 1, a.err, 5);
           if (!(ok = __shfl_sync(0xFFFFFFFFu, w_ok, 0) != 0)) break;
         }
         uint8_t *atile = tiles + s * STAGE_BYTES;
-        const int hf = ks & 1;
 #pragma unroll
         for (int t = 0; t < kTasks; ++t) {
-          const int r_ = (ct + t * kConvThreads) >> 2;
-          const int R = c.m0 + r_;
-          uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
-          if (R < a.rows) {
-            const uint32_t s0 = (sw[t] >> (16 * hf)) & 0xFFu, s1 = (sw[t] >> (16 * hf + 8)) & 0xFFu;
-            const uint32_t h0 = pack_f16x2(e8m0_to_f32(s0), e8m0_to_f32(s0));
-            const uint32_t h1 = pack_f16x2(e8m0_to_f32(s1), e8m0_to_f32(s1));
-            uint32_t f[4];
-            e2m1x8_to_f16x8(cw[t].x, f);
-            o0 = make_uint4(hmul2(f[0], h0), hmul2(f[1], h0), hmul2(f[2], h0), hmul2(f[3], h0));
-            e2m1x8_to_f16x8(cw[t].y, f);
-            o1 = make_uint4(hmul2(f[0], h1), hmul2(f[1], h1), hmul2(f[2], h1), hmul2(f[3], h1));
-          }
-          // chunks q (block 2hf) and 4 + q (block 2hf + 1), 128-byte swizzle.
-          // Odd rows store their two chunks in the opposite order, so the 8
-          // lanes (two rows) of each store wavefront hit 8 different banks.
+          const int r_ = (gt + t * kGroupThreads) >> 2;
+          // chunks q and 4 + q of the row under the 128-byte swizzle. Odd rows
+          // store their two chunks in the opposite order, so the 8 lanes (two
+          // rows) of each store wavefront hit 8 different bank groups.
           const int x7 = r_ & 7;
           uint8_t *rowp = atile + (r_ >> 3) * 1024 + x7 * 128;
           const bool odd = r_ & 1;
-          *reinterpret_cast<uint4 *>(rowp + (((odd ? 4 + q : q) ^ x7) << 4)) = odd ? o1 : o0;
-          *reinterpret_cast<uint4 *>(rowp + (((odd ? q : 4 + q) ^ x7) << 4)) = odd ? o0 : o1;
+          *reinterpret_cast<uint4 *>(rowp + (((odd ? 4 + q : q) ^ x7) << 4)) = odd ? o[t][1] : o[t][0];
+          *reinterpret_cast<uint4 *>(rowp + (((odd ? q : 4 + q) ^ x7) << 4)) = odd ? o[t][0] : o[t][1];
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
+        if (lane == 0) mbar_arrive_cluster(full_cl(s));
       }
     }
-    cp_async_wait<0>();
   } else {
     // ------------------------------------------------------------ epilogue
     const int lq = warp & 3;            // TMEM lane quarter this warp may access
     const int ew = warp - (2 + kConvWarps);
+    const int half = ew >> 2;           // which 32-column chunks: 2m + half
     const int r = lq * 32 + lane;       // accumulator row = weight row within the tile
+    const int up_row = lane & 1;
     int j = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x, ++j) {
+    for (int item = pair; item < total; item += n_pairs, ++j) {
       const Coords c = coords(item);
       const int buf = j & 1, rr = j >> 1;
+      const int eg = a.expert_base + c.e;
+      const int pos_base = a.offsets[eg] + c.n0;
       // one thread waits; the four epilogue warps follow its verdict together
-      if (ew == 0 && lane == 0) epi_ok = mbar_wait(&acc_full[buf], rr & 1, a.err, 4);
+      if (ew == 0 && lane == 0) epi_ok = mbar_wait_cl(&acc_full[buf], rr & 1, a.err, 4);
       named_bar_sync(1, kEpiWarps * 32);
       const bool ok = epi_ok != 0;
+      if (GEMM == 1)  // every warp is past the previous item: refill the column scales
+        for (int col = ew * 32 + lane; col < BN; col += kEpiWarps * 32)
+          col_scale[col] = col < c.nvalid ? a.pos_scale[pos_base + col] : 0.f;
       named_bar_sync(1, kEpiWarps * 32);
       if (!ok) break;
       tc_fence_after();
-      const int eg = a.expert_base + c.e;
-      const int pos_base = a.offsets[eg] + c.n0;
-      const int R = c.m0 + r;
+      const int R = c.m0 + (int)rank * BM + r;
       const float bias_own = R < a.rows ? bf16_to_f32(a.bias[(size_t)eg * a.rows + R]) : 0.f;
       const float bias_other = __shfl_xor_sync(0xFFFFFFFFu, bias_own, 1);
-      const bool up_row = lane & 1;
-      for (int c0 = 0; c0 < c.nvalid; c0 += 32) {
-        float v[32];
-        tmem_ld_32(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(buf * BN + c0), v);
+      const float bg = up_row ? bias_other : bias_own, bu = up_row ? bias_own : bias_other;
+      const bool row_ok = R < a.rows;
+
+      // one 32-column chunk of the accumulator, straight to global memory
+      auto process = [&](const uint32_t(&v)[32], int c0) {
+        const int ncol = min(32, c.nvalid - c0);
         if (GEMM == 2) {
-          if (R < a.H) {
-            const int ncol = min(32, c.nvalid - c0);
-            for (int cc = 0; cc < ncol; ++cc)
-              a.y_slot[(size_t)(pos_base + c0 + cc) * a.H + R] = v[cc] + bias_own;
+          if (row_ok) {
+            float *dst = a.y_slot + (size_t)(pos_base + c0) * a.H + R;
+#pragma unroll
+            for (int cc = 0; cc < 32; ++cc)
+              if (cc < ncol) dst[(size_t)cc * a.H] = __uint_as_float(v[cc]) + bias_own;
           }
         } else {
-          // gate (even lane) and up (odd lane) of pair p = R / 2; each lane of
-          // the pair computes the SwiGLU for every other column
-          uint16_t *st_hi = reinterpret_cast<uint16_t *>(epi);
-          uint16_t *st_lo = st_hi + 32 * 64;
-          const float bg = up_row ? bias_other : bias_own, bu = up_row ? bias_own : bias_other;
+          // Gate (even lane) and up (odd lane) rows of pair R / 2: for each
+          // column pair the even lane finishes the even column and the odd
+          // lane the odd one, so all 32 lanes run the SwiGLU together. Each
+          // store writes 16 consecutive f16 of two token rows.
+          const size_t cstride = (size_t)a.I;
+          uint16_t *hh = a.h_hi + (size_t)(pos_base + c0) * cstride + (R >> 1);
+          uint16_t *hl = a.h_lo + (size_t)(pos_base + c0) * cstride + (R >> 1);
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) {
-            const float other = __shfl_xor_sync(0xFFFFFFFFu, v[cc], 1);
-            if ((cc & 1) == (int)up_row) {
-              const int col = c0 + cc;
-              float hv = 0.f;
-              if (col < c.nvalid) {
-                const float sc = a.pos_scale[pos_base + col];
-                const float g = up_row ? other : v[cc], u = up_row ? v[cc] : other;
-                hv = swiglu_clamped(fmaf(g, sc, bg), fmaf(u, sc, bu), a.alpha, a.limit);
-              }
-              const uint32_t hi2 = pack_f16x2(hv, 0.f);
-              const float hi = unpack_f16x2(hi2).x;
-              const uint32_t lo2 = pack_f16x2(hv - hi, 0.f);
-              st_hi[cc * 64 + (r >> 1)] = (uint16_t)(hi2 & 0xFFFFu);
-              st_lo[cc * 64 + (r >> 1)] = (uint16_t)(lo2 & 0xFFFFu);
+          for (int cp = 0; cp < 16; ++cp) {
+            const float ve = __uint_as_float(v[2 * cp]), vo = __uint_as_float(v[2 * cp + 1]);
+            const float oe = __shfl_xor_sync(0xFFFFFFFFu, ve, 1);
+            const float oo = __shfl_xor_sync(0xFFFFFFFFu, vo, 1);
+            const int cc = 2 * cp + up_row;
+            const float sc = col_scale[c0 + cc];
+            const float g = up_row ? oo : ve, u = up_row ? vo : oe;
+            const float hv = swiglu_clamped_fast(fmaf(g, sc, bg), fmaf(u, sc, bu), a.alpha, a.limit);
+            const uint32_t hi2 = pack_f16x2(hv, 0.f);
+            const uint32_t lo2 = pack_f16x2(hv - unpack_f16x2(hi2).x, 0.f);
+            if (row_ok && cc < ncol) {
+              hh[(size_t)cc * cstride] = (uint16_t)(hi2 & 0xFFFFu);
+              hl[(size_t)cc * cstride] = (uint16_t)(lo2 & 0xFFFFu);
             }
           }
-          named_bar_sync(1, kEpiWarps * 32);
-          // each warp writes 8 token rows of 64 pairs (128 B) per half
-          const int p0 = c.m0 >> 1;
-          for (int cc = ew * 8; cc < ew * 8 + 8; ++cc) {
-            const int col = c0 + cc;
-            if (col < c.nvalid) {
-              const size_t o = (size_t)(pos_base + col) * a.I + p0 + 2 * lane;
-              if (!misaligned((uint64_t)(a.h_hi + o), 4, a.err, 107) &&
-                  !misaligned((uint64_t)(a.h_lo + o), 4, a.err, 107)) {
-                *reinterpret_cast<uint32_t *>(a.h_hi + o) =
-                    *reinterpret_cast<const uint32_t *>(st_hi + cc * 64 + 2 * lane);
-                *reinterpret_cast<uint32_t *>(a.h_lo + o) =
-                    *reinterpret_cast<const uint32_t *>(st_lo + cc * 64 + 2 * lane);
-              }
-            }
-          }
-          named_bar_sync(1, kEpiWarps * 32);
         }
+      };
+      // this warp's chunks start at 32 * half, 64 columns apart (the other
+      // warp of the lane quarter takes the ones in between)
+      const uint32_t tbase = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(buf * BN);
+      for (int c0 = 32 * half; c0 < c.nvalid; c0 += 64) {
+        uint32_t v[32];
+        tmem_ld_32_async(tbase + (uint32_t)c0, v);
+        tmem_wait_ld(v);
+        process(v, c0);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&acc_empty[buf]), 0));
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // the pair's MMAs, loads and remote arrives are all done
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
 // x rows in slot-position order, as f16 x * 2^-sigma (exact for bf16 input
@@ -492,22 +524,46 @@ cudaError_t make_tmap(CUtensorMap *m, const void *base, size_t rows, int cols, i
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int GEMM, int BN>
+template <int GEMM, int STAGES>
 size_t gemm_smem_bytes() {
   constexpr int NB = GEMM == 1 ? 1 : 2;
-  return 1024 + (size_t)kStagesP * (BM * BK * 2 + NB * BN * BK * 2) +
-         (size_t)kCodeStages * kCodeStageBytes + 2 * 32 * 64 * 2;
+  return 1024 + (size_t)STAGES * (BM * BK * 2 + NB * BNH * BK * 2);
 }
 
-template <int GEMM, int BN>
+// Persistent grid of CTA pairs: as many clusters of 2 as fit at once (asked of
+// the occupancy calculator once per device and kernel).
+template <int GEMM, int STAGES>
 cudaError_t launch_gemm(const CUtensorMap &m0, const CUtensorMap &m1, const PrefillArgs &a,
-                        int n_sms, cudaStream_t stream) {
-  const size_t smem = gemm_smem_bytes<GEMM, BN>();
-  auto fn = prefill_gemm_kernel<GEMM, BN>;
+                        cudaStream_t stream) {
+  const size_t smem = gemm_smem_bytes<GEMM, STAGES>();
+  auto fn = prefill_gemm_kernel<GEMM, STAGES>;
   cudaError_t st = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (st != cudaSuccess) return st;
-  fn<<<n_sms, kThreadsP, smem, stream>>>(m0, m1, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreadsP);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int pairs_of_device[64] = {0};
+  int dev = 0;
+  if ((st = cudaGetDevice(&dev)) != cudaSuccess) return st;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (pairs_of_device[dev] == 0) {
+    cfg.gridDim = dim3(2);
+    int n_clusters = 0;
+    st = cudaOccupancyMaxActiveClusters(&n_clusters, fn, &cfg);
+    if (st != cudaSuccess) return st;
+    if (n_clusters < 1) return cudaErrorLaunchOutOfResources;
+    pairs_of_device[dev] = n_clusters;
+  }
+  cfg.gridDim = dim3(2 * pairs_of_device[dev]);
+  return cudaLaunchKernelEx(&cfg, fn, m0, m1, a);
 }
 
 }  // namespace
@@ -535,8 +591,13 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
                                 cudaStream_t stream) {
   if (io.S == 0) return cudaSuccess;
   if (w.H % BK || w.I % BK || w.E > kMaxExpertsP) return cudaErrorInvalidValue;
+  // the converters load 8-byte code words and 2-byte scale pairs, the
+  // epilogue stores 4-byte h pairs
+  if (((uintptr_t)w.w1 & 7) || ((uintptr_t)w.s1 & 3) || ((uintptr_t)io.h_hi & 3) ||
+      ((uintptr_t)io.h_lo & 3))
+    return cudaErrorInvalidValue;
   CUtensorMap m0, m1;
-  cudaError_t st = make_tmap(&m0, io.xp, io.S, w.H, 256);
+  cudaError_t st = make_tmap(&m0, io.xp, io.S, w.H, BNH);
   if (st != cudaSuccess) return st;
   m1 = m0;
   PrefillArgs a{};
@@ -558,17 +619,19 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.limit = w.limit;
   a.H = w.H;
   a.err = io.err;
-  return launch_gemm<1, 256>(m0, m1, a, n_sms, stream);
+  (void)n_sms;
+  return launch_gemm<1, 6>(m0, m1, a, stream);
 }
 
 cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream) {
   if (io.S == 0) return cudaSuccess;
   if (w.H % BK || w.I % BK || w.E > kMaxExpertsP) return cudaErrorInvalidValue;
+  if (((uintptr_t)w.w2 & 7) || ((uintptr_t)w.s2 & 3)) return cudaErrorInvalidValue;
   CUtensorMap m0, m1;
-  cudaError_t st = make_tmap(&m0, io.h_hi, io.S, w.I, 128);
+  cudaError_t st = make_tmap(&m0, io.h_hi, io.S, w.I, BNH);
   if (st != cudaSuccess) return st;
-  st = make_tmap(&m1, io.h_lo, io.S, w.I, 128);
+  st = make_tmap(&m1, io.h_lo, io.S, w.I, BNH);
   if (st != cudaSuccess) return st;
   PrefillArgs a{};
   a.codes = w.w2;
@@ -585,7 +648,8 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.I = w.I;
   a.H = w.H;
   a.err = io.err;
-  return launch_gemm<2, 128>(m0, m1, a, n_sms, stream);
+  (void)n_sms;
+  return launch_gemm<2, 4>(m0, m1, a, stream);
 }
 
 }  // namespace oxg

@@ -28,8 +28,10 @@ struct Layer {
   uint16_t *router_w = nullptr, *router_b = nullptr;
   uint8_t *w1 = nullptr, *s1 = nullptr, *w2 = nullptr, *s2 = nullptr;
   uint16_t *b1 = nullptr, *b2 = nullptr;
-  // Every E8M0 scale is 0 or in [104, 141], so scale * E2M1 is exact in f16
-  // and the tensor-core prefill path applies (H and I multiples of 64 too).
+  // Every E8M0 scale is 0 or in [104, 140], so scale * E2M1 is exact in f16
+  // (0.5 * 2^-23 is the smallest f16 subnormal, 6 * 2^13 = 49152 stays below
+  // the f16 maximum 65504 while 6 * 2^14 would not) and the tensor-core
+  // prefill path applies (H and I multiples of 64 too).
   bool prefill_ok = false;
   unsigned scale_min = 0, scale_max = 0;
 };
@@ -481,7 +483,7 @@ int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void
   if (mode == OXG_MODE_PREFILL && !L->prefill_ok)
     return fail(ctx, OXG_ERR_UNSUPPORTED,
                 "prefill mode needs hidden and intermediate multiples of 64 and E8M0 scales "
-                "0 or in [104, 141]; this layer has scales in [%u, %u]",
+                "0 or in [104, 140]; this layer has scales in [%u, %u]",
                 L->scale_min, L->scale_max);
   if (precision != OXG_PRECISION_PARITY)
     return fail(ctx, OXG_ERR_UNSUPPORTED, "unknown precision %d", precision);
@@ -709,7 +711,7 @@ int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_
     L.scale_min = mm[0];
     L.scale_max = mm[1];
     L.prefill_ok = H % 64 == 0 && I % 64 == 0 &&
-                   (mm[1] == 0u || (mm[0] >= 104u && mm[1] <= 141u));
+                   (mm[1] == 0u || (mm[0] >= 104u && mm[1] <= 140u));
     return cudaSuccess;
   };
   st = body();
