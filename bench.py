@@ -310,7 +310,8 @@ def run_moe(args, ws, rank, local):
     for i in range(args.steps):
         step(i)
     torch.cuda.synchronize()
-    names = ("route_small", "router_topk", "permute", "moe_mlp1_decode", "moe_mlp2_decode", "combine")
+    names = ("route_small", "router_topk", "router_mma", "permute", "scatter", "moe_mlp1_decode",
+             "moe_mlp2_decode", "combine")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     ctx.profile(False)
@@ -414,7 +415,8 @@ def run_prefill(args, ws, rank, local):
     for i in range(args.steps):
         step(i)
     torch.cuda.synchronize()
-    names = ("router_topk", "permute", "gather_f16", "moe_mlp1_prefill", "moe_mlp2_prefill", "combine")
+    names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
+             "moe_mlp2_prefill", "combine")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     ctx.profile(False)

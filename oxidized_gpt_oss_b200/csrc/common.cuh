@@ -107,6 +107,12 @@ __device__ __forceinline__ void cp_async_4(void *smem, const void *gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem)
                : "memory");
 }
+// 16-byte copy reading src_bytes (0 or 16) bytes and zero-filling the rest.
+__device__ __forceinline__ void cp_async_16_zfill(void *smem, const void *gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(src_bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -126,6 +132,23 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
         "f"(c[2]), "f"(c[3]));
 }
 
+// Same shape with bf16 operands.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Four 8x8 b16 matrices from shared memory; lanes 8i..8i+7 give the row
+// addresses of matrix i, register i receives it in the mma fragment layout.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *smem_row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(smem_row)));
+}
+
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -138,6 +161,26 @@ __device__ __forceinline__ float2 unpack_f16x2(uint32_t v) {
       : "=f"(r.x), "=f"(r.y)
       : "r"(v));
   return r;
+}
+
+// One bf16 activation row to f16 x * 2^-sigma (exact within the token's
+// range, see router.cu) by one warp; H a multiple of 8, both rows 16-byte
+// aligned.
+__device__ __forceinline__ void stage_row_f16(const uint16_t *__restrict__ src,
+                                              uint16_t *__restrict__ dst, int H, int sigma,
+                                              int lane) {
+  const float inv = __uint_as_float((uint32_t)(127 - sigma) << 23);
+  const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 v = s4[c];
+    uint4 o;
+    o.x = pack_f16x2(bf16_to_f32(v.x & 0xFFFFu) * inv, bf16_to_f32(v.x >> 16) * inv);
+    o.y = pack_f16x2(bf16_to_f32(v.y & 0xFFFFu) * inv, bf16_to_f32(v.y >> 16) * inv);
+    o.z = pack_f16x2(bf16_to_f32(v.z & 0xFFFFu) * inv, bf16_to_f32(v.z >> 16) * inv);
+    o.w = pack_f16x2(bf16_to_f32(v.w & 0xFFFFu) * inv, bf16_to_f32(v.w >> 16) * inv);
+    d4[c] = o;
+  }
 }
 
 }  // namespace oxg

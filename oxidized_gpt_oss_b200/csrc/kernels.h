@@ -34,12 +34,32 @@ cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint1
                                int E, int k, int32_t *idx, float *wts, float *logits,
                                int32_t *sigma, cudaStream_t stream);
 
+// Batched router on the tensor cores for E a multiple of 16 (<= 64) and H a
+// multiple of 16: the same outputs as launch_router_topk plus, per CTA of
+// router_mma_ctas(T) CTAs, the expert histogram cta_hist[cta, E] and each
+// slot's rank among the CTA's slots of its expert, local_rank[T*k] (slot order).
+bool router_mma_supported(int H, int E, int k);
+int router_mma_ctas(int T);
+cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
+                              int E, int k, int32_t *idx, float *wts, float *logits,
+                              int32_t *sigma, int32_t *cta_hist, int32_t *local_rank,
+                              cudaStream_t stream);
+
 // ---- permutation (permute.cu) -------------------------------------------------
 // Stable counting sort of the T*k (token, j) slots by expert.
 //   counts[E], offsets[E+1], perm[T*k] (position -> slot), slot_pos[T*k]
 //   (slot -> position).
 cudaError_t launch_permute(const int32_t *idx, int n_slots, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
+                           cudaStream_t stream);
+
+// Positions from launch_router_mma's histograms and ranks (same result as
+// launch_permute) and, when xp is not null, the prefill gather: xp[p] = f16
+// x[token of slot perm[p]] * 2^-sigma, pos_scale[p] = 2^sigma.
+cudaError_t launch_scatter(const int32_t *cta_hist, int n_cta, const int32_t *idx,
+                           const int32_t *local_rank, int T, int k, int E, int32_t *counts,
+                           int32_t *offsets, int32_t *perm, int32_t *slot_pos, const uint16_t *x,
+                           const int32_t *sigma, int H, uint16_t *xp, float *pos_scale,
                            cudaStream_t stream);
 
 // ---- fused routing for small batches (route_small.cu) -------------------------

@@ -45,7 +45,17 @@ constexpr int BNH = BN / 2;         // token rows of the tile each CTA loads
 constexpr int BK = 64;              // K per stage (one 128-byte swizzle atom of f16)
 constexpr int kConvWarps = 8;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, alternating 32-column chunks
-constexpr int kThreadsP = (2 + kConvWarps + kEpiWarps) * 32;  // 576
+// Warp layout (warp w runs on sub-partition w % 4): 0 TMA producer, 1 MMA
+// issuer, converters on warps 2-4, 6-8, 10-11 (none beside the MMA issuer, so
+// its tensor-core instructions do not queue behind their shared-memory
+// traffic), 5 and 9 idle, epilogue on 12-19 (two per TMEM lane quarter).
+constexpr int kEpiWarp0 = 12;
+constexpr int kThreadsP = (kEpiWarp0 + kEpiWarps) * 32;  // 640
+__device__ __forceinline__ int converter_index(int warp) {
+  // warps 2, 3, 4, 6, 7, 8, 10, 11 -> 0..7; -1 otherwise
+  return (warp >= 2 && warp < kEpiWarp0 && warp != 5 && warp != 9) ? warp - 2 - (warp > 5) - (warp > 9)
+                                                                   : -1;
+}
 constexpr int kConvThreads = kConvWarps * 32;
 // The converter warps form kGroups groups; group g fills the A tiles of the
 // k-steps it with it % kGroups == g, so each warp pays the per-step waits and
@@ -194,7 +204,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int row0 = a.offsets[a.expert_base + c.e] + c.n0 + (rank ? n_mma / 2 : 0);
         for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
           const int s = it % STAGES, r = it / STAGES;
-          if (r > 0 && !(ok = mbar_wait_cl(&empty_[s], (r - 1) & 1, a.err, 1))) break;
+          if (r > 0) {
+            if (!(ok = mbar_wait_cl(&empty_[s], (r - 1) & 1, a.err, 1))) break;
+            // rank 0's stage is free only once the pair MMAs reading both
+            // CTAs' halves of it are done: pass that on to rank 1
+            if (rank == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&empty_[s]), 1));
+          }
           uint8_t *st = tiles + s * STAGE_BYTES;
           if (misaligned(smem_addr(st + A_BYTES), 1024, a.err, 101) ||
               misaligned((uint64_t)&tm0, 64, a.err, 102)) {
@@ -221,6 +236,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       // later; shared addresses stay below 2^18, so adding to the 14-bit start
       // field of the descriptor never carries into the next field
       const uint64_t desc_a0 = desc_sw128_kmajor(smem_addr(tiles));
+      // one commit per k-step, to rank 0's barrier (rank 0's TMA producer
+      // and epilogue pass the news on to rank 1); stage and phase counters
+      // advance without divisions
+      int s = 0, phase = 0;
+      const uint32_t empty0 = smem_addr(&empty_[0]);
       for (int item = pair; ok && item < total; item += n_pairs, ++j) {
         const Coords c = coords(item);
         const int buf = j & 1, rr = j >> 1;
@@ -230,8 +250,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int n_mma = (c.nvalid + 15) / 16 * 16;
         const uint32_t idesc = idesc_f16_f32(2 * BM, n_mma);
         for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
-          const int s = it % STAGES, r = it / STAGES;
-          if (!(ok = mbar_wait_cl(&full_[s], r & 1, a.err, 2))) break;
+          if (!(ok = mbar_wait_cl(&full_[s], phase, a.err, 2))) break;
           tc_fence_after();
           // descriptors of k16 slice 0; slice kk starts 32 B (2 units) further
           const uint64_t ad = desc_a0 + (uint64_t)(s * (STAGE_BYTES >> 4));
@@ -241,28 +260,26 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
             if (NB == 2) umma_f16_pair(d, ad + 2 * kk, bd + (B_BYTES >> 4) + 2 * kk, idesc, 1);
           }
-          const uint32_t e_own = smem_addr(&empty_[s]);
-          umma_commit_pair(mapa_shared(e_own, 0));
-          umma_commit_pair(mapa_shared(e_own, 1));
+          umma_commit_pair(empty0 + (uint32_t)(s * sizeof(uint64_t)));
+          if (++s == STAGES) {
+            s = 0;
+            phase ^= 1;
+          }
         }
-        if (ok) {
-          const uint32_t f_own = smem_addr(&acc_full[buf]);
-          umma_commit_pair(mapa_shared(f_own, 0));
-          umma_commit_pair(mapa_shared(f_own, 1));
-        }
+        if (ok) umma_commit_pair(smem_addr(&acc_full[buf]));
       }
       // nothing may be left in flight when TMEM is released
       umma_commit_pair(mapa_shared(smem_addr(&mma_done), 0));
       mbar_wait_cl(&mma_done, 0, a.err, 2);
     }
-  } else if (warp < 2 + kConvWarps) {
+  } else if (converter_index(warp) >= 0) {
     // ------------------------------------------------------------ converters
     // Thread gt of group grp owns kTasks (row, q) pairs of each of its weight
     // tiles: row (gt + t * kGroupThreads) / 4, 16-byte chunks q (block 2hf of
     // the k-step pair) and 4 + q (block 2hf + 1). Its codes (8 B: word q of
     // the two blocks, adjacent in the relaid order) and the two scale bytes
     // are loaded into registers kLead of its k-steps before use.
-    const int ct = threadIdx.x - 64;
+    const int ct = converter_index(warp) * 32 + lane;
     const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
     const int q = gt & 3;
     const int full = a.K / 128;  // complete 4-block groups per row
@@ -359,10 +376,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (lane == 0) mbar_arrive_cluster(full_cl(s));
       }
     }
-  } else {
+  } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
     const int lq = warp & 3;            // TMEM lane quarter this warp may access
-    const int ew = warp - (2 + kConvWarps);
+    const int ew = warp - kEpiWarp0;
     const int half = ew >> 2;           // which 32-column chunks: 2m + half
     const int r = lq * 32 + lane;       // accumulator row = weight row within the tile
     const int up_row = lane & 1;
@@ -373,7 +390,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const int eg = a.expert_base + c.e;
       const int pos_base = a.offsets[eg] + c.n0;
       // one thread waits; the four epilogue warps follow its verdict together
-      if (ew == 0 && lane == 0) epi_ok = mbar_wait_cl(&acc_full[buf], rr & 1, a.err, 4);
+      if (ew == 0 && lane == 0) {
+        epi_ok = mbar_wait_cl(&acc_full[buf], rr & 1, a.err, 4);
+        // the MMAs of the item are done in both CTAs' TMEM: tell rank 1
+        if (epi_ok && rank == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&acc_full[buf]), 1));
+      }
       named_bar_sync(1, kEpiWarps * 32);
       const bool ok = epi_ok != 0;
       if (GEMM == 1)  // every warp is past the previous item: refill the column scales

@@ -51,6 +51,7 @@ struct Scratch {
   int32_t *active = nullptr, *n_active = nullptr;
   int32_t *idx = nullptr, *sigma = nullptr, *counts = nullptr, *offsets = nullptr;
   int32_t *perm = nullptr, *slot_pos = nullptr;
+  int32_t *cta_hist = nullptr, *local_rank = nullptr;  // batched router's counting-sort halves
   float *wts = nullptr, *logits = nullptr, *h = nullptr, *y_slot = nullptr;
   uint16_t *x_stage = nullptr;
   float *y_stage = nullptr;
@@ -201,6 +202,7 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
   char *p_xp = take(S * d.hidden * 2), *p_hhi = take(S * d.intermediate * 2);
   char *p_hlo = take(S * d.intermediate * 2), *p_psc = take(S * 4);
+  char *p_hist = take((size_t)oxg::router_mma_ctas(T) * d.n_experts * 4), *p_rank = take(S * 4);
   if (s && base) {
     s->done = (uint32_t *)p_cnt;
     s->err = (int *)(s->done + 1);
@@ -219,6 +221,8 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
     s->offsets = (int32_t *)p_offsets;
     s->perm = (int32_t *)p_perm;
     s->slot_pos = (int32_t *)p_slot;
+    s->cta_hist = (int32_t *)p_hist;
+    s->local_rank = (int32_t *)p_rank;
     s->h = (float *)p_h;
     s->y_slot = (float *)p_y;
     s->x_stage = (uint16_t *)p_xs;
@@ -296,14 +300,62 @@ cudaError_t launch(oxg_ctx *ctx, const char *name, F &&fn) {
   return st;
 }
 
+// Routing of T tokens. Batches beyond the fused small-batch path go to the
+// tensor-core router when the shape allows, which also leaves the first half
+// of the counting sort in the scratch (*ranked = true) for scatter.
 int route(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, int32_t *idx, float *wts,
-          float *logits) {
+          float *logits, bool *ranked = nullptr) {
   const oxg_moe_dims &d = L.dims;
+  const bool mma = T > oxg::kMaxRouteTokens && oxg::router_mma_supported(d.hidden, d.n_experts, d.top_k);
+  if (ranked) *ranked = mma;
+  if (mma) {
+    OXG_CUDA(ctx, launch(ctx, "router_mma", [&] {
+               return oxg::launch_router_mma(x, L.router_w, L.router_b, T, d.hidden, d.n_experts,
+                                             d.top_k, idx, wts, logits, ctx->ws.sigma,
+                                             ctx->ws.cta_hist, ctx->ws.local_rank, ctx->stream);
+             }),
+             "router_mma launch");
+    return OXG_OK;
+  }
   OXG_CUDA(ctx, launch(ctx, "router_topk", [&] {
              return oxg::launch_router_topk(x, L.router_w, L.router_b, T, d.hidden, d.n_experts,
                                             d.top_k, idx, wts, logits, ctx->ws.sigma, ctx->stream);
            }),
            "router_topk launch");
+  return OXG_OK;
+}
+
+// Expert-sorted positions of the T * k slots (and, for prefill, the f16
+// operand rows): from the router's ranks when it left them, else the
+// single-CTA counting sort (and a separate gather).
+int sort_slots(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, bool ranked, bool prefill) {
+  const oxg_moe_dims &d = L.dims;
+  const int S = T * d.top_k;
+  if (ranked) {
+    OXG_CUDA(ctx, launch(ctx, prefill ? "scatter_gather" : "scatter", [&] {
+               return oxg::launch_scatter(ctx->ws.cta_hist, oxg::router_mma_ctas(T), ctx->ws.idx,
+                                          ctx->ws.local_rank, T, d.top_k, d.n_experts,
+                                          ctx->ws.counts, ctx->ws.offsets, ctx->ws.perm,
+                                          ctx->ws.slot_pos, x, ctx->ws.sigma, d.hidden,
+                                          prefill ? ctx->ws.xp : nullptr, ctx->ws.pos_scale,
+                                          ctx->stream);
+             }),
+             "scatter launch");
+    return OXG_OK;
+  }
+  OXG_CUDA(ctx, launch(ctx, "permute", [&] {
+             return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts,
+                                        ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos,
+                                        ctx->stream);
+           }),
+           "permute launch");
+  if (prefill)
+    OXG_CUDA(ctx, launch(ctx, "gather_f16", [&] {
+               return oxg::launch_gather_f16(x, ctx->ws.perm, ctx->ws.sigma, S, d.hidden, d.top_k,
+                                             ctx->ws.xp, ctx->ws.pos_scale, ctx->ws.err,
+                                             ctx->stream);
+             }),
+             "gather launch");
   return OXG_OK;
 }
 
@@ -377,20 +429,10 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
 int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
-  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
+  bool ranked = false;
+  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked);
   if (rc) return rc;
-  OXG_CUDA(ctx, launch(ctx, "permute", [&] {
-             return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts,
-                                        ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos,
-                                        ctx->stream);
-           }),
-           "permute launch");
-  OXG_CUDA(ctx, launch(ctx, "gather_f16", [&] {
-             return oxg::launch_gather_f16(x, ctx->ws.perm, ctx->ws.sigma, S, d.hidden, d.top_k,
-                                           ctx->ws.xp, ctx->ws.pos_scale, ctx->ws.err,
-                                           ctx->stream);
-           }),
-           "gather launch");
+  if ((rc = sort_slots(ctx, L, x, T, ranked, true))) return rc;
   const oxg::MoeDeviceWeights w = device_weights(L);
   oxg::PrefillIO io{};
   io.S = S;
@@ -427,14 +469,10 @@ int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, i
   if (mode == OXG_MODE_PREFILL || (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && L.prefill_ok))
     return forward_prefill(ctx, L, x, T, y);
   if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y);
-  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits);
+  bool ranked = false;
+  int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked);
   if (rc) return rc;
-  OXG_CUDA(ctx, launch(ctx, "permute", [&] {
-             return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts,
-                                        ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos,
-                                        ctx->stream);
-           }),
-           "permute launch");
+  if ((rc = sort_slots(ctx, L, x, T, ranked, false))) return rc;
   const oxg::MoeDeviceWeights w = device_weights(L);
   OXG_CUDA(ctx, launch(ctx, "moe_mlp1_decode", [&] {
              return oxg::launch_moe_mlp1_decode(w, x, ctx->ws.perm, ctx->ws.sigma, ctx->ws.counts,

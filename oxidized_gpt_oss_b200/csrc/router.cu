@@ -28,6 +28,76 @@ constexpr int kRouterThreads = 256;
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 16;
 
+// One warp selects the k largest of E logits (logit_s, shared memory) in the
+// order of a stable descending sort and writes their softmax: each lane owns
+// experts lane, lane+32, ...; a repeated arg-max with ties to the lower index
+// reproduces the stable sort's first k. Optionally also the ids to idx_smem.
+__device__ __forceinline__ void select_topk_softmax(const float *logit_s, int E, int k, int lane,
+                                                    int32_t *__restrict__ idx_out,
+                                                    float *__restrict__ wts_out,
+                                                    int32_t *idx_smem) {
+  constexpr int kPer = kMaxExperts / 32;
+  float v[kPer];
+  bool taken[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? logit_s[e] : -INFINITY;
+    taken[i] = !(e < E);
+  }
+  float top_v[kMaxTopK];
+  int top_e[kMaxTopK];
+  for (int j = 0; j < k; ++j) {
+    float bv = 0.f;
+    int be = 0x7FFFFFFF;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      if (!taken[i] && (be == 0x7FFFFFFF || v[i] > bv)) {
+        bv = v[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
+      const bool other_better =
+          oe != 0x7FFFFFFF && (be == 0x7FFFFFFF || ov > bv || (ov == bv && oe < be));
+      if (other_better) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    top_v[j] = bv;
+    top_e[j] = be;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (lane + 32 * i == be) taken[i] = true;
+  }
+  if (lane == 0) {
+    float mx = -INFINITY;
+    for (int j = 0; j < k; ++j) mx = fmaxf(mx, top_v[j]);
+    float sum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      top_v[j] = expf(top_v[j] - mx);
+      sum += top_v[j];
+    }
+    for (int j = 0; j < k; ++j) {
+      idx_out[j] = top_e[j];
+      wts_out[j] = sum == 0.f ? 1.0f / (float)k : top_v[j] / sum;
+      if (idx_smem) idx_smem[j] = top_e[j];
+    }
+  }
+}
+
+// sigma from the biased exponent of max|x| (as f32 bits >> 23): max|x| <
+// 2^(ex - 126), so max|x| * 2^-sigma < 2^15; clamped to [-110, 100].
+__device__ __forceinline__ int sigma_of(uint32_t ex) {
+  const int sg = (int)ex - 141;
+  return sg < -110 ? -110 : (sg > 100 ? 100 : sg);
+}
+
 __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
     const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, const uint16_t *__restrict__ b,
     int H, int E, int k, int32_t *__restrict__ idx, float *__restrict__ wts,
@@ -77,63 +147,150 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
   __syncthreads();
 
   if (warp == 0) {
-    // Each lane owns experts lane, lane+32, ...; repeated arg-max with ties to
-    // the lower index reproduces the stable descending sort's first k.
-    constexpr int kPer = kMaxExperts / 32;
-    float v[kPer];
-    bool taken[kPer];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int e = lane + 32 * i;
-      v[i] = e < E ? logit_s[e] : -INFINITY;
-      taken[i] = !(e < E);
+    select_topk_softmax(logit_s, E, k, lane, idx + (size_t)t * k, wts + (size_t)t * k, nullptr);
+    if (lane == 0) sigma_out[t] = sigma_of(amax_s >> 23);
+  }
+}
+
+
+// ---- batched router on the tensor cores -------------------------------------
+// CTAs of 64 tokens (4 warps x 16) compute the [64, E] logits with
+// mma.sync.m16n8k16 on bf16 operands (exact products, f32 accumulation),
+// streaming x and W through shared memory in 128-column chunks (cp.async,
+// double-buffered, 16-byte chunks XOR-swizzled by row so the ldmatrix reads
+// are conflict-free). max|x| per token comes from the A fragments. After the
+// bias and the same top-k/softmax as above, warp 0 ranks the CTA's T*k slots
+// per expert in slot order (the counting sort's first half): local_rank of
+// each slot and the CTA's histogram, which scatter_kernel turns into
+// positions.
+constexpr int kRmTokens = 64;
+constexpr int kRmThreads = 128;
+constexpr int kRmKC = 128;  // columns per chunk
+constexpr int kRmMaxE = 64;
+
+__global__ void __launch_bounds__(kRmThreads) router_mma_kernel(
+    const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, const uint16_t *__restrict__ b,
+    int T, int H, int E, int k, int32_t *__restrict__ idx, float *__restrict__ wts,
+    float *__restrict__ logits_out, int32_t *__restrict__ sigma_out,
+    int32_t *__restrict__ cta_hist, int32_t *__restrict__ local_rank) {
+  extern __shared__ __align__(128) uint8_t rm_smem[];
+  __shared__ float logit_s[kRmTokens][kRmMaxE];
+  __shared__ int32_t idx_s[kRmTokens * kMaxTopK];
+  __shared__ int cnt_s[kRmMaxE];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kRmTokens;
+  const int stage_bytes = (kRmTokens + E) * kRmKC * 2;
+  const int n_chunks = (H + kRmKC - 1) / kRmKC;
+
+  auto load_chunk = [&](int c, int buf) {
+    uint8_t *xs = rm_smem + buf * stage_bytes;
+    uint8_t *ws = xs + kRmTokens * kRmKC * 2;
+    const int k0 = c * kRmKC;
+    for (int i = threadIdx.x; i < (kRmTokens + E) * 16; i += kRmThreads) {
+      const int r = i >> 4, ch = i & 15, col = k0 + ch * 8;
+      const bool is_x = r < kRmTokens;
+      const int row = is_x ? r : r - kRmTokens;
+      const bool ok = col < H && (!is_x || t0 + row < T);
+      const uint16_t *src = is_x ? x + (size_t)(ok ? t0 + row : 0) * H + (ok ? col : 0)
+                                 : w + (size_t)row * H + (ok ? col : 0);
+      uint8_t *dst = (is_x ? xs : ws) + row * (kRmKC * 2) + ((ch ^ (row & 7)) << 4);
+      cp_async_16_zfill(dst, src, ok ? 16u : 0u);
     }
-    float top_v[kMaxTopK];
-    int top_e[kMaxTopK];
-    for (int j = 0; j < k; ++j) {
-      float bv = 0.f;
-      int be = 0x7FFFFFFF;
+    cp_async_commit();
+  };
+
+  const int NT = E / 8;  // n-tiles of 8 experts (E is a multiple of 16)
+  float acc[kRmMaxE / 8][4];
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        if (!taken[i] && (be == 0x7FFFFFFF || v[i] > bv)) {
-          bv = v[i];
-          be = e;
+  for (int j = 0; j < kRmMaxE / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  uint32_t amax_lo = 0u, amax_hi = 0u;  // |x| bf16 bits of rows g and g + 8, two per register
+  const int mi = lane >> 3, ri = lane & 7;
+
+  load_chunk(0, 0);
+  for (int c = 0; c < n_chunks; ++c) {
+    if (c + 1 < n_chunks)
+      load_chunk(c + 1, (c + 1) & 1);
+    else
+      cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint8_t *xs = rm_smem + (c & 1) * stage_bytes;
+    const uint8_t *ws = xs + kRmTokens * kRmKC * 2;
+#pragma unroll
+    for (int kk = 0; kk < kRmKC / 16; ++kk) {
+      const int arow = warp * 16 + ri + 8 * (mi & 1), ach = 2 * kk + (mi >> 1);
+      uint32_t a[4];
+      ldmatrix_x4(a, xs + arow * (kRmKC * 2) + ((ach ^ (arow & 7)) << 4));
+      amax_lo = __vmaxu2(amax_lo, __vmaxu2(a[0] & 0x7FFF7FFFu, a[2] & 0x7FFF7FFFu));
+      amax_hi = __vmaxu2(amax_hi, __vmaxu2(a[1] & 0x7FFF7FFFu, a[3] & 0x7FFF7FFFu));
+#pragma unroll
+      for (int j = 0; j < kRmMaxE / 8; j += 2) {
+        if (j < NT) {
+          const int brow = 8 * (j + (mi >> 1)) + ri, bch = 2 * kk + (mi & 1);
+          uint32_t bq[4];
+          ldmatrix_x4(bq, ws + brow * (kRmKC * 2) + ((bch ^ (brow & 7)) << 4));
+          mma_bf16_16816(acc[j], a, bq[0], bq[1]);
+          mma_bf16_16816(acc[j + 1], a, bq[2], bq[3]);
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-        int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-        const bool other_better =
-            oe != 0x7FFFFFFF && (be == 0x7FFFFFFF || ov > bv || (ov == bv && oe < be));
-        if (other_better) {
-          bv = ov;
-          be = oe;
-        }
-      }
-      top_v[j] = bv;
-      top_e[j] = be;
-#pragma unroll
-      for (int i = 0; i < kPer; ++i)
-        if (lane + 32 * i == be) taken[i] = true;
     }
-    if (lane == 0) {
-      float mx = -INFINITY;
-      for (int j = 0; j < k; ++j) mx = fmaxf(mx, top_v[j]);
-      float sum = 0.f;
-      for (int j = 0; j < k; ++j) {
-        top_v[j] = expf(top_v[j] - mx);
-        sum += top_v[j];
-      }
-      for (int j = 0; j < k; ++j) {
-        idx[(size_t)t * k + j] = top_e[j];
-        wts[(size_t)t * k + j] = sum == 0.f ? 1.0f / (float)k : top_v[j] / sum;
-      }
-      const int ex = (int)(amax_s >> 23);  // max|x| < 2^(ex - 126)
-      const int sg = ex - 141;             // max|x| * 2^-sg < 2^15
-      sigma_out[t] = sg < -110 ? -110 : (sg > 100 ? 100 : sg);
+    __syncthreads();  // the buffer is refilled by the next iteration's load
+  }
+
+  // logits (+ bias) of rows g and g + 8 of this warp, experts 8j + 2q + {0, 1}
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int j = 0; j < kRmMaxE / 8; ++j) {
+    if (j < NT) {
+      const int e0 = 8 * j + 2 * q;
+      const float b0 = b ? bf16_to_f32(b[e0]) : 0.f, b1 = b ? bf16_to_f32(b[e0 + 1]) : 0.f;
+      logit_s[warp * 16 + g][e0] = acc[j][0] + b0;
+      logit_s[warp * 16 + g][e0 + 1] = acc[j][1] + b1;
+      logit_s[warp * 16 + g + 8][e0] = acc[j][2] + b0;
+      logit_s[warp * 16 + g + 8][e0 + 1] = acc[j][3] + b1;
     }
+  }
+  // max|x| of the rows: halves of the packed maxima, then over the quad
+  uint32_t mlo = max(amax_lo & 0xFFFFu, amax_lo >> 16), mhi = max(amax_hi & 0xFFFFu, amax_hi >> 16);
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    mlo = max(mlo, __shfl_xor_sync(0xFFFFFFFFu, mlo, o));
+    mhi = max(mhi, __shfl_xor_sync(0xFFFFFFFFu, mhi, o));
+  }
+  if (q == 0) {
+    const int ta = t0 + warp * 16 + g, tb = ta + 8;
+    if (ta < T) sigma_out[ta] = sigma_of(mlo >> 7);  // bf16 bits >> 7 = f32 exponent
+    if (tb < T) sigma_out[tb] = sigma_of(mhi >> 7);
+  }
+  __syncthreads();
+  const int n_tok = min(kRmTokens, T - t0);
+  if (logits_out)
+    for (int i = threadIdx.x; i < n_tok * E; i += kRmThreads)
+      logits_out[(size_t)t0 * E + i] = logit_s[i / E][i % E];
+  for (int tl = warp; tl < n_tok; tl += kRmThreads / 32) {
+    const size_t t = (size_t)t0 + tl;
+    select_topk_softmax(logit_s[tl], E, k, lane, idx + t * k, wts + t * k, idx_s + tl * k);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int e = lane; e < E; e += 32) cnt_s[e] = 0;
+    __syncwarp();
+    const int n_slots = n_tok * k;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int s0 = 0; s0 < n_slots; s0 += 32) {
+      const int sl = s0 + lane;
+      const bool valid = sl < n_slots;
+      const int e = valid ? idx_s[sl] : E + lane;  // distinct dummies never match
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+      const int prior = valid ? cnt_s[e] : 0;
+      __syncwarp();
+      if (valid) {
+        local_rank[(size_t)t0 * k + sl] = prior + __popc(peers & lt_mask);
+        if ((peers & lt_mask) == 0u) cnt_s[e] = prior + __popc(peers);
+      }
+      __syncwarp();
+    }
+    for (int e = lane; e < E; e += 32) cta_hist[(size_t)blockIdx.x * E + e] = cnt_s[e];
   }
 }
 
@@ -151,6 +308,28 @@ cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint1
   if (st != cudaSuccess) return st;
   router_topk_kernel<<<T, kRouterThreads, smem, stream>>>(x, w, b, H, E, k, idx, wts, logits,
                                                           sigma);
+  return cudaGetLastError();
+}
+
+bool router_mma_supported(int H, int E, int k) {
+  return E % 16 == 0 && E <= kRmMaxE && k <= kMaxTopK && k <= E && H % 16 == 0;
+}
+
+int router_mma_ctas(int T) { return (T + kRmTokens - 1) / kRmTokens; }
+
+cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
+                              int E, int k, int32_t *idx, float *wts, float *logits,
+                              int32_t *sigma, int32_t *cta_hist, int32_t *local_rank,
+                              cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  if (!router_mma_supported(H, E, k)) return cudaErrorInvalidValue;
+  if ((uintptr_t)x & 15 || (uintptr_t)w & 15) return cudaErrorInvalidValue;
+  const size_t smem = 2 * (size_t)(kRmTokens + E) * kRmKC * 2;
+  cudaError_t st = cudaFuncSetAttribute(router_mma_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (st != cudaSuccess) return st;
+  router_mma_kernel<<<router_mma_ctas(T), kRmThreads, smem, stream>>>(
+      x, w, b, T, H, E, k, idx, wts, logits, sigma, cta_hist, local_rank);
   return cudaGetLastError();
 }
 

@@ -77,6 +77,8 @@ def test_small_golden_fixture(cuda_ctx):
     (2880, 2880, 32, 4, 3),
     (256, 224, 16, 4, 40),  # experts with > 8 tokens: several token passes
     (128, 96, 8, 4, 80),    # beyond the fused-routing batch size: separate router/permute/combine
+    (256, 224, 16, 4, 200),  # tensor-core router + scatter, decode kernels (I % 64 != 0)
+    (512, 512, 32, 4, 300),  # tensor-core router + scatter/gather, prefill kernels; ragged last CTA
 ])
 def test_shapes(cuda_ctx, H, I, E, K, T):
     d = synth.moe_layer(seed=H + I + T, hidden=H, intermediate=I, n_experts=E, top_k=K)
