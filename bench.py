@@ -2,26 +2,30 @@
 """Benchmark of the MXFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_decode|moe_prefill|dequant] [--tokens T]
+                    [--workload moe_prefill|moe_decode|dequant] [--tokens T] [--layers L]
 
 Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
+  moe_prefill (default) 8192 tokens per GPU through one MoE block on the
+              tcgen05 grouped-GEMM path (router logits ~N(0, 1), so expert
+              loads are roughly uniform). Metric: tokens/s; roofline: TFLOP/s
+              of the gate/up GEMM against the measured dense 16-bit tensor
+              peak. On N GPUs the experts are split 32/N per GPU (expert
+              parallel) with NCCL all-to-all dispatch and return; on one GPU
+              the line also carries a "decode" object (the moe_decode
+              workload measured in the same process).
   moe_decode  one MoE block forward over T tokens (default 8: the 8-token
               gpt-oss-20b block — hidden 2880, 32 experts top-4, MXFP4
               weights with E8M0 scales in [118, 126], bf16 activations).
-              Steps cycle over 4 uploaded layers (4 x 424 MB of packed
-              weights), so inputs are larger than L2 and no step finds the
-              previous step's weights cached. Metric: tokens/s.
-  moe_prefill 8192 tokens per GPU through one MoE block on the tcgen05
-              grouped-GEMM path (router logits ~N(0, 1), so expert loads are
-              roughly uniform). Metric: tokens/s; roofline: TFLOP/s of the
-              gate/up GEMM against the measured dense 16-bit tensor peak.
+              Metric: tokens/s; roofline: HBM GB/s of the gate/up kernel.
+              N > 1: independent replicas.
   dequant     standalone MXFP4 -> bf16 dequant of one layer's expert tensors
               (32x5760x2880 + 32x2880x2880, E8M0 in [110, 135]). Metric: GB/s
               of algorithmic traffic (423,014,400 B read + 1,592,524,800 B written).
 
-N > 1 runs one process per GPU (torchrun); every rank processes its own
-tokens through its own copy of the layer (replicas: no data-path collective),
-timing is max over ranks and ``value`` is the whole-job aggregate.
+Steps cycle over L uploaded layers (default 4 x 424 MB of packed weights), so
+inputs are larger than L2 and no step finds the previous step's weights
+cached. N > 1 runs one process per GPU (torchrun); timing is max over ranks
+and ``value`` is the whole-job aggregate.
 
 ``--impl reference`` times the reference's own CPU algorithm for the same
 workload (the oracle's REF-FAITHFUL restatement: f16 buffers, per-call
@@ -368,9 +372,11 @@ def run_moe(args, ws, rank, local):
 
 def run_prefill(args, ws, rank, local):
     """8192 tokens per GPU through one gpt-oss-20b MoE layer on the tcgen05
-    grouped-GEMM path (router logits ~N(0, 1): x ~N(0, 1), W_router ~N(0, 0.02))."""
+    grouped-GEMM path (router logits ~N(0, 1): x ~N(0, 1), W_router ~N(0, 0.02)).
+    On N GPUs the 32 experts are split 32/N per GPU (expert parallel): every
+    rank routes its own 8192 tokens and the rows travel by NCCL all-to-all."""
     import torch
-    from oxidized_gpt_oss_b200 import abi, synth
+    from oxidized_gpt_oss_b200 import abi, ep, synth
     from oxidized_gpt_oss_b200.moe import MoELayer
     from oxidized_gpt_oss_b200.mxfp4 import context
 
@@ -379,17 +385,26 @@ def run_prefill(args, ws, rank, local):
     d0 = synth.moe_layer(seed=0)
     H, I, E, K = d0["hidden"], d0["intermediate"], d0["n_experts"], d0["top_k"]
     ctx = context(None)
-    layers = [MoELayer(d, ctx=ctx, layer=i) for i, d in enumerate(gpu_layers(args, d0, device))]
+    shard = ep.shard_range(E, ws, rank) if ws > 1 else None
+    layers = [MoELayer(d, ctx=ctx, layer=i, experts=shard) for i, d in enumerate(gpu_layers(args, d0, device))]
     for L in layers:
         L.reserve(T)
+    eps = [ep.ExpertParallelMoE(L) for L in layers] if ws > 1 else None
     n_x = 2
     xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
     xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
     y = torch.empty((T, H), dtype=torch.float32, device=device)
     mode = abi.OXG_MODE_PREFILL
+    rows_done = [0]  # expert rows this rank computed (varies with the routing under EP)
 
     def step(i):
-        layers[i % len(layers)].forward(xs[i % n_x], out=y, mode=mode)
+        if eps is None:
+            rows_done[0] += T * K
+            return layers[i % len(layers)].forward(xs[i % n_x], out=y, mode=mode)
+        m = eps[i % len(eps)]
+        out = m.forward(xs[i % n_x])
+        rows_done[0] += sum(m.last_splits[1])
+        return out
 
     for i in range(args.warmup):
         step(i)
@@ -412,9 +427,11 @@ def run_prefill(args, ws, rank, local):
     ctx.sync()
     ctx.profile(True)
     ctx.profile_reset()
+    rows_done[0] = 0
     for i in range(args.steps):
         step(i)
     torch.cuda.synchronize()
+    rows_profiled = rows_done[0]
     names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
              "moe_mlp2_prefill", "combine")
     k_ms = {n: ctx.profile_read(n) for n in names}
@@ -422,25 +439,41 @@ def run_prefill(args, ws, rank, local):
     ctx.profile(False)
     ms_max = max_over_ranks(ms, ws)
 
-    S = T * K
-    flop1 = 2.0 * S * (2 * I) * H          # GEMM1 algorithmic FLOPs per step
-    flop2 = 2.0 * S * H * I                # GEMM2 (the f16 hi/lo split executes it twice)
+    # algorithmic FLOPs per expert row: GEMM1 2 * 2I * H, GEMM2 2 * H * I
+    # (the f16 hi/lo split executes GEMM2 twice); rows = T*k per step on one
+    # GPU, the rows this rank received under EP
+    f1_row, f2_row = 2.0 * (2 * I) * H, 2.0 * H * I
+    rows_per_step = rows_profiled / args.steps
+    flop1, flop2 = f1_row * rows_per_step, f2_row * rows_per_step
     peak, peak_kind = tensor_peak()
     m1_ms, m1_n = k_ms["moe_mlp1_prefill"]
     m2_ms, m2_n = k_ms["moe_mlp2_prefill"]
-    achieved = flop1 * m1_n / (m1_ms * 1e-3) / 1e12
+    achieved = f1_row * rows_profiled / (m1_ms * 1e-3) / 1e12
     layer_tflops = (flop1 + flop2) * args.steps / (ms * 1e-3) / 1e12
 
-    # end to end through the host-buffer API
+    # end to end: host x (pinned) in, host y (pinned) out, every step
     xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
     yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    if eps is None:
+        def e2e_step(i):
+            layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
+    else:
+        x_dev = torch.empty((T, H), dtype=torch.int16, device=device)
+
+        def e2e_step(i):
+            x_dev.copy_(xh[i % n_x], non_blocking=True)
+            yh.copy_(step_out(i, x_dev), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        def step_out(i, x):
+            return eps[i % len(eps)].forward(x)
     for i in range(min(args.warmup, 2)):
-        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
+        e2e_step(i)
     barrier(ws)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(args.steps):
-        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
+        e2e_step(i)
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, ws)
 
     out = {"metric": METRIC, "value": T * ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
@@ -453,11 +486,13 @@ def run_prefill(args, ws, rank, local):
                       "layers_cycled": args.layers,
                       "l2": "inputs larger than L2 (424 MB of packed weights and 189 MB of slot "
                             "activations per step)",
-                      "parallelism": "replicas" if ws > 1 else "single"},
+                      "parallelism": f"ep{ws} (experts 32/{ws} per GPU, NCCL all-to-all)" if ws > 1 else "single",
+                      "expert_rows_per_step_rank0": rows_per_step},
            "roofline": {"bound": "tensor", "kernel": "moe_mlp1_prefill", "achieved": achieved, "peak": peak,
                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
-                        "traffic": ncu_traffic("moe_mlp1_prefill", f"T{T}"),
+                        "traffic": ncu_traffic("moe_mlp1_prefill", f"T{T}") if ws == 1 else None,
                         "algorithmic_flop_per_launch": flop1,
+                        "flop_per_unit": f1_row, "unit_of_work": "expert row (token, slot)",
                         "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3},
            "layer": {"tflops": layer_tflops, "frac": layer_tflops / peak,
                      "kernel_us_per_step": {n: v[0] / max(v[1], 1) * 1e3 for n, v in k_ms.items()},
@@ -566,7 +601,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant"], default="moe_decode")
+    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant"], default="moe_prefill")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="moe_prefill on one GPU: skip the decode measurement added to the line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
@@ -587,6 +624,13 @@ def main():
     try:
         run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe}[args.workload]
         out = run(args, ws, rank, local)
+        if args.workload == "moe_prefill" and ws == 1 and not args.no_decode:
+            # the metric's decode half (tokens/s and HBM GB/s at 8 tokens), same process
+            dargs = argparse.Namespace(**vars(args))
+            dargs.tokens, dargs.steps, dargs.warmup = 8, max(args.steps, 20), max(args.warmup, 5)
+            dec = run_moe(dargs, ws, rank, local)
+            out["decode"] = {k: dec[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline", "e2e",
+                                                  "config", "cpu_baseline") if k in dec}
         if rank == 0:
             emit(out)
     finally:

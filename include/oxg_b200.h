@@ -153,6 +153,53 @@ OXG_API int oxg_moe_route(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_
  * E ints). Waits for the context's stream. */
 OXG_API int oxg_moe_last_counts(oxg_ctx *ctx, int32_t *counts_host, int n_experts);
 
+/* ---- Expert parallelism ------------------------------------------------------
+ * No counterpart in the reference, which runs every expert of a layer in one
+ * process (MoELayer::forward, src/moe.rs:76-97). With N processes, one per
+ * GPU, each holding a contiguous range of a layer's experts:
+ *   1. oxg_moe_dispatch routes the process's own tokens and writes their
+ *      n_tokens * k slot rows expert-major (so also destination-process-major)
+ *      into caller buffers, with the per-expert row counts;
+ *   2. the caller exchanges the rows (an all-to-all) so that every process
+ *      receives, source process by source process, the rows of its own
+ *      experts in expert order;
+ *   3. oxg_moe_experts runs the resident experts' MLPs over the received rows;
+ *   4. the caller returns the output rows to their sources (the reverse
+ *      all-to-all), which then lie in the order step 1 wrote;
+ *   5. oxg_moe_combine forms y = sum_j w_j * row(t, j), as oxg_moe_forward does.
+ * Rows are the prefill operand: f16 x * 2^-sigma (hidden halves per row) with a
+ * per-row f32 2^sigma; all four calls need a layer the prefill kernels accept
+ * (hidden and intermediate multiples of 64, E8M0 scales 0 or in [104, 140]). */
+
+/* Uploads the router (all n_experts rows) and experts [expert_begin,
+ * expert_begin + expert_count) of the given weights, whose arrays hold every
+ * expert (oxg_moe_weights layout). oxg_moe_forward refuses such a layer
+ * unless the range is all experts. */
+OXG_API int oxg_moe_upload_shard(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims,
+                                 const oxg_moe_weights *weights, int expert_begin,
+                                 int expert_count);
+
+/* rows_dev [n_tokens*k, hidden] f16 and row_scale_dev [n_tokens*k] f32 (both
+ * device, 16- and 4-byte aligned), expert_counts_dev [n_experts] int32. The
+ * positions and routing weights stay on the context for oxg_moe_combine until
+ * the next dispatch or forward on it. */
+OXG_API int oxg_moe_dispatch(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_tokens,
+                             uint16_t *rows_dev, float *row_scale_dev, int32_t *expert_counts_dev);
+
+/* rows_dev/row_scale_dev: the received rows, seg_counts_host [n_src *
+ * expert_count] (host) the number from source s for resident expert e at
+ * s * expert_count + e, in row order. Writes y_rows_dev [sum, hidden] f32
+ * (16-byte aligned): each row's expert output with bias, before the routing
+ * weight. n_src * expert_count must not exceed 256. */
+OXG_API int oxg_moe_experts(oxg_ctx *ctx, int layer, const uint16_t *rows_dev,
+                            const float *row_scale_dev, int n_src, const int32_t *seg_counts_host,
+                            float *y_rows_dev);
+
+/* y_rows_dev [n_tokens*k, hidden] f32 in the order oxg_moe_dispatch wrote
+ * rows_dev; y_dev [n_tokens, hidden] f32. n_tokens must be the dispatch's. */
+OXG_API int oxg_moe_combine(oxg_ctx *ctx, int layer, const float *y_rows_dev, int n_tokens,
+                            float *y_dev);
+
 /* Has no counterpart in the reference. The same layer forward as
  * oxg_moe_forward (same kernels, same results), for callers that must not
  * have the library allocate device memory during a forward: serving runtimes

@@ -74,6 +74,10 @@ SIGNATURES = {
     "oxg_moe_route": (_I, [_CTX, _I, _P, _I, _P, _P, _P]),
     "oxg_moe_last_counts": (_I, [_CTX, _P, _I]),
     "oxg_moe_forward_noalloc": (_I, [_CTX, _I, _P, _I, _P]),
+    "oxg_moe_upload_shard": (_I, [_CTX, _I, ctypes.POINTER(MoeDims), ctypes.POINTER(MoeWeights), _I, _I]),
+    "oxg_moe_dispatch": (_I, [_CTX, _I, _P, _I, _P, _P, _P]),
+    "oxg_moe_experts": (_I, [_CTX, _I, _P, _P, _I, _P, _P]),
+    "oxg_moe_combine": (_I, [_CTX, _I, _P, _I, _P]),
     "oxg_profile_enable": (_I, [_CTX, _I]),
     "oxg_profile_read": (_I, [_CTX, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_int)]),

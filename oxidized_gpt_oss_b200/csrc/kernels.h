@@ -139,8 +139,11 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
 // Buffers of one prefill pass over S expert-sorted slots.
 struct PrefillIO {
   int S;
-  const int32_t *counts, *offsets;  // per expert (global ids)
-  int expert_base, n_local_experts;
+  // The S slot rows are n_segments runs (counts[v] rows from offsets[v]); run v
+  // is multiplied by the layer's local expert v % weight_mod. One GPU: the
+  // runs are the experts. Expert parallel: (source rank, local expert) pairs.
+  const int32_t *counts, *offsets;
+  int n_segments, weight_mod;
   const uint16_t *xp;               // [S, H] f16 x * 2^-sigma in slot order (gather)
   const float *pos_scale;           // [S] 2^sigma of each slot's token
   uint16_t *h_hi, *h_lo;            // [S, I] f16 SwiGLU output, hi + lo
@@ -154,8 +157,8 @@ cudaError_t launch_scale_range(const uint8_t *scales, size_t n, unsigned *minmax
 cudaError_t launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *sigma, int S,
                               int H, int topk, uint16_t *xp, float *pos_scale, int *err,
                               cudaStream_t stream);
-// tcgen05 grouped GEMMs (persistent grid of n_sms CTAs). Need H and I
-// multiples of 64 and every E8M0 scale 0 or in [104, 140].
+// tcgen05 grouped GEMMs (persistent grid of CTA pairs). Need H and I
+// multiples of 64, every E8M0 scale 0 or in [104, 140] and n_segments <= 256.
 cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream);
 cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,

@@ -72,7 +72,8 @@ struct PrefillArgs {
   const uint16_t *bias;   // [E, rows]
   int K, rows, kb_pad;
   const int32_t *counts, *offsets;
-  int n_experts, expert_base;
+  int n_segments;  // runs of slot rows sharing one expert (counts/offsets index)
+  int weight_mod;  // segment v multiplies by the layer's local expert v % weight_mod
   // GEMM1 epilogue
   const float *pos_scale;  // [S] 2^sigma of the token in each slot position
   uint16_t *h_hi, *h_lo;   // [S, I] f16
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const int E = a.n_experts;
+  const int E = a.n_segments;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       // both CTAs' converter groups + rank 0's expect_tx arrival
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     int run = 0;
     for (int e = 0; e < E; ++e) {
       ntile_prefix[e] = run;
-      run += (a.counts[a.expert_base + e] + BN - 1) / BN;
+      run += (a.counts[e] + BN - 1) / BN;
     }
     ntile_prefix[E] = run;
   }
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     while (e + 1 < E && ntile_prefix[e + 1] <= ntg) ++e;
     c.e = e;
     c.n0 = (ntg - ntile_prefix[e]) * BN;
-    c.nvalid = min(BN, a.counts[a.expert_base + e] - c.n0);
+    c.nvalid = min(BN, a.counts[e] - c.n0);
     return c;
   };
   // rank 0's full barriers as seen from either CTA
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       for (int item = pair; ok && item < total; item += n_pairs) {
         const Coords c = coords(item);
         const int n_mma = (c.nvalid + 15) / 16 * 16;
-        const int row0 = a.offsets[a.expert_base + c.e] + c.n0 + (rank ? n_mma / 2 : 0);
+        const int row0 = a.offsets[c.e] + c.n0 + (rank ? n_mma / 2 : 0);
         for (int ks = 0; ks < KSTEPS; ++ks, ++it) {
           const int s = it % STAGES, r = it / STAGES;
           if (r > 0) {
@@ -293,7 +294,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     auto set_rows = [&](int item) {
       const Coords c = coords(item);
       const int R0 = c.m0 + (int)rank * BM + (gt >> 2);
-      const size_t erow = (size_t)(a.expert_base + c.e) * a.rows + R0;
+      const size_t erow = (size_t)(c.e % a.weight_mod) * a.rows + R0;
       crow = a.codes + erow * row_bytes;
       srow = a.scales + erow * a.kb_pad;
       n_rows_ok = R0 < a.rows ? min(kTasks, (a.rows - R0 + kGroupThreads / 4 - 1) / (kGroupThreads / 4)) : 0;
@@ -387,8 +388,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     for (int item = pair; item < total; item += n_pairs, ++j) {
       const Coords c = coords(item);
       const int buf = j & 1, rr = j >> 1;
-      const int eg = a.expert_base + c.e;
-      const int pos_base = a.offsets[eg] + c.n0;
+      const int eg = c.e % a.weight_mod;
+      const int pos_base = a.offsets[c.e] + c.n0;
       // one thread waits; the four epilogue warps follow its verdict together
       if (ew == 0 && lane == 0) {
         epi_ok = mbar_wait_cl(&acc_full[buf], rr & 1, a.err, 4);
@@ -611,7 +612,9 @@ cudaError_t launch_gather_f16(const uint16_t *x, const int32_t *perm, const int3
 cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream) {
   if (io.S == 0) return cudaSuccess;
-  if (w.H % BK || w.I % BK || w.E > kMaxExpertsP) return cudaErrorInvalidValue;
+  if (w.H % BK || w.I % BK || io.n_segments > kMaxExpertsP || io.n_segments < 1 ||
+      io.weight_mod < 1)
+    return cudaErrorInvalidValue;
   // the converters load 8-byte code words and 2-byte scale pairs, the
   // epilogue stores 4-byte h pairs
   if (((uintptr_t)w.w1 & 7) || ((uintptr_t)w.s1 & 3) || ((uintptr_t)io.h_hi & 3) ||
@@ -630,8 +633,8 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.kb_pad = (w.H / 32 + 3) / 4 * 4;
   a.counts = io.counts;
   a.offsets = io.offsets;
-  a.n_experts = io.n_local_experts;
-  a.expert_base = io.expert_base;
+  a.n_segments = io.n_segments;
+  a.weight_mod = io.weight_mod;
   a.pos_scale = io.pos_scale;
   a.h_hi = io.h_hi;
   a.h_lo = io.h_lo;
@@ -647,7 +650,9 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
 cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream) {
   if (io.S == 0) return cudaSuccess;
-  if (w.H % BK || w.I % BK || w.E > kMaxExpertsP) return cudaErrorInvalidValue;
+  if (w.H % BK || w.I % BK || io.n_segments > kMaxExpertsP || io.n_segments < 1 ||
+      io.weight_mod < 1)
+    return cudaErrorInvalidValue;
   if (((uintptr_t)w.w2 & 7) || ((uintptr_t)w.s2 & 3)) return cudaErrorInvalidValue;
   CUtensorMap m0, m1;
   cudaError_t st = make_tmap(&m0, io.h_hi, io.S, w.I, BNH);
@@ -663,8 +668,8 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.kb_pad = (w.I / 32 + 3) / 4 * 4;
   a.counts = io.counts;
   a.offsets = io.offsets;
-  a.n_experts = io.n_local_experts;
-  a.expert_base = io.expert_base;
+  a.n_segments = io.n_segments;
+  a.weight_mod = io.weight_mod;
   a.y_slot = io.y_slot;
   a.I = w.I;
   a.H = w.H;

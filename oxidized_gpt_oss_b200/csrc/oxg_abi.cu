@@ -34,6 +34,10 @@ struct Layer {
   // prefill path applies (H and I multiples of 64 too).
   bool prefill_ok = false;
   unsigned scale_min = 0, scale_max = 0;
+  // experts [expert_begin, expert_begin + expert_count) are resident (all of
+  // them unless uploaded with oxg_moe_upload_shard); the router is complete
+  int expert_begin = 0, expert_count = 0;
+  bool sharded() const { return expert_count != dims.n_experts; }
 };
 
 // Completion counters at the start of the scratch: zeroed when the scratch is
@@ -120,10 +124,21 @@ struct oxg_ctx {
   std::vector<Layer> layers;
   Scratch ws;
   int last_layer = -1;
+  int ep_tokens = -1;  // tokens of the last oxg_moe_dispatch (its positions feed oxg_moe_combine)
   int n_sms = 148;
   long long launches = 0;
   bool prefill_pending = false;  // a prefill ran since the error word was last read
   Profiler prof;
+  // Expert-parallel receive side (oxg_moe_experts): kept apart from ws so
+  // that sizing it for the received rows never discards the dispatch's
+  // slot positions and weights that oxg_moe_combine reads.
+  struct {
+    void *base = nullptr;
+    size_t bytes = 0;
+    uint16_t *h_hi = nullptr, *h_lo = nullptr;
+    int32_t *seg = nullptr;  // counts [256] then offsets [257]
+  } ep;
+  std::vector<int32_t> seg_host;
 };
 
 namespace {
@@ -328,17 +343,19 @@ int route(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, int32_t *idx, float 
 // Expert-sorted positions of the T * k slots (and, for prefill, the f16
 // operand rows): from the router's ranks when it left them, else the
 // single-CTA counting sort (and a separate gather).
-int sort_slots(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, bool ranked, bool prefill) {
+int sort_slots(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, bool ranked, bool prefill,
+               uint16_t *xp = nullptr, float *pos_scale = nullptr) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
+  if (!xp) xp = ctx->ws.xp;
+  if (!pos_scale) pos_scale = ctx->ws.pos_scale;
   if (ranked) {
     OXG_CUDA(ctx, launch(ctx, prefill ? "scatter_gather" : "scatter", [&] {
                return oxg::launch_scatter(ctx->ws.cta_hist, oxg::router_mma_ctas(T), ctx->ws.idx,
                                           ctx->ws.local_rank, T, d.top_k, d.n_experts,
                                           ctx->ws.counts, ctx->ws.offsets, ctx->ws.perm,
                                           ctx->ws.slot_pos, x, ctx->ws.sigma, d.hidden,
-                                          prefill ? ctx->ws.xp : nullptr, ctx->ws.pos_scale,
-                                          ctx->stream);
+                                          prefill ? xp : nullptr, pos_scale, ctx->stream);
              }),
              "scatter launch");
     return OXG_OK;
@@ -352,8 +369,7 @@ int sort_slots(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, bool ranked, bo
   if (prefill)
     OXG_CUDA(ctx, launch(ctx, "gather_f16", [&] {
                return oxg::launch_gather_f16(x, ctx->ws.perm, ctx->ws.sigma, S, d.hidden, d.top_k,
-                                             ctx->ws.xp, ctx->ws.pos_scale, ctx->ws.err,
-                                             ctx->stream);
+                                             xp, pos_scale, ctx->ws.err, ctx->stream);
              }),
              "gather launch");
   return OXG_OK;
@@ -438,8 +454,8 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) 
   io.S = S;
   io.counts = ctx->ws.counts;
   io.offsets = ctx->ws.offsets;
-  io.expert_base = 0;
-  io.n_local_experts = d.n_experts;
+  io.n_segments = d.n_experts;
+  io.weight_mod = d.n_experts;
   io.xp = ctx->ws.xp;
   io.pos_scale = ctx->ws.pos_scale;
   io.h_hi = ctx->ws.h_hi;
@@ -514,6 +530,11 @@ int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
   Layer *L = get_layer(ctx, layer);
   if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  if (L->sharded())
+    return fail(ctx, OXG_ERR_STATE,
+                "layer %d holds experts [%d, %d) only: use oxg_moe_dispatch / oxg_moe_experts / "
+                "oxg_moe_combine",
+                layer, L->expert_begin, L->expert_begin + L->expert_count);
   if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
   if (T > 0 && (!x || !y)) return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be non-NULL");
   if (mode != OXG_MODE_AUTO && mode != OXG_MODE_DECODE && mode != OXG_MODE_PREFILL)
@@ -605,6 +626,7 @@ int oxg_ctx_destroy(oxg_ctx *ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   for (Layer &L : ctx->layers) free_layer(L);
   if (ctx->ws.base) cudaFree(ctx->ws.base);
+  if (ctx->ep.base) cudaFree(ctx->ep.base);
   ctx->prof.destroy();
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -676,19 +698,25 @@ int oxg_swiglu(oxg_ctx *ctx, const float *gate, const float *up, size_t n, float
   return OXG_OK;
 }
 
-int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe_weights *w) {
+namespace {
+int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe_weights *w,
+                int eb, int ec) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
   if (layer < 0 || layer > 4096) return fail(ctx, OXG_ERR_INVALID_ARG, "layer %d out of range", layer);
   int rc = check_dims(ctx, dims);
   if (rc) return rc;
+  if (eb < 0 || ec < 1 || eb + ec > dims->n_experts)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "expert range [%d, %d) is not inside [0, %d)", eb, eb + ec,
+                dims->n_experts);
   if (!w || !w->router_w || !w->w1_blocks || !w->w1_scales || !w->b1 || !w->w2_blocks ||
       !w->w2_scales || !w->b2)
     return fail(ctx, OXG_ERR_INVALID_ARG, "all weight pointers except router_b must be non-NULL");
   DeviceGuard g(ctx->device);
   const oxg_moe_dims d = *dims;
-  const size_t E = d.n_experts, H = d.hidden, I = d.intermediate;
+  // E: resident experts (the router below always has all d.n_experts rows)
+  const size_t E = ec, H = d.hidden, I = d.intermediate, ER = d.n_experts;
   const size_t kb1 = (H / 32 + 3) / 4 * 4, kb2 = (I / 32 + 3) / 4 * 4;
-  const size_t n_rw = E * H * 2, n_rb = E * 2;
+  const size_t n_rw = ER * H * 2, n_rb = ER * 2;
   const size_t n_w1 = E * 2 * I * (H / 2), n_s1 = E * 2 * I * kb1, n_b1 = E * 2 * I * 2;
   const size_t n_w2 = E * H * (I / 2), n_s2 = E * H * kb2, n_b2 = E * H * 2;
   size_t off = 0;
@@ -714,6 +742,8 @@ int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_
   }
   char *base = (char *)block;
   L.block = block;
+  L.expert_begin = eb;
+  L.expert_count = ec;
   L.router_w = (uint16_t *)(base + o_rw);
   L.router_b = w->router_b ? (uint16_t *)(base + o_rb) : nullptr;
   L.w1 = (uint8_t *)(base + o_w1);
@@ -723,20 +753,27 @@ int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_
   L.s2 = (uint8_t *)(base + o_s2);
   L.b2 = (uint16_t *)(base + o_b2);
   cudaStream_t s = ctx->stream;
+  // the shard's slices of the caller's arrays (all experts, expert-major)
+  const uint8_t *w1_src = (const uint8_t *)w->w1_blocks + (size_t)eb * 2 * I * (H / 2);
+  const uint8_t *s1_src = (const uint8_t *)w->w1_scales + (size_t)eb * 2 * I * (H / 32);
+  const uint16_t *b1_src = w->b1 + (size_t)eb * 2 * I;
+  const uint8_t *w2_src = (const uint8_t *)w->w2_blocks + (size_t)eb * H * (I / 2);
+  const uint8_t *s2_src = (const uint8_t *)w->w2_scales + (size_t)eb * H * (I / 32);
+  const uint16_t *b2_src = w->b2 + (size_t)eb * H;
   auto body = [&]() -> cudaError_t {
     cudaError_t e;
     if ((e = cudaMemcpyAsync(L.router_w, w->router_w, n_rw, cudaMemcpyDefault, s))) return e;
     if (w->router_b && (e = cudaMemcpyAsync(L.router_b, w->router_b, n_rb, cudaMemcpyDefault, s)))
       return e;
-    if ((e = cudaMemcpyAsync(L.b1, w->b1, n_b1, cudaMemcpyDefault, s))) return e;
-    if ((e = cudaMemcpyAsync(L.b2, w->b2, n_b2, cudaMemcpyDefault, s))) return e;
-    if ((e = cudaMemcpyAsync(stage, w->w1_blocks, n_w1, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(L.b1, b1_src, n_b1, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(L.b2, b2_src, n_b2, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w1_src, n_w1, cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w1, E * 2 * I, (int)H, s))) return e;
-    if ((e = cudaMemcpyAsync(stage, w->w1_scales, E * 2 * I * (H / 32), cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, s1_src, E * 2 * I * (H / 32), cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s1, E * 2 * I, (int)H, s))) return e;
-    if ((e = cudaMemcpyAsync(stage, w->w2_blocks, n_w2, cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, w2_src, n_w2, cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w2, E * H, (int)I, s))) return e;
-    if ((e = cudaMemcpyAsync(stage, w->w2_scales, E * H * (I / 32), cudaMemcpyDefault, s))) return e;
+    if ((e = cudaMemcpyAsync(stage, s2_src, E * H * (I / 32), cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s2, E * H, (int)I, s))) return e;
     // scale range over both matrices (padding bytes are zero and ignored)
     const unsigned init[2] = {255u, 0u};
@@ -761,6 +798,18 @@ int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_
   L.present = true;
   ctx->layers[layer] = L;
   return OXG_OK;
+}
+}  // namespace
+
+int oxg_moe_upload(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe_weights *w) {
+  if (!dims) return fail(ctx, OXG_ERR_INVALID_ARG, "dims is NULL");
+  return upload_impl(ctx, layer, dims, w, 0, dims->n_experts);
+}
+
+int oxg_moe_upload_shard(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims,
+                         const oxg_moe_weights *w, int expert_begin, int expert_count) {
+  if (!dims) return fail(ctx, OXG_ERR_INVALID_ARG, "dims is NULL");
+  return upload_impl(ctx, layer, dims, w, expert_begin, expert_count);
 }
 
 int oxg_moe_release(oxg_ctx *ctx, int layer) {
@@ -794,6 +843,7 @@ int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y,
   rc = ensure_scratch(ctx, L->dims, T);
   if (rc) return rc;
   ctx->last_layer = layer;
+  ctx->ep_tokens = -1;
   return forward_device(ctx, *L, x, T, y, mode);
 }
 
@@ -807,6 +857,7 @@ int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T,
   rc = ensure_scratch(ctx, L->dims, T);
   if (rc) return rc;
   ctx->last_layer = layer;
+  ctx->ep_tokens = -1;
   const size_t H = L->dims.hidden;
   OXG_CUDA(ctx, cudaMemcpyAsync(ctx->ws.x_stage, x_host, (size_t)T * H * 2, cudaMemcpyDefault, ctx->stream),
            "copy x to device");
@@ -844,6 +895,166 @@ int oxg_moe_last_counts(oxg_ctx *ctx, int32_t *counts_host, int n_experts) {
   OXG_CUDA(ctx, cudaMemcpyAsync(counts_host, ctx->ws.counts, (size_t)n_experts * 4, cudaMemcpyDefault, ctx->stream),
            "copy counts");
   OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return OXG_OK;
+}
+
+// ---- expert parallelism -------------------------------------------------------
+namespace {
+
+int check_ep_layer(oxg_ctx *ctx, int layer, Layer **out) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return fail(ctx, OXG_ERR_STATE, "layer %d has not been uploaded", layer);
+  if (!L->prefill_ok)
+    return fail(ctx, OXG_ERR_UNSUPPORTED,
+                "expert-parallel rows use the prefill kernels: hidden and intermediate must be "
+                "multiples of 64 and E8M0 scales 0 or in [104, 140]; this layer has scales in "
+                "[%u, %u]",
+                L->scale_min, L->scale_max);
+  *out = L;
+  return OXG_OK;
+}
+
+// Receive-side scratch for R rows: SwiGLU output hi/lo and the segment table.
+int ensure_ep_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, size_t R) {
+  const size_t hb = align_up(R * (size_t)d.intermediate * 2, 256);
+  const size_t need = 2 * hb + align_up((256 + 257) * 4, 256);
+  if (need > ctx->ep.bytes) {
+    if (ctx->ep.base) {
+      OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+      cudaFree(ctx->ep.base);
+      ctx->ep.base = nullptr;
+      ctx->ep.bytes = 0;
+    }
+    void *p = nullptr;
+    OXG_CUDA(ctx, cudaMalloc(&p, need), "cudaMalloc(expert-parallel scratch)");
+    ctx->ep.base = p;
+    ctx->ep.bytes = need;
+  }
+  char *b = (char *)ctx->ep.base;
+  ctx->ep.h_hi = (uint16_t *)b;
+  ctx->ep.h_lo = (uint16_t *)(b + hb);
+  ctx->ep.seg = (int32_t *)(b + 2 * hb);
+  return OXG_OK;
+}
+
+}  // namespace
+
+int oxg_moe_dispatch(oxg_ctx *ctx, int layer, const uint16_t *x, int T, uint16_t *rows,
+                     float *row_scale, int32_t *expert_counts) {
+  Layer *L = nullptr;
+  int rc = check_ep_layer(ctx, layer, &L);
+  if (rc) return rc;
+  if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
+  if (!expert_counts) return fail(ctx, OXG_ERR_INVALID_ARG, "expert_counts must be non-NULL");
+  if (T > 0 && (!x || !rows || !row_scale))
+    return fail(ctx, OXG_ERR_INVALID_ARG, "x, rows and row_scale must be non-NULL");
+  if (((uintptr_t)x & 15) || ((uintptr_t)rows & 15) || ((uintptr_t)row_scale & 3))
+    return fail(ctx, OXG_ERR_INVALID_ARG, "x and rows must be 16-byte aligned, row_scale 4-byte");
+  DeviceGuard g(ctx->device);
+  const oxg_moe_dims &d = L->dims;
+  if (T == 0) {
+    OXG_CUDA(ctx, cudaMemsetAsync(expert_counts, 0, (size_t)d.n_experts * 4, ctx->stream),
+             "cudaMemsetAsync(expert_counts)");
+    return OXG_OK;
+  }
+  if ((rc = ensure_scratch(ctx, d, T))) return rc;
+  bool ranked = false;
+  if ((rc = route(ctx, *L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked))) return rc;
+  if ((rc = sort_slots(ctx, *L, x, T, ranked, true, rows, row_scale))) return rc;
+  OXG_CUDA(ctx, cudaMemcpyAsync(expert_counts, ctx->ws.counts, (size_t)d.n_experts * 4,
+                                cudaMemcpyDeviceToDevice, ctx->stream),
+           "copy expert counts");
+  ctx->last_layer = layer;
+  ctx->ep_tokens = T;  // forward calls reset it: they reuse the same scratch
+  return OXG_OK;
+}
+
+int oxg_moe_experts(oxg_ctx *ctx, int layer, const uint16_t *rows, const float *row_scale,
+                    int n_src, const int32_t *seg_counts, float *y_rows) {
+  Layer *L = nullptr;
+  int rc = check_ep_layer(ctx, layer, &L);
+  if (rc) return rc;
+  const int ec = L->expert_count;
+  if (n_src < 1 || (long long)n_src * ec > 256)
+    return fail(ctx, OXG_ERR_INVALID_ARG,
+                "n_src * resident experts must be in [1, 256], got %d * %d", n_src, ec);
+  if (!seg_counts) return fail(ctx, OXG_ERR_INVALID_ARG, "seg_counts must be non-NULL");
+  long long R = 0;
+  for (int v = 0; v < n_src * ec; ++v) {
+    if (seg_counts[v] < 0)
+      return fail(ctx, OXG_ERR_INVALID_ARG, "seg_counts[%d] = %d is negative", v, seg_counts[v]);
+    R += seg_counts[v];
+  }
+  if (R > (1LL << 30)) return fail(ctx, OXG_ERR_SHAPE, "%lld rows is too many", R);
+  if (R == 0) return OXG_OK;
+  if (!rows || !row_scale || !y_rows)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "rows, row_scale and y_rows must be non-NULL");
+  if (((uintptr_t)rows & 15) || ((uintptr_t)row_scale & 3) || ((uintptr_t)y_rows & 15))
+    return fail(ctx, OXG_ERR_INVALID_ARG,
+                "rows and y_rows must be 16-byte aligned, row_scale 4-byte");
+  DeviceGuard g(ctx->device);
+  const oxg_moe_dims &d = L->dims;
+  if (!ctx->ws.base && (rc = ensure_scratch(ctx, d, 1))) return rc;  // error word
+  if ((rc = ensure_ep_scratch(ctx, d, (size_t)R))) return rc;
+  // segment table: (source rank, resident expert) runs in row order
+  const int nv = n_src * ec;
+  ctx->seg_host.assign(256 + 257, 0);
+  int run = 0;
+  for (int v = 0; v < nv; ++v) {
+    ctx->seg_host[v] = seg_counts[v];
+    ctx->seg_host[256 + v] = run;
+    run += seg_counts[v];
+  }
+  ctx->seg_host[256 + nv] = run;
+  // from pageable memory: the call returns once the table is staged, so the
+  // host vector may be rewritten by the next call
+  OXG_CUDA(ctx, cudaMemcpyAsync(ctx->ep.seg, ctx->seg_host.data(), (256 + 257) * 4,
+                                cudaMemcpyHostToDevice, ctx->stream),
+           "copy segment table");
+  const oxg::MoeDeviceWeights w = device_weights(*L);
+  oxg::PrefillIO io{};
+  io.S = (int)R;
+  io.counts = ctx->ep.seg;
+  io.offsets = ctx->ep.seg + 256;
+  io.n_segments = nv;
+  io.weight_mod = ec;
+  io.xp = rows;
+  io.pos_scale = row_scale;
+  io.h_hi = ctx->ep.h_hi;
+  io.h_lo = ctx->ep.h_lo;
+  io.y_slot = y_rows;
+  io.err = ctx->ws.err;
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp1_prefill", [&] {
+             return oxg::launch_prefill_mlp1(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp1 launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp2_prefill", [&] {
+             return oxg::launch_prefill_mlp2(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp2 launch");
+  ctx->prefill_pending = true;
+  return OXG_OK;
+}
+
+int oxg_moe_combine(oxg_ctx *ctx, int layer, const float *y_rows, int T, float *y) {
+  Layer *L = nullptr;
+  int rc = check_ep_layer(ctx, layer, &L);
+  if (rc) return rc;
+  if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
+  if (T == 0) return OXG_OK;
+  if (!y_rows || !y) return fail(ctx, OXG_ERR_INVALID_ARG, "y_rows and y must be non-NULL");
+  if (ctx->last_layer != layer || !ctx->ws.base || ctx->ep_tokens != T)
+    return fail(ctx, OXG_ERR_STATE,
+                "oxg_moe_combine needs the dispatch of the same %d tokens of layer %d first", T,
+                layer);
+  DeviceGuard g(ctx->device);
+  const oxg_moe_dims &d = L->dims;
+  OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+             return oxg::launch_combine(y_rows, ctx->ws.slot_pos, ctx->ws.wts, T, d.hidden,
+                                        d.top_k, y, ctx->stream);
+           }),
+           "combine launch");
   return OXG_OK;
 }
 

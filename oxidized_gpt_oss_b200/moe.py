@@ -41,7 +41,10 @@ class MoELayer:
 
     _next_layer = 0
 
-    def __init__(self, weights: dict, *, ctx: abi.Context | None = None, layer: int | None = None):
+    def __init__(self, weights: dict, *, ctx: abi.Context | None = None, layer: int | None = None,
+                 experts: tuple[int, int] | None = None):
+        """experts: (begin, count) to keep only that range of experts resident
+        (expert parallelism: ``dispatch`` / ``experts`` / ``combine``)."""
         self.ctx = context(ctx)
         if layer is None:
             layer = MoELayer._next_layer
@@ -51,6 +54,7 @@ class MoELayer:
         self.intermediate = int(weights["intermediate"])
         self.n_experts = int(weights["n_experts"])
         self.top_k = int(weights["top_k"])
+        self.expert_begin, self.expert_count = experts if experts is not None else (0, self.n_experts)
         dims = abi.MoeDims(self.hidden, self.intermediate, self.n_experts, self.top_k,
                            float(weights["alpha"]), float(weights["limit"]))
         keep = {}
@@ -62,8 +66,13 @@ class MoELayer:
                 v = v.contiguous()
             keep[k] = v
         w = abi.MoeWeights(*[_ptr(keep[k]) for k in _WEIGHT_KEYS])
-        abi.check(self.ctx.lib.oxg_moe_upload(self.ctx.handle, self.layer, ctypes.byref(dims), ctypes.byref(w)),
-                  self.ctx.handle)
+        if experts is None:
+            abi.check(self.ctx.lib.oxg_moe_upload(self.ctx.handle, self.layer, ctypes.byref(dims), ctypes.byref(w)),
+                      self.ctx.handle)
+        else:
+            abi.check(self.ctx.lib.oxg_moe_upload_shard(self.ctx.handle, self.layer, ctypes.byref(dims),
+                                                        ctypes.byref(w), int(experts[0]), int(experts[1])),
+                      self.ctx.handle)
 
     def reserve(self, n_tokens: int) -> None:
         abi.check(self.ctx.lib.oxg_moe_reserve(self.ctx.handle, self.layer, int(n_tokens)), self.ctx.handle)
@@ -113,6 +122,45 @@ class MoELayer:
         abi.check(self.ctx.lib.oxg_moe_last_counts(self.ctx.handle, counts.ctypes.data, self.n_experts),
                   self.ctx.handle)
         return counts
+
+    # ---- expert parallelism (see include/oxg_b200.h) --------------------------
+    def dispatch(self, hidden: torch.Tensor):
+        """Routes ``hidden`` [T, H] and lays its T*k slot rows out expert-major:
+        (rows [T*k, H] f16, row_scale [T*k] f32, counts [E] int32),
+        all on the device."""
+        x = hidden.contiguous()
+        T = x.shape[0]
+        S = T * self.top_k
+        rows = torch.empty((S, self.hidden), dtype=torch.float16, device=x.device)
+        scale = torch.empty((S,), dtype=torch.float32, device=x.device)
+        counts = torch.empty((self.n_experts,), dtype=torch.int32, device=x.device)
+        c = context(self.ctx)
+        abi.check(c.lib.oxg_moe_dispatch(c.handle, self.layer, x.data_ptr(), T, rows.data_ptr(),
+                                         scale.data_ptr(), counts.data_ptr()), c.handle)
+        return rows, scale, counts
+
+    def experts(self, rows: torch.Tensor, row_scale: torch.Tensor, seg_counts) -> torch.Tensor:
+        """Resident experts over received rows; seg_counts [n_src, expert_count]
+        (host) rows per (source, resident expert) in row order. -> [R, H] f32."""
+        seg = np.ascontiguousarray(np.asarray(seg_counts, dtype=np.int32).reshape(-1, self.expert_count))
+        R = int(seg.sum())
+        if R != rows.shape[0]:
+            raise ValueError(f"seg_counts sum to {R} rows, rows has {rows.shape[0]}")
+        y = torch.empty((R, self.hidden), dtype=torch.float32, device=rows.device)
+        c = context(self.ctx)
+        abi.check(c.lib.oxg_moe_experts(c.handle, self.layer, rows.data_ptr() if R else None,
+                                        row_scale.data_ptr() if R else None, seg.shape[0], seg.ctypes.data,
+                                        y.data_ptr() if R else None), c.handle)
+        return y
+
+    def combine(self, y_rows: torch.Tensor, n_tokens: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Weighted top-k combine of the rows returned in dispatch order -> [T, H] f32."""
+        if out is None:
+            out = torch.empty((n_tokens, self.hidden), dtype=torch.float32, device=y_rows.device)
+        c = context(self.ctx)
+        abi.check(c.lib.oxg_moe_combine(c.handle, self.layer, y_rows.data_ptr(), int(n_tokens), out.data_ptr()),
+                  c.handle)
+        return out
 
     def release(self) -> None:
         abi.check(self.ctx.lib.oxg_moe_release(self.ctx.handle, self.layer), self.ctx.handle)

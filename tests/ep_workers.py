@@ -1,0 +1,127 @@
+"""Worker processes for the expert-parallel tests (spawned, one per rank).
+
+The CPU tests run the orchestrator over gloo with ``NumpyShard`` — the layer
+computed in float64 numpy from the oracle's restatement — standing in for the
+CUDA shard, so the collective plumbing (counts, splits, row exchange, return,
+combine order) is checked without a GPU. The GPU worker runs the real shard
+over NCCL and compares with the single-GPU forward."""
+import datetime
+import os
+import pickle
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from oracle import oracle
+from oxidized_gpt_oss_b200 import ep, synth
+
+
+class NumpyShard:
+    """dispatch / experts / combine of one expert range, in float64."""
+
+    def __init__(self, d, begin, count):
+        self.d = d
+        self.n_experts, self.top_k, self.hidden = d["n_experts"], d["top_k"], d["hidden"]
+        self.expert_begin, self.expert_count = begin, count
+
+    def dispatch(self, hidden):
+        d, K = self.d, self.top_k
+        x = oracle.np_bf16_to_f32(hidden.numpy().view(np.uint16)).astype(np.float64)
+        logits = x @ oracle.np_bf16_to_f32(d["router_w"]).astype(np.float64).T
+        if d.get("router_b") is not None:
+            logits = logits + oracle.np_bf16_to_f32(d["router_b"]).astype(np.float64)
+        idx = np.argsort(-logits, axis=1, kind="stable")[:, :K]
+        top = np.take_along_axis(logits, idx, axis=1)
+        ex = np.exp(top - top.max(axis=1, keepdims=True))
+        self.wts = ex / ex.sum(axis=1, keepdims=True)
+        self.idx = idx
+        flat = idx.reshape(-1)
+        order = np.argsort(flat, kind="stable")
+        self.pos = np.empty_like(order)
+        self.pos[order] = np.arange(order.size)
+        rows = torch.from_numpy(np.ascontiguousarray(x[order // K]))
+        scale = torch.ones(order.size, dtype=torch.float64)
+        counts = torch.from_numpy(np.bincount(flat, minlength=self.n_experts).astype(np.int32))
+        return rows, scale, counts
+
+    def _expert(self, e, xr):
+        d = self.d
+        w1 = oracle.np_dequant_f32(d["w1_blocks"][e], d["w1_scales"][e]).astype(np.float64)
+        w2 = oracle.np_dequant_f32(d["w2_blocks"][e], d["w2_scales"][e]).astype(np.float64)
+        b1 = oracle.np_bf16_to_f32(d["b1"][e]).astype(np.float64)
+        b2 = oracle.np_bf16_to_f32(d["b2"][e]).astype(np.float64)
+        h1 = xr @ w1.T + b1
+        g = np.minimum(h1[:, 0::2], d["limit"])
+        u = np.clip(h1[:, 1::2], -d["limit"], d["limit"])
+        h = g / (1.0 + np.exp(-d["alpha"] * g)) * (u + 1.0)
+        return h @ w2.T + b2
+
+    def experts(self, rows, scale, seg):
+        x = rows.numpy() * scale.numpy()[:, None]
+        out = np.zeros((x.shape[0], self.hidden))
+        r = 0
+        for s in range(seg.shape[0]):
+            for el in range(self.expert_count):
+                n = int(seg[s, el])
+                if n:
+                    out[r:r + n] = self._expert(self.expert_begin + el, x[r:r + n])
+                r += n
+        return torch.from_numpy(out)
+
+    def combine(self, y_rows, T):
+        y = y_rows.numpy()
+        K = self.top_k
+        out = np.zeros((T, self.hidden))
+        for j in range(K):
+            out += self.wts[:, j:j + 1] * y[self.pos[np.arange(T) * K + j]]
+        return torch.from_numpy(out)
+
+
+def _init(rank, world, port, backend):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group(backend, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+
+
+def cpu_worker(rank, world, port, layer_kw, tokens, out_dir, bias_rank0):
+    _init(rank, world, port, "gloo")
+    try:
+        d = synth.moe_layer(**layer_kw)
+        if bias_rank0:  # every slot to rank 0's experts: empty splits elsewhere
+            b = np.zeros(d["n_experts"], np.float32)
+            b[: d["n_experts"] // world] = 50.0
+            d["router_b"] = synth.f32_to_bf16_bits(b)
+        begin, count = ep.shard_range(d["n_experts"], world, rank)
+        moe = ep.ExpertParallelMoE(NumpyShard(d, begin, count))
+        x = synth.activations(100 + rank, tokens[rank], d["hidden"])
+        y = moe(torch.from_numpy(x.view(np.int16))).numpy()
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump({"x": x, "y": y, "splits": moe.last_splits}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def gpu_worker(rank, world, port, layer_kw, tokens, out_dir):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    try:
+        from oxidized_gpt_oss_b200.moe import MoELayer
+        d = synth.moe_layer(**layer_kw)
+        begin, count = ep.shard_range(d["n_experts"], world, rank)
+        shard = MoELayer(d, experts=(begin, count))
+        full = MoELayer(d)
+        moe = ep.ExpertParallelMoE(shard)
+        x = torch.from_numpy(synth.activations(100 + rank, tokens[rank], d["hidden"]).view(np.int16)).cuda()
+        y_ep = moe(x).clone()
+        y_full = full.forward(x).clone()
+        torch.cuda.synchronize()
+        dist.barrier()
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump({"equal": bool(torch.equal(y_ep, y_full)),
+                         "max_diff": float((y_ep - y_full).abs().max()) if y_ep.numel() else 0.0,
+                         "splits": moe.last_splits}, f)
+    finally:
+        dist.destroy_process_group()
