@@ -389,7 +389,12 @@ def run_prefill(args, ws, rank, local):
     layers = [MoELayer(d, ctx=ctx, layer=i, experts=shard) for i, d in enumerate(gpu_layers(args, d0, device))]
     for L in layers:
         L.reserve(T)
-    eps = [ep.ExpertParallelMoE(L) for L in layers] if ws > 1 else None
+    p2p = None
+    eps = None
+    if ws > 1 and args.ep == "p2p":
+        p2p = ep.PeerExpertParallelMoE(layers[0], max_tokens=T)
+    elif ws > 1:
+        eps = [ep.ExpertParallelMoE(L) for L in layers]
     n_x = 2
     xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
     xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
@@ -397,12 +402,20 @@ def run_prefill(args, ws, rank, local):
     mode = abi.OXG_MODE_PREFILL
     rows_done = [0]  # expert rows this rank computed (varies with the routing under EP)
 
-    def step(i):
+    count_rows = [False]  # in the profiled pass: ask each step how many rows it received
+
+    def step(i, x=None):
+        x = xs[i % n_x] if x is None else x
+        if p2p is not None:
+            out = p2p.forward(x, out=y, shard=layers[i % len(layers)])
+            if count_rows[0]:
+                rows_done[0] += p2p.last_received()
+            return out
         if eps is None:
             rows_done[0] += T * K
-            return layers[i % len(layers)].forward(xs[i % n_x], out=y, mode=mode)
+            return layers[i % len(layers)].forward(x, out=y, mode=mode)
         m = eps[i % len(eps)]
-        out = m.forward(xs[i % n_x])
+        out = m.forward(x)
         rows_done[0] += sum(m.last_splits[1])
         return out
 
@@ -428,9 +441,11 @@ def run_prefill(args, ws, rank, local):
     ctx.profile(True)
     ctx.profile_reset()
     rows_done[0] = 0
+    count_rows[0] = True
     for i in range(args.steps):
         step(i)
     torch.cuda.synchronize()
+    count_rows[0] = False
     rows_profiled = rows_done[0]
     names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
              "moe_mlp2_prefill", "combine")
@@ -454,7 +469,7 @@ def run_prefill(args, ws, rank, local):
     # end to end: host x (pinned) in, host y (pinned) out, every step
     xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
     yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    if eps is None:
+    if ws == 1:
         def e2e_step(i):
             layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
     else:
@@ -462,11 +477,8 @@ def run_prefill(args, ws, rank, local):
 
         def e2e_step(i):
             x_dev.copy_(xh[i % n_x], non_blocking=True)
-            yh.copy_(step_out(i, x_dev), non_blocking=True)
+            yh.copy_(step(i, x_dev), non_blocking=True)
             torch.cuda.current_stream().synchronize()
-
-        def step_out(i, x):
-            return eps[i % len(eps)].forward(x)
     for i in range(min(args.warmup, 2)):
         e2e_step(i)
     barrier(ws)
@@ -486,7 +498,10 @@ def run_prefill(args, ws, rank, local):
                       "layers_cycled": args.layers,
                       "l2": "inputs larger than L2 (424 MB of packed weights and 189 MB of slot "
                             "activations per step)",
-                      "parallelism": f"ep{ws} (experts 32/{ws} per GPU, NCCL all-to-all)" if ws > 1 else "single",
+                      "parallelism": (f"ep{ws} (experts 32/{ws} per GPU; " +
+                                      ("rows and output rows stored over NVLink peer memory by the "
+                                       "library's kernels)" if p2p is not None else "NCCL all-to-all)"))
+                                     if ws > 1 else "single",
                       "expert_rows_per_step_rank0": rows_per_step},
            "roofline": {"bound": "tensor", "kernel": "moe_mlp1_prefill", "achieved": achieved, "peak": peak,
                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -501,6 +516,8 @@ def run_prefill(args, ws, rank, local):
                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
            "gpu_launches": launches,
            "clocks": clk.summary()}
+    if p2p is not None:
+        p2p.close()
     if rank == 0 and ws == 1:
         from oracle import oracle
         n_cpu = 2
@@ -607,6 +624,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
+                    help="moe_prefill on N > 1 GPUs: exchange over peer memory in the library's kernels "
+                         "(default) or by NCCL all-to-all")
     args = ap.parse_args()
     if args.tokens is None:
         args.tokens = 8192 if args.workload == "moe_prefill" else 8

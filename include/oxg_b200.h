@@ -200,6 +200,31 @@ OXG_API int oxg_moe_experts(oxg_ctx *ctx, int layer, const uint16_t *rows_dev,
 OXG_API int oxg_moe_combine(oxg_ctx *ctx, int layer, const float *y_rows_dev, int n_tokens,
                             float *y_dev);
 
+/* The same exchange done by the library's own kernels over NVLink peer memory
+ * (no host round trip per forward): every process allocates one buffer
+ * (oxg_ep_init, which writes its 64-byte CUDA IPC handle to handle_out), the
+ * processes exchange the handles, and each maps the others' (oxg_ep_connect,
+ * handles: world x 64 bytes in rank order). oxg_moe_forward_ep then takes a
+ * process's own n_tokens (<= max_tokens) to y_dev [n_tokens, hidden] f32:
+ * rows are stored straight into the owner's receive buffer, output rows
+ * straight back into the source's, and per-forward counts and completion
+ * flags travel the same way; every wait is bounded and a failure on one
+ * process is reported by all (oxg_sync returns it). All processes must call
+ * oxg_moe_forward_ep the same number of times (n_tokens may be 0). The layer
+ * must hold experts [rank * E / world, (rank + 1) * E / world); E a multiple
+ * of 16 and of world, at most 64; world at most 8. max_recv_rows caps the rows
+ * one process can receive per forward (<= 0: world * max_tokens * k, the
+ * worst case). Call oxg_ep_close on every process after all of them have
+ * finished their last forward. */
+OXG_API int oxg_ep_init(oxg_ctx *ctx, int layer, int rank, int world, int max_tokens,
+                        long long max_recv_rows, void *handle_out);
+OXG_API int oxg_ep_connect(oxg_ctx *ctx, const void *handles);
+OXG_API int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_tokens,
+                               float *y_dev);
+OXG_API int oxg_ep_close(oxg_ctx *ctx);
+/* Rows this process received in its last oxg_moe_forward_ep (waits for it). */
+OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
+
 /* Has no counterpart in the reference. The same layer forward as
  * oxg_moe_forward (same kernels, same results), for callers that must not
  * have the library allocate device memory during a forward: serving runtimes

@@ -78,6 +78,11 @@ SIGNATURES = {
     "oxg_moe_dispatch": (_I, [_CTX, _I, _P, _I, _P, _P, _P]),
     "oxg_moe_experts": (_I, [_CTX, _I, _P, _P, _I, _P, _P]),
     "oxg_moe_combine": (_I, [_CTX, _I, _P, _I, _P]),
+    "oxg_ep_init": (_I, [_CTX, _I, _I, _I, _I, ctypes.c_longlong, _P]),
+    "oxg_ep_connect": (_I, [_CTX, _P]),
+    "oxg_moe_forward_ep": (_I, [_CTX, _I, _P, _I, _P]),
+    "oxg_ep_close": (_I, [_CTX]),
+    "oxg_ep_last_received": (_I, [_CTX, ctypes.POINTER(ctypes.c_longlong)]),
     "oxg_profile_enable": (_I, [_CTX, _I]),
     "oxg_profile_read": (_I, [_CTX, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_int)]),

@@ -148,6 +148,7 @@ struct PrefillIO {
   const float *pos_scale;           // [S] 2^sigma of each slot's token
   uint16_t *h_hi, *h_lo;            // [S, I] f16 SwiGLU output, hi + lo
   float *y_slot;                    // [S, H] f32 expert outputs
+  float *const *y_seg;              // or per segment: its rows' destination (null: y_slot)
   int *err;                         // pipeline timeout code (0 = none)
 };
 // min over non-zero and max of E8M0 scale bytes into minmax[0..1] (which
@@ -163,6 +164,40 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
                                 cudaStream_t stream);
 cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, int n_sms,
                                 cudaStream_t stream);
+
+// ---- expert-parallel exchange over peer memory (ep_p2p.cu) ---------------------
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpMaxExperts = 64;
+constexpr int kEpMaxSegments = 256;
+// One rank's symmetric buffer (the same layout on every rank): flags
+// [3][kEpMaxRanks] u32 (counts / rows / returns, indexed by the rank that
+// raised them), counts inbox [kEpMaxRanks][kEpMaxExperts] i32, receive scales
+// [max_recv] f32, receive rows [max_recv, H] f16, return rows
+// [max_tokens * k, H] f32.
+struct EpLayout {
+  int W, E, H, k, rank, per;
+  long long max_tokens, max_recv;
+  size_t off_flags, off_inbox, off_recv_scale, off_recv_rows, off_ret_rows, bytes;
+};
+struct EpPeers {
+  char *base[kEpMaxRanks];  // every rank's symmetric buffer as mapped here ([rank]: own)
+};
+EpLayout ep_layout(int W, int E, int H, int k, int rank, long long max_tokens, long long max_recv);
+cudaError_t launch_ep_counts(const EpLayout &L, const EpPeers &P, const int32_t *cta_hist, int n_cta,
+                             int32_t *counts, int32_t *offsets, int *ok_word, uint32_t epoch,
+                             cudaStream_t stream);
+// kind 0: counts, 2: returns (rows are awaited by launch_ep_segments)
+cudaError_t launch_ep_wait(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch, int *err,
+                           int code, int *ok_word, cudaStream_t stream);
+cudaError_t launch_ep_scatter(const EpLayout &L, const EpPeers &P, const int32_t *cta_hist, int n_cta,
+                              const int32_t *idx, const int32_t *local_rank, int T, const uint16_t *x,
+                              const int32_t *sigma, int32_t *slot_pos, uint32_t *done_ctr,
+                              int *ok_word, int *err, uint32_t epoch, cudaStream_t stream);
+// seg: counts [kEpMaxSegments] then offsets [kEpMaxSegments + 1]; seg_ptr [kEpMaxSegments]
+cudaError_t launch_ep_segments(const EpLayout &L, const EpPeers &P, uint32_t epoch, int *err,
+                               int *ok_word, int32_t *seg, float **seg_ptr, cudaStream_t stream);
+cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch,
+                             const int *ok_word, cudaStream_t stream);
 
 // out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,

@@ -79,8 +79,11 @@ struct PrefillArgs {
   uint16_t *h_hi, *h_lo;   // [S, I] f16
   int I;
   float alpha, limit;
-  // GEMM2 epilogue
+  // GEMM2 epilogue: row p of segment v goes to y_seg[v] + p * H when y_seg is
+  // given (expert parallel: the source rank's buffer, possibly a peer GPU's),
+  // else to y_slot + (offsets[v] + p) * H
   float *y_slot;  // [S, H]
+  float *const *y_seg;
   int H;
   int *err;
 };
@@ -415,7 +418,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const int ncol = min(32, c.nvalid - c0);
         if (GEMM == 2) {
           if (row_ok) {
-            float *dst = a.y_slot + (size_t)(pos_base + c0) * a.H + R;
+            float *dst = (a.y_seg ? a.y_seg[c.e] + (size_t)(c.n0 + c0) * a.H
+                                  : a.y_slot + (size_t)(pos_base + c0) * a.H) + R;
 #pragma unroll
             for (int cc = 0; cc < 32; ++cc)
               if (cc < ncol) dst[(size_t)cc * a.H] = __uint_as_float(v[cc]) + bias_own;
@@ -671,6 +675,7 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.n_segments = io.n_segments;
   a.weight_mod = io.weight_mod;
   a.y_slot = io.y_slot;
+  a.y_seg = io.y_seg;
   a.I = w.I;
   a.H = w.H;
   a.err = io.err;

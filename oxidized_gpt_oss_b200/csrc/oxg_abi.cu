@@ -139,9 +139,37 @@ struct oxg_ctx {
     int32_t *seg = nullptr;  // counts [256] then offsets [257]
   } ep;
   std::vector<int32_t> seg_host;
+  // Expert parallelism over peer memory (oxg_ep_init / oxg_ep_connect).
+  struct {
+    bool init = false, connected = false;
+    int layer = -1;
+    oxg::EpLayout lay{};
+    oxg::EpPeers peers{};
+    void *sym = nullptr;  // this rank's symmetric buffer (exported)
+    void *local = nullptr;  // h hi/lo [max_recv, I] x 2, segment table + pointers, counters
+    uint16_t *h_hi = nullptr, *h_lo = nullptr;
+    int32_t *seg = nullptr;
+    float **seg_ptr = nullptr;
+    uint32_t *done_ctr = nullptr;
+    int *ok_word = nullptr;
+    uint32_t epoch = 0;
+    int I = 0;  // intermediate size the h buffers were sized for
+  } p2p;
 };
 
 namespace {
+
+// Unmaps the peers' buffers and frees this rank's (callers synchronise ranks
+// first, so no peer still writes into it).
+void p2p_release(oxg_ctx *ctx) {
+  auto &q = ctx->p2p;
+  if (q.connected)
+    for (int r = 0; r < q.lay.W; ++r)
+      if (r != q.lay.rank && q.peers.base[r]) cudaIpcCloseMemHandle(q.peers.base[r]);
+  if (q.sym) cudaFree(q.sym);
+  if (q.local) cudaFree(q.local);
+  q = {};
+}
 
 struct DeviceGuard {
   int prev = -1;
@@ -519,8 +547,12 @@ int read_pipeline_error(oxg_ctx *ctx) {
   ctx->prefill_pending = false;
   if (h) {
     cudaMemsetAsync(ctx->ws.err, 0, sizeof(int), ctx->stream);
+    if (h == 50)
+      return fail(ctx, OXG_ERR_STATE, "another rank reported a failed expert-parallel step");
+    if (h == 51)
+      return fail(ctx, OXG_ERR_SHAPE, "expert-parallel receive capacity exceeded (raise max_recv_rows)");
     return fail(ctx, h >= 100 ? OXG_ERR_CUDA : OXG_ERR_TIMEOUT,
-                h >= 100 ? "prefill self-check failed (code %d)" : "prefill pipeline wait timed out (stage %d)", h);
+                h >= 100 ? "prefill self-check failed (code %d)" : "pipeline wait timed out (stage %d)", h);
   }
   return OXG_OK;
 }
@@ -627,6 +659,7 @@ int oxg_ctx_destroy(oxg_ctx *ctx) {
   for (Layer &L : ctx->layers) free_layer(L);
   if (ctx->ws.base) cudaFree(ctx->ws.base);
   if (ctx->ep.base) cudaFree(ctx->ep.base);
+  p2p_release(ctx);
   ctx->prof.destroy();
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -1053,6 +1086,206 @@ int oxg_moe_combine(oxg_ctx *ctx, int layer, const float *y_rows, int T, float *
   OXG_CUDA(ctx, launch(ctx, "combine", [&] {
              return oxg::launch_combine(y_rows, ctx->ws.slot_pos, ctx->ws.wts, T, d.hidden,
                                         d.top_k, y, ctx->stream);
+           }),
+           "combine launch");
+  return OXG_OK;
+}
+
+// ---- expert parallelism over peer memory -----------------------------------------
+int oxg_ep_init(oxg_ctx *ctx, int layer, int rank, int world, int max_tokens, long long max_recv_rows,
+                void *handle_out) {
+  Layer *L = nullptr;
+  int rc = check_ep_layer(ctx, layer, &L);
+  if (rc) return rc;
+  const oxg_moe_dims &d = L->dims;
+  if (world < 1 || world > oxg::kEpMaxRanks || rank < 0 || rank >= world)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "rank %d of world %d: world must be in [1, %d]", rank, world,
+                oxg::kEpMaxRanks);
+  if (d.n_experts % world || d.n_experts > oxg::kEpMaxExperts ||
+      !oxg::router_mma_supported(d.hidden, d.n_experts, d.top_k))
+    return fail(ctx, OXG_ERR_UNSUPPORTED,
+                "peer-memory expert parallelism needs n_experts (%d) a multiple of the world (%d) "
+                "and of 16, at most %d, and hidden a multiple of 16",
+                d.n_experts, world, oxg::kEpMaxExperts);
+  const int per = d.n_experts / world;
+  if (L->expert_begin != rank * per || L->expert_count != per)
+    return fail(ctx, OXG_ERR_STATE, "rank %d must hold experts [%d, %d) of layer %d", rank, rank * per,
+                rank * per + per, layer);
+  if (max_tokens < 1) return fail(ctx, OXG_ERR_INVALID_ARG, "max_tokens must be >= 1");
+  const long long worst = (long long)world * max_tokens * d.top_k;
+  if (max_recv_rows <= 0) max_recv_rows = worst;
+  if (max_recv_rows > worst) max_recv_rows = worst;
+  if (!handle_out) return fail(ctx, OXG_ERR_INVALID_ARG, "handle_out must be non-NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  p2p_release(ctx);
+  auto &q = ctx->p2p;
+  q.lay = oxg::ep_layout(world, d.n_experts, d.hidden, d.top_k, rank, max_tokens, max_recv_rows);
+  OXG_CUDA(ctx, cudaMalloc(&q.sym, q.lay.bytes), "cudaMalloc(expert-parallel symmetric buffer)");
+  OXG_CUDA(ctx, cudaMemset(q.sym, 0, q.lay.off_inbox), "zero the flags");
+  const size_t hb = align_up((size_t)max_recv_rows * d.intermediate * 2, 256);
+  const size_t local_bytes = 2 * hb + align_up((oxg::kEpMaxSegments * 2 + 1) * 4, 256) +
+                             align_up(oxg::kEpMaxSegments * sizeof(float *), 256) + 256;
+  OXG_CUDA(ctx, cudaMalloc(&q.local, local_bytes), "cudaMalloc(expert-parallel scratch)");
+  OXG_CUDA(ctx, cudaMemset(q.local, 0, local_bytes), "zero the expert-parallel scratch");
+  char *b = (char *)q.local;
+  q.h_hi = (uint16_t *)b;
+  q.h_lo = (uint16_t *)(b + hb);
+  q.seg = (int32_t *)(b + 2 * hb);
+  q.seg_ptr = (float **)(b + 2 * hb + align_up((oxg::kEpMaxSegments * 2 + 1) * 4, 256));
+  q.done_ctr = (uint32_t *)((char *)q.seg_ptr + align_up(oxg::kEpMaxSegments * sizeof(float *), 256));
+  q.ok_word = (int *)(q.done_ctr + 1);
+  cudaIpcMemHandle_t h;
+  OXG_CUDA(ctx, cudaIpcGetMemHandle(&h, q.sym), "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  q.peers.base[rank] = (char *)q.sym;
+  q.layer = layer;
+  q.I = d.intermediate;
+  q.init = true;
+  return OXG_OK;
+}
+
+int oxg_ep_connect(oxg_ctx *ctx, const void *handles) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  auto &q = ctx->p2p;
+  if (!q.init) return fail(ctx, OXG_ERR_STATE, "oxg_ep_init first");
+  if (!handles) return fail(ctx, OXG_ERR_INVALID_ARG, "handles must be non-NULL");
+  DeviceGuard g(ctx->device);
+  const char *hb = (const char *)handles;
+  for (int r = 0; r < q.lay.W; ++r) {
+    if (r == q.lay.rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+    void *p = nullptr;
+    OXG_CUDA(ctx, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess),
+             "cudaIpcOpenMemHandle (peer buffer)");
+    q.peers.base[r] = (char *)p;
+  }
+  q.connected = true;
+  return OXG_OK;
+}
+
+int oxg_ep_close(oxg_ctx *ctx) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(ctx->device);
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  p2p_release(ctx);
+  return OXG_OK;
+}
+
+int oxg_ep_last_received(oxg_ctx *ctx, long long *rows) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  if (!rows) return fail(ctx, OXG_ERR_INVALID_ARG, "rows must be non-NULL");
+  auto &q = ctx->p2p;
+  if (!q.connected) return fail(ctx, OXG_ERR_STATE, "oxg_ep_init and oxg_ep_connect first");
+  DeviceGuard g(ctx->device);
+  int32_t total = 0;
+  OXG_CUDA(ctx, cudaMemcpyAsync(&total, q.seg + oxg::kEpMaxSegments + q.lay.W * q.lay.per, sizeof(total),
+                                cudaMemcpyDeviceToHost, ctx->stream),
+           "read received rows");
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  *rows = total;
+  return OXG_OK;
+}
+
+int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y) {
+  Layer *L = nullptr;
+  int rc = check_ep_layer(ctx, layer, &L);
+  if (rc) return rc;
+  auto &q = ctx->p2p;
+  if (!q.connected) return fail(ctx, OXG_ERR_STATE, "oxg_ep_init and oxg_ep_connect first");
+  if (L->expert_begin != q.lay.rank * q.lay.per || L->expert_count != q.lay.per ||
+      L->dims.n_experts != q.lay.E || L->dims.hidden != q.lay.H || L->dims.intermediate != q.I ||
+      L->dims.top_k != q.lay.k)
+    return fail(ctx, OXG_ERR_STATE, "layer %d does not hold rank %d's experts of the connected layout",
+                layer, q.lay.rank);
+  if (T < 0 || T > q.lay.max_tokens)
+    return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be in [0, %lld], got %d", q.lay.max_tokens, T);
+  if (T > 0 && (!x || !y)) return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be non-NULL");
+  if (((uintptr_t)x & 15) || ((uintptr_t)y & 15))
+    return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  const oxg_moe_dims &d = L->dims;
+  if ((rc = ensure_scratch(ctx, d, T < 1 ? 1 : T))) return rc;
+  ctx->last_layer = layer;
+  ctx->ep_tokens = -1;
+  // every rank takes every step, also with no tokens of its own: the others wait for its flags
+  const uint32_t epoch = ++q.epoch;
+  const oxg::EpLayout lay = q.lay;
+  const oxg::EpPeers peers = q.peers;
+  const int n_cta = oxg::router_mma_ctas(T);
+  if (T > 0) {
+    OXG_CUDA(ctx, launch(ctx, "router_mma", [&] {
+               return oxg::launch_router_mma(x, L->router_w, L->router_b, T, d.hidden, d.n_experts,
+                                             d.top_k, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits,
+                                             ctx->ws.sigma, ctx->ws.cta_hist, ctx->ws.local_rank,
+                                             ctx->stream);
+             }),
+             "router_mma launch");
+  }
+  OXG_CUDA(ctx, launch(ctx, "ep_counts", [&] {
+             return oxg::launch_ep_counts(lay, peers, ctx->ws.cta_hist, n_cta, ctx->ws.counts,
+                                          ctx->ws.offsets, q.ok_word, epoch, ctx->stream);
+           }),
+           "ep_counts launch");
+  OXG_CUDA(ctx, launch(ctx, "ep_wait", [&] {
+             return oxg::launch_ep_wait(lay, peers, 0, epoch, ctx->ws.err, 11, q.ok_word, ctx->stream);
+           }),
+           "ep_wait launch");
+  if (T > 0) {
+    OXG_CUDA(ctx, launch(ctx, "ep_scatter", [&] {
+               return oxg::launch_ep_scatter(lay, peers, ctx->ws.cta_hist, n_cta, ctx->ws.idx,
+                                             ctx->ws.local_rank, T, x, ctx->ws.sigma, ctx->ws.slot_pos,
+                                             q.done_ctr, q.ok_word, ctx->ws.err, epoch, ctx->stream);
+             }),
+             "ep_scatter launch");
+  } else {  // nothing to send: raise the rows flags at once
+    OXG_CUDA(ctx, launch(ctx, "ep_signal", [&] {
+               return oxg::launch_ep_signal(lay, peers, 1, epoch, q.ok_word, ctx->stream);
+             }),
+             "ep_signal launch");
+  }
+  OXG_CUDA(ctx, launch(ctx, "ep_segments", [&] {
+             return oxg::launch_ep_segments(lay, peers, epoch, ctx->ws.err, q.ok_word, q.seg,
+                                            q.seg_ptr, ctx->stream);
+           }),
+           "ep_segments launch");
+  const oxg::MoeDeviceWeights w = device_weights(*L);
+  oxg::PrefillIO io{};
+  io.S = (int)lay.max_recv;
+  io.counts = q.seg;
+  io.offsets = q.seg + oxg::kEpMaxSegments;
+  io.n_segments = lay.W * lay.per;
+  io.weight_mod = lay.per;
+  io.xp = (const uint16_t *)((char *)q.sym + lay.off_recv_rows);
+  io.pos_scale = (const float *)((char *)q.sym + lay.off_recv_scale);
+  io.h_hi = q.h_hi;
+  io.h_lo = q.h_lo;
+  io.y_slot = nullptr;
+  io.y_seg = q.seg_ptr;
+  io.err = ctx->ws.err;
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp1_prefill", [&] {
+             return oxg::launch_prefill_mlp1(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp1 launch");
+  OXG_CUDA(ctx, launch(ctx, "moe_mlp2_prefill", [&] {
+             return oxg::launch_prefill_mlp2(w, io, ctx->n_sms, ctx->stream);
+           }),
+           "prefill mlp2 launch");
+  OXG_CUDA(ctx, launch(ctx, "ep_signal", [&] {
+             return oxg::launch_ep_signal(lay, peers, 2, epoch, q.ok_word, ctx->stream);
+           }),
+           "ep_signal launch");
+  OXG_CUDA(ctx, launch(ctx, "ep_wait", [&] {
+             return oxg::launch_ep_wait(lay, peers, 2, epoch, ctx->ws.err, 13, q.ok_word, ctx->stream);
+           }),
+           "ep_wait launch");
+  ctx->prefill_pending = true;
+  if (T == 0) return OXG_OK;
+  OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+             return oxg::launch_combine((const float *)((char *)q.sym + lay.off_ret_rows),
+                                        ctx->ws.slot_pos, ctx->ws.wts, T, d.hidden, d.top_k, y,
+                                        ctx->stream);
            }),
            "combine launch");
   return OXG_OK;

@@ -88,3 +88,63 @@ class ExpertParallelMoE:
         return self.shard.combine(y_back, T)
 
     __call__ = forward
+
+
+class PeerExpertParallelMoE:
+    """The same split with the exchange inside the library: rows and output
+    rows are stored straight into the other GPUs' buffers (CUDA IPC mappings
+    over NVLink), counts and completion flags too, so a forward needs no host
+    round trip (``oxg_moe_forward_ep``). ``torch.distributed`` only carries
+    the IPC handles once, at construction. Every rank must call ``forward``
+    the same number of times; ``close`` on every rank when all are done."""
+
+    def __init__(self, shard, max_tokens: int, group=None, max_recv_rows: int = 0):
+        import ctypes
+        from .mxfp4 import context
+        self.shard = shard
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_tokens = int(max_tokens)
+        c = context(shard.ctx)
+        self._ctx = c
+        handle = (ctypes.c_char * 64)()
+        from . import abi
+        abi.check(c.lib.oxg_ep_init(c.handle, shard.layer, self.rank, self.world, self.max_tokens,
+                                    int(max_recv_rows), handle), c.handle)
+        mine = bytes(handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        blob = (ctypes.c_char * (64 * self.world)).from_buffer_copy(b"".join(handles))
+        abi.check(c.lib.oxg_ep_connect(c.handle, blob), c.handle)
+        self._abi = abi
+
+    def forward(self, hidden: torch.Tensor, out: torch.Tensor | None = None, shard=None) -> torch.Tensor:
+        """shard: another layer's shard on the same context with the same
+        shapes and expert range (the buffers depend only on those)."""
+        from .mxfp4 import context
+        shard = shard or self.shard
+        x = hidden.contiguous()
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, shard.hidden), dtype=torch.float32, device=x.device)
+        c = context(shard.ctx)
+        self._abi.check(c.lib.oxg_moe_forward_ep(c.handle, shard.layer, x.data_ptr() if T else None, T,
+                                                 out.data_ptr() if T else None), c.handle)
+        return out
+
+    def last_received(self) -> int:
+        """Rows this rank received in the last forward (waits for it)."""
+        import ctypes
+        n = ctypes.c_longlong()
+        self._abi.check(self._ctx.lib.oxg_ep_last_received(self._ctx.handle, ctypes.byref(n)), self._ctx.handle)
+        return n.value
+
+    __call__ = forward
+
+    def close(self) -> None:
+        """After every rank's last forward: synchronise, then unmap and free."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self._abi.check(self._ctx.lib.oxg_ep_close(self._ctx.handle), self._ctx.handle)
+        dist.barrier(group=self.group)

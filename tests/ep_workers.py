@@ -125,3 +125,34 @@ def gpu_worker(rank, world, port, layer_kw, tokens, out_dir):
                          "splits": moe.last_splits}, f)
     finally:
         dist.destroy_process_group()
+
+
+def gpu_p2p_worker(rank, world, port, layer_kw, tokens, out_dir):
+    """Peer-memory expert parallelism: two forwards (two epochs) per rank, each
+    compared with the full layer's single-GPU forward."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    moe = None
+    try:
+        from oxidized_gpt_oss_b200.moe import MoELayer
+        d = synth.moe_layer(**layer_kw)
+        begin, count = ep.shard_range(d["n_experts"], world, rank)
+        shard = MoELayer(d, experts=(begin, count))
+        full = MoELayer(d)
+        moe = ep.PeerExpertParallelMoE(shard, max_tokens=max(tokens))
+        res = []
+        for it in range(2):
+            x = torch.from_numpy(synth.activations(100 * it + rank, tokens[rank], d["hidden"]).view(np.int16)).cuda()
+            y_ep = moe(x).clone()
+            y_full = full.forward(x).clone() if tokens[rank] else torch.empty_like(y_ep)
+            torch.cuda.synchronize()
+            shard.ctx.sync()
+            res.append((bool(torch.equal(y_ep, y_full)),
+                        float((y_ep - y_full).abs().max()) if y_ep.numel() else 0.0))
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump({"res": res}, f)
+    finally:
+        if moe is not None:
+            moe.close()
+        dist.destroy_process_group()

@@ -33,3 +33,20 @@ def test_two_gpus_equal_single_gpu(tmp_path, layer_kw, tokens):
         with open(os.path.join(tmp_path, f"rank{r}.pkl"), "rb") as f:
             got = pickle.load(f)
         assert got["equal"], f"rank {r}: max |ep - single| = {got['max_diff']}"
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+@pytest.mark.parametrize("layer_kw,tokens", [
+    (dict(seed=31, hidden=256, intermediate=256, n_experts=16, top_k=4), (200, 90)),
+    (dict(seed=33, hidden=256, intermediate=256, n_experts=16, top_k=4), (150, 0)),  # a rank with no tokens
+    (dict(seed=32), (300, 257)),
+])
+def test_two_gpus_peer_memory_equal_single_gpu(tmp_path, layer_kw, tokens):
+    mp.spawn(ep_workers.gpu_p2p_worker, args=(2, _port(), layer_kw, tokens, str(tmp_path)), nprocs=2,
+             join=True)
+    for r in range(2):
+        with open(os.path.join(tmp_path, f"rank{r}.pkl"), "rb") as f:
+            got = pickle.load(f)
+        for it, (equal, diff) in enumerate(got["res"]):
+            assert equal, f"rank {r} forward {it}: max |ep - single| = {diff}"
