@@ -315,23 +315,29 @@ def run_moe(args, ws, rank, local):
         step(i)
     torch.cuda.synchronize()
     names = ("route_small", "router_topk", "router_mma", "permute", "scatter", "moe_mlp1_decode",
-             "moe_mlp2_decode", "combine")
+             "moe_mlp2_decode", "mxf_mlp1", "mxf_mlp2", "combine")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     ctx.profile(False)
     ms_max = max_over_ranks(ms, ws)
 
-    # roofline of the dominant kernel (mlp1: gate/up projection + SwiGLU)
+    # roofline of the dominant kernel (mlp1: gate/up projection + SwiGLU).
+    # Algorithmic bytes: the hit experts' codes, scales and biases once, x
+    # once, and the intermediate h once each way (f32 on the mma.sync path,
+    # four E4M3 terms on the block-scaled path).
+    mxf = "mxf_mlp1" in k_ms
+    k1, k2 = ("mxf_mlp1", "mxf_mlp2") if mxf else ("moe_mlp1_decode", "moe_mlp2_decode")
+    h_bytes = T * K * I * 4  # f32, or four E4M3 terms
     mlp1_w = 2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2
     mlp2_w = H * I // 2 + H * I // 32 + H * 2
-    mlp1_bytes = hits * mlp1_w + args.steps * (T * H * 2 + T * K * I * 4)
-    mlp2_bytes = hits * mlp2_w + args.steps * (T * K * I * 4 + T * K * H * 4)
+    mlp1_bytes = hits * mlp1_w + args.steps * (T * H * 2 + h_bytes)
+    mlp2_bytes = hits * mlp2_w + args.steps * (h_bytes + T * K * H * 4)
     layer_bytes = mlp1_bytes + mlp2_bytes + args.steps * (E * H * 2 + T * H * 4)
     hbm, hbm_kind = peaks()
-    m1_ms, m1_n = k_ms["moe_mlp1_decode"]
-    m2_ms, m2_n = k_ms["moe_mlp2_decode"]
+    m1_ms, m1_n = k_ms[k1]
+    m2_ms, m2_n = k_ms[k2]
     achieved = mlp1_bytes / (m1_ms * 1e-3) / 1e9
-    traffic = ncu_traffic("moe_mlp1_decode", f"T{T}")
+    traffic = ncu_traffic(k1, f"T{T}")
 
     # end to end through the host-buffer API: pinned x in, y out, every step
     xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
@@ -350,9 +356,11 @@ def run_moe(args, ws, rank, local):
     out = {"metric": METRIC, "value": T * ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-           "dtype": "mxfp4 weights x bf16 activations (exact f16 MMA operands), f32 accumulate",
+           "dtype": ("mxfp4 weights (E2M1 + E8M0 into tcgen05 block-scaled MMA) x bf16 activations as "
+                     "E4M3 terms (2 for x, 4 for h), f32 accumulate") if mxf else
+                    "mxfp4 weights x bf16 activations (exact f16 MMA operands), f32 accumulate",
            "data": "synthetic", "config": moe_config(args, d0),
-           "roofline": {"bound": "hbm", "kernel": "moe_mlp1_decode", "achieved": achieved, "peak": hbm,
+           "roofline": {"bound": "hbm", "kernel": k1, "achieved": achieved, "peak": hbm,
                         "peak_kind": hbm_kind, "unit": "GB/s", "frac": achieved / hbm,
                         "traffic": traffic,
                         "algorithmic_bytes_per_launch": mlp1_bytes / max(m1_n, 1),
@@ -399,7 +407,7 @@ def run_prefill(args, ws, rank, local):
     xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
     xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
     y = torch.empty((T, H), dtype=torch.float32, device=device)
-    mode = abi.OXG_MODE_PREFILL
+    mode = abi.OXG_MODE_MXF4 if args.path == "mxf4" else abi.OXG_MODE_PREFILL
     rows_done = [0]  # expert rows this rank computed (varies with the routing under EP)
 
     count_rows = [False]  # in the profiled pass: ask each step how many rows it received
@@ -448,9 +456,11 @@ def run_prefill(args, ws, rank, local):
     count_rows[0] = False
     rows_profiled = rows_done[0]
     names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
-             "moe_mlp2_prefill", "combine")
+             "moe_mlp2_prefill", "scatter_e4m3", "gather_e4m3", "mxf_gemm1", "mxf_gemm2", "combine")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
+    mxf = "mxf_gemm1" in k_ms
+    k1, k2 = ("mxf_gemm1", "mxf_gemm2") if mxf else ("moe_mlp1_prefill", "moe_mlp2_prefill")
     ctx.profile(False)
     ms_max = max_over_ranks(ms, ws)
 
@@ -461,8 +471,8 @@ def run_prefill(args, ws, rank, local):
     rows_per_step = rows_profiled / args.steps
     flop1, flop2 = f1_row * rows_per_step, f2_row * rows_per_step
     peak, peak_kind = tensor_peak()
-    m1_ms, m1_n = k_ms["moe_mlp1_prefill"]
-    m2_ms, m2_n = k_ms["moe_mlp2_prefill"]
+    m1_ms, m1_n = k_ms[k1]
+    m2_ms, m2_n = k_ms[k2]
     achieved = f1_row * rows_profiled / (m1_ms * 1e-3) / 1e12
     layer_tflops = (flop1 + flop2) * args.steps / (ms * 1e-3) / 1e12
 
@@ -491,7 +501,9 @@ def run_prefill(args, ws, rank, local):
     out = {"metric": METRIC, "value": T * ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-           "dtype": "mxfp4 weights x bf16 activations (exact f16 tcgen05 operands), f32 accumulate",
+           "dtype": ("mxfp4 weights (E2M1 + E8M0 into tcgen05 block-scaled MMA) x bf16 activations as E4M3 "
+                     "terms (2 for x, 3 for h), f32 accumulate") if mxf else
+                    "mxfp4 weights x bf16 activations (exact f16 tcgen05 operands), f32 accumulate",
            "data": "synthetic",
            "config": {"workload": "moe_prefill", "tokens_per_gpu": T, "hidden": H, "intermediate": I,
                       "experts": E, "top_k": K, "weights": "mxfp4 e2m1 + e8m0[118,126]",
@@ -503,9 +515,9 @@ def run_prefill(args, ws, rank, local):
                                        "library's kernels)" if p2p is not None else "NCCL all-to-all)"))
                                      if ws > 1 else "single",
                       "expert_rows_per_step_rank0": rows_per_step},
-           "roofline": {"bound": "tensor", "kernel": "moe_mlp1_prefill", "achieved": achieved, "peak": peak,
+           "roofline": {"bound": "tensor", "kernel": k1, "achieved": achieved, "peak": peak,
                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
-                        "traffic": ncu_traffic("moe_mlp1_prefill", f"T{T}") if ws == 1 else None,
+                        "traffic": ncu_traffic(k1, f"T{T}") if ws == 1 else None,
                         "algorithmic_flop_per_launch": flop1,
                         "flop_per_unit": f1_row, "unit_of_work": "expert row (token, slot)",
                         "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3},
@@ -624,6 +636,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--path", choices=["mxf4", "f16"], default="mxf4",
+                    help="prefill expert kernels on one GPU: block-scaled (E2M1 straight into tcgen05) or the "
+                         "f16-dequant tcgen05 GEMMs")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="moe_prefill on N > 1 GPUs: exchange over peer memory in the library's kernels "
                          "(default) or by NCCL all-to-all")

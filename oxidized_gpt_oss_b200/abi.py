@@ -29,6 +29,7 @@ OXG_SCALE_BF16 = 1
 OXG_MODE_AUTO = 0
 OXG_MODE_DECODE = 1
 OXG_MODE_PREFILL = 2
+OXG_MODE_MXF4 = 3
 OXG_PRECISION_PARITY = 0
 
 

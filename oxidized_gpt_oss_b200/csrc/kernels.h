@@ -49,18 +49,31 @@ cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16
 // Stable counting sort of the T*k (token, j) slots by expert.
 //   counts[E], offsets[E+1], perm[T*k] (position -> slot), slot_pos[T*k]
 //   (slot -> position).
+// pad > 1: each expert's positions start at a multiple of pad (offsets[E]
+// is the padded total; perm is defined on the occupied positions only).
 cudaError_t launch_permute(const int32_t *idx, int n_slots, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int pad = 1);
 
 // Positions from launch_router_mma's histograms and ranks (same result as
 // launch_permute) and, when xp is not null, the prefill gather: xp[p] = f16
 // x[token of slot perm[p]] * 2^-sigma, pos_scale[p] = 2^sigma.
+// With terms: each expert's positions start at a multiple of 128 (offsets
+// padded; offsets[E] the padded total) and x rows are written as the
+// block-scaled prefill operand (two E4M3 planes [2][rows_cap][H] and scale
+// atoms [2][rows_cap / 128][ceil(H / 128)][512]).
+struct ScatterTerms {
+  uint8_t *xq, *xsf;
+  int rows_cap;  // multiple of 128, >= T * k + E * 127
+};
 cudaError_t launch_scatter(const int32_t *cta_hist, int n_cta, const int32_t *idx,
                            const int32_t *local_rank, int T, int k, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos, const uint16_t *x,
                            const int32_t *sigma, int H, uint16_t *xp, float *pos_scale,
-                           cudaStream_t stream);
+                           cudaStream_t stream, const ScatterTerms *terms = nullptr);
+// The same operand rows from slot_pos (after launch_permute with pad 128).
+cudaError_t launch_gather_e4m3(const uint16_t *x, const int32_t *slot_pos, int S, int k, int H,
+                               const ScatterTerms &terms, cudaStream_t stream);
 
 // ---- fused routing for small batches (route_small.cu) -------------------------
 constexpr int kMaxRouteTokens = 64;
@@ -77,10 +90,70 @@ struct RouteSmallArgs {
   uint32_t *done;              // CTA completion counter (zero between calls)
   uint32_t *band_done;         // per-band counters of the mlp2 kernel, zeroed here
   int n_bands;
+  // optional (block-scaled expert path): x as two E4M3 terms per element,
+  // rows 2t + term of xq [2T, H], and their UE8M0 scale atoms xsf
+  // [ceil(H/128)][512] (row 2t + term, one byte per 32-element block)
+  uint8_t *xq, *xsf;
 };
 // pdl: launch with programmatic stream serialisation (overlaps the previous
 // kernel's tail; the kernel waits for it before touching memory).
 cudaError_t launch_route_small(const RouteSmallArgs &a, cudaStream_t stream, bool pdl);
+
+// ---- block-scaled decode MoE (moe_mxf.cu) -------------------------------------
+constexpr int kMaxMxfTokens = 8;
+constexpr int kMxfPrefillTileN = 192;  // weight rows per prefill GEMM tile (the pair's MMA N)
+
+// Weights as the block-scaled path reads them: the checkpoint's packed codes
+// (64 bytes of slack after each matrix) and UE8M0 scale atoms
+// [E][ceil(rows/128)][ceil(K/128)][512].
+struct MxfWeights {
+  int H, I, E, k;
+  float alpha, limit;
+  const uint8_t *q1, *a1;  // [E, 2I, H/2], atoms of [E, 2I, H/32]
+  const uint16_t *b1;
+  const uint8_t *q2, *a2;  // [E, H, I/2], atoms of [E, H, I/32]
+  const uint16_t *b2;
+};
+struct MxfScratch {
+  const int32_t *active, *n_active, *counts, *offsets, *idx, *slot_pos;
+  const float *wts;
+  const uint8_t *xq, *xsf;   // from route_small
+  uint8_t *hq, *hsf;         // [4 T k, I] terms, [E][ceil(I/128)][512] atoms
+  float *y_slot;             // [T k, H]
+  uint32_t *band_done;       // 4 per 128-row band of H, zero between calls
+  float *y;                  // [T, H]
+  int *err;
+};
+bool mxf_decode_supported(int H, int I, int T, int k);
+// scale atoms of [E][rows][K/32] for weight tiles of tile_rows rows (128:
+// decode, one atom per tile; 192: prefill, two)
+size_t sf_atoms_bytes(int E, int rows, int K, int tile_rows);
+cudaError_t launch_sf_atoms(const uint8_t *scales, int E, int rows, int K, int tile_rows, uint8_t *atoms,
+                            cudaStream_t stream);
+cudaError_t launch_mxf_mlp1(const MxfWeights &w, const MxfScratch &s, int T, int n_sms, bool pdl,
+                            cudaStream_t stream);
+cudaError_t launch_mxf_mlp2(const MxfWeights &w, const MxfScratch &s, int T, int n_sms, bool pdl,
+                            cudaStream_t stream);
+
+// ---- block-scaled prefill GEMMs (moe_mxf_prefill.cu) ---------------------------
+// Operand buffers: x terms [2][rows_cap][H] with atoms [2][rows_cap/128][ceil(H/128)][512]
+// (from launch_scatter / launch_gather_e4m3), h terms [3][rows_cap][I] with
+// atoms [3][rows_cap/128][ceil(I/128)][512], y_slot [rows_cap][H] f32;
+// counts/offsets with every expert's first position a multiple of 128.
+struct MxfPrefillIO {
+  const int32_t *counts, *offsets;
+  const uint8_t *xq, *xsf;
+  uint8_t *hq, *hsf;
+  int rows_cap;
+  float *y_slot;
+  int *err;
+};
+bool mxf_prefill_supported(int H, int I, int E);
+int mxf_rows_cap(int n_slots, int E);
+// gemm 1 (x terms -> h terms) or 2 (h terms -> y_slot); p_atoms: that
+// GEMM's weight scale atoms for 192-row tiles (sf_atoms_bytes(.., 192))
+cudaError_t launch_mxf_prefill(const MxfWeights &w, const uint8_t *p_atoms, const MxfPrefillIO &io, int gemm,
+                               int n_sms, cudaStream_t stream);
 
 // ---- decode MoE (moe_decode.cu) ---------------------------------------------
 struct MoeDeviceWeights {

@@ -34,6 +34,13 @@ struct Layer {
   // prefill path applies (H and I multiples of 64 too).
   bool prefill_ok = false;
   unsigned scale_min = 0, scale_max = 0;
+  // The block-scaled tensor-core copy: the checkpoint's packed codes as they
+  // are and the scale atoms (moe_mxf.cu). Usable when H and I are multiples
+  // of 64 (>= 128) and no scale is 255 (NaN as a UE8M0 scale; +inf in the
+  // reference's dequantisation).
+  uint8_t *q1 = nullptr, *a1 = nullptr, *q2 = nullptr, *a2 = nullptr;
+  uint8_t *p1 = nullptr, *p2 = nullptr;  // scale atoms of the prefill GEMMs' 192-row weight tiles
+  bool mxf_ok = false;
   // experts [expert_begin, expert_begin + expert_count) are resident (all of
   // them unless uploaded with oxg_moe_upload_shard); the router is complete
   int expert_begin = 0, expert_count = 0;
@@ -59,6 +66,14 @@ struct Scratch {
   float *wts = nullptr, *logits = nullptr, *h = nullptr, *y_slot = nullptr;
   uint16_t *x_stage = nullptr;
   float *y_stage = nullptr;
+  // block-scaled decode operands: x and h as E4M3 terms and their scale
+  // atoms; zeroed whenever the layout changes (no stale NaN scale bytes)
+  uint8_t *xq = nullptr, *xsf = nullptr, *hq = nullptr, *hsf = nullptr;
+  size_t xq_bytes = 0, xsf_bytes = 0, hq_bytes = 0, hsf_bytes = 0;
+  size_t layout_key = 0;
+  // block-scaled prefill operands (padded positions, rows_cap rows per plane)
+  uint8_t *pxq = nullptr, *pxsf = nullptr, *phq = nullptr, *phsf = nullptr;
+  int rows_cap = 0;
 };
 
 // CUDA-event brackets around kernel launches, read back on demand.
@@ -241,12 +256,33 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_logits = take((size_t)T * d.n_experts * 4);
   char *p_counts = take((size_t)d.n_experts * 4), *p_offsets = take(((size_t)d.n_experts + 1) * 4);
   char *p_perm = take(S * 4), *p_slot = take(S * 4);
-  char *p_h = take(S * d.intermediate * 4), *p_y = take(S * d.hidden * 4);
+  const int rows_cap = oxg::mxf_rows_cap((int)S, d.n_experts);
+  char *p_h = take(S * d.intermediate * 4), *p_y = take(std::max(S, (size_t)rows_cap) * d.hidden * 4);
   char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
   char *p_xp = take(S * d.hidden * 2), *p_hhi = take(S * d.intermediate * 2);
   char *p_hlo = take(S * d.intermediate * 2), *p_psc = take(S * 4);
   char *p_hist = take((size_t)oxg::router_mma_ctas(T) * d.n_experts * 4), *p_rank = take(S * 4);
+  const size_t xq_b = (size_t)2 * T * d.hidden, xsf_b = (size_t)(d.hidden + 127) / 128 * 512;
+  const size_t hq_b = 4 * S * d.intermediate;
+  const size_t hsf_b = (size_t)d.n_experts * ((d.intermediate + 127) / 128) * 512;
+  char *p_xq = take(xq_b), *p_xsf = take(xsf_b), *p_hq = take(hq_b), *p_hsf = take(hsf_b);
+  const size_t rt = (size_t)rows_cap / 128, kt1 = (d.hidden + 127) / 128, kt2 = (d.intermediate + 127) / 128;
+  char *p_pxq = take(2 * (size_t)rows_cap * d.hidden), *p_pxsf = take(2 * rt * kt1 * 512);
+  char *p_phq = take(3 * (size_t)rows_cap * d.intermediate), *p_phsf = take(3 * rt * kt2 * 512);
   if (s && base) {
+    s->pxq = (uint8_t *)p_pxq;
+    s->pxsf = (uint8_t *)p_pxsf;
+    s->phq = (uint8_t *)p_phq;
+    s->phsf = (uint8_t *)p_phsf;
+    s->rows_cap = rows_cap;
+    s->xq = (uint8_t *)p_xq;
+    s->xsf = (uint8_t *)p_xsf;
+    s->hq = (uint8_t *)p_hq;
+    s->hsf = (uint8_t *)p_hsf;
+    s->xq_bytes = xq_b;
+    s->xsf_bytes = xsf_b;
+    s->hq_bytes = hq_b;
+    s->hsf_bytes = hsf_b;
     s->done = (uint32_t *)p_cnt;
     s->err = (int *)(s->done + 1);
     s->band_done = s->done + 2;
@@ -277,9 +313,20 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
 int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
   const int Tc = T < 1 ? 1 : T;
   const size_t need = scratch_bytes(d, Tc, nullptr, nullptr);
+  const size_t key = ((size_t)Tc * 1000003u + (size_t)d.hidden) * 1000003u +
+                     ((size_t)d.intermediate * 4099u + (size_t)d.n_experts * 17u + (size_t)d.top_k);
+  auto zero_terms = [&]() -> int {
+    if (ctx->ws.layout_key == key) return OXG_OK;
+    OXG_CUDA(ctx, cudaMemsetAsync(ctx->ws.xq, 0, ctx->ws.xq_bytes, ctx->stream), "cudaMemsetAsync(xq)");
+    OXG_CUDA(ctx, cudaMemsetAsync(ctx->ws.xsf, 0, ctx->ws.xsf_bytes, ctx->stream), "cudaMemsetAsync(xsf)");
+    OXG_CUDA(ctx, cudaMemsetAsync(ctx->ws.hq, 0, ctx->ws.hq_bytes, ctx->stream), "cudaMemsetAsync(hq)");
+    OXG_CUDA(ctx, cudaMemsetAsync(ctx->ws.hsf, 0, ctx->ws.hsf_bytes, ctx->stream), "cudaMemsetAsync(hsf)");
+    ctx->ws.layout_key = key;
+    return OXG_OK;
+  };
   if (need <= ctx->ws.bytes) {
     scratch_bytes(d, Tc, &ctx->ws, (char *)ctx->ws.base);
-    return OXG_OK;
+    return zero_terms();
   }
   if (ctx->ws.base) {
     OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
@@ -292,7 +339,7 @@ int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
   ctx->ws.bytes = need;
   scratch_bytes(d, Tc, &ctx->ws, (char *)p);
   OXG_CUDA(ctx, cudaMemsetAsync(p, 0, kCounterBytes, ctx->stream), "cudaMemsetAsync(counters)");
-  return OXG_OK;
+  return zero_terms();
 }
 
 Layer *get_layer(oxg_ctx *ctx, int layer) {
@@ -320,6 +367,23 @@ oxg::MoeDeviceWeights device_weights(const Layer &L) {
   w.b1 = L.b1;
   w.w2 = L.w2;
   w.s2 = L.s2;
+  w.b2 = L.b2;
+  return w;
+}
+
+oxg::MxfWeights mxf_weights(const Layer &L) {
+  oxg::MxfWeights w{};
+  w.H = L.dims.hidden;
+  w.I = L.dims.intermediate;
+  w.E = L.dims.n_experts;
+  w.k = L.dims.top_k;
+  w.alpha = L.dims.swiglu_alpha;
+  w.limit = L.dims.swiglu_limit;
+  w.q1 = L.q1;
+  w.a1 = L.a1;
+  w.b1 = L.b1;
+  w.q2 = L.q2;
+  w.a2 = L.a2;
   w.b2 = L.b2;
   return w;
 }
@@ -416,7 +480,7 @@ int expected_active(int E, int k, int T) {
 // Decode fast path (T <= kMaxRouteTokens): fused routing + permutation, then
 // the two expert kernels, all chained with programmatic dependent launch; the
 // weighted combine is done by the mlp2 kernel.
-int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
+int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bool mxf) {
   const oxg_moe_dims &d = L.dims;
   const oxg::MoeDeviceWeights w = device_weights(L);
   const int exp_active = expected_active(d.n_experts, d.top_k, T);
@@ -428,7 +492,7 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   sched.bands2 = oxg::decode_bands(d.hidden, exp_active, ctx->n_sms);
   sched.n_sms = ctx->n_sms;
   sched.pdl = true;
-  const int n_bands = sched.bands2;
+  const int n_bands = mxf ? 4 * ((d.hidden + 127) / 128) : sched.bands2;
   if (n_bands > kMaxBands) return fail(ctx, OXG_ERR_UNSUPPORTED, "too many row bands (%d)", n_bands);
   oxg::RouteSmallArgs ra{};
   ra.x = x;
@@ -451,8 +515,41 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
   ra.done = ctx->ws.done;
   ra.band_done = ctx->ws.band_done;
   ra.n_bands = n_bands;
+  if (mxf) {
+    ra.xq = ctx->ws.xq;
+    ra.xsf = ctx->ws.xsf;
+  }
   OXG_CUDA(ctx, launch(ctx, "route_small", [&] { return oxg::launch_route_small(ra, ctx->stream, true); }),
            "route_small launch");
+  if (mxf) {
+    const oxg::MxfWeights mw = mxf_weights(L);
+    oxg::MxfScratch ms{};
+    ms.active = ctx->ws.active;
+    ms.n_active = ctx->ws.n_active;
+    ms.counts = ctx->ws.counts;
+    ms.offsets = ctx->ws.offsets;
+    ms.idx = ctx->ws.idx;
+    ms.slot_pos = ctx->ws.slot_pos;
+    ms.wts = ctx->ws.wts;
+    ms.xq = ctx->ws.xq;
+    ms.xsf = ctx->ws.xsf;
+    ms.hq = ctx->ws.hq;
+    ms.hsf = ctx->ws.hsf;
+    ms.y_slot = ctx->ws.y_slot;
+    ms.band_done = ctx->ws.band_done;
+    ms.y = y;
+    ms.err = ctx->ws.err;
+    OXG_CUDA(ctx, launch(ctx, "mxf_mlp1", [&] {
+               return oxg::launch_mxf_mlp1(mw, ms, T, ctx->n_sms, true, ctx->stream);
+             }),
+             "mxf mlp1 launch");
+    OXG_CUDA(ctx, launch(ctx, "mxf_mlp2", [&] {
+               return oxg::launch_mxf_mlp2(mw, ms, T, ctx->n_sms, true, ctx->stream);
+             }),
+             "mxf mlp2 launch");
+    ctx->prefill_pending = true;  // the kernels report wait timeouts in the error word
+    return OXG_OK;
+  }
   OXG_CUDA(ctx, launch(ctx, "moe_mlp1_decode", [&] {
              return oxg::launch_moe_mlp1_sched(w, x, ctx->ws.perm, ctx->ws.sigma, ctx->ws.idx,
                                                ctx->ws.counts, ctx->ws.offsets, sched, T, ctx->ws.h,
@@ -470,12 +567,62 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
 
 // Prefill path: routing and permutation, the slot-ordered f16 activations,
 // the two tcgen05 grouped GEMMs and the weighted combine.
-int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) {
+int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bool mxf) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
   bool ranked = false;
   int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked);
   if (rc) return rc;
+  if (mxf) {
+    // block-scaled path: padded positions with the E4M3 x terms, the two
+    // tcgen05 block-scaled GEMMs, the combine
+    const oxg::ScatterTerms terms{ctx->ws.pxq, ctx->ws.pxsf, ctx->ws.rows_cap};
+    if (ranked) {
+      OXG_CUDA(ctx, launch(ctx, "scatter_e4m3", [&] {
+                 return oxg::launch_scatter(ctx->ws.cta_hist, oxg::router_mma_ctas(T), ctx->ws.idx,
+                                            ctx->ws.local_rank, T, d.top_k, d.n_experts, ctx->ws.counts,
+                                            ctx->ws.offsets, ctx->ws.perm, ctx->ws.slot_pos, x, ctx->ws.sigma,
+                                            d.hidden, nullptr, nullptr, ctx->stream, &terms);
+               }),
+               "scatter launch");
+    } else {
+      OXG_CUDA(ctx, launch(ctx, "permute", [&] {
+                 return oxg::launch_permute(ctx->ws.idx, S, d.n_experts, ctx->ws.counts, ctx->ws.offsets,
+                                            ctx->ws.perm, ctx->ws.slot_pos, ctx->stream, 128);
+               }),
+               "permute launch");
+      OXG_CUDA(ctx, launch(ctx, "gather_e4m3", [&] {
+                 return oxg::launch_gather_e4m3(x, ctx->ws.slot_pos, S, d.top_k, d.hidden, terms, ctx->stream);
+               }),
+               "gather launch");
+    }
+    oxg::MxfPrefillIO io{};
+    io.counts = ctx->ws.counts;
+    io.offsets = ctx->ws.offsets;
+    io.xq = ctx->ws.pxq;
+    io.xsf = ctx->ws.pxsf;
+    io.hq = ctx->ws.phq;
+    io.hsf = ctx->ws.phsf;
+    io.rows_cap = ctx->ws.rows_cap;
+    io.y_slot = ctx->ws.y_slot;
+    io.err = ctx->ws.err;
+    const oxg::MxfWeights mw = mxf_weights(L);
+    OXG_CUDA(ctx, launch(ctx, "mxf_gemm1", [&] {
+               return oxg::launch_mxf_prefill(mw, L.p1, io, 1, ctx->n_sms, ctx->stream);
+             }),
+             "mxf gemm1 launch");
+    OXG_CUDA(ctx, launch(ctx, "mxf_gemm2", [&] {
+               return oxg::launch_mxf_prefill(mw, L.p2, io, 2, ctx->n_sms, ctx->stream);
+             }),
+             "mxf gemm2 launch");
+    OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+               return oxg::launch_combine(ctx->ws.y_slot, ctx->ws.slot_pos, ctx->ws.wts, T, d.hidden, d.top_k, y,
+                                          ctx->stream);
+             }),
+             "combine launch");
+    ctx->prefill_pending = true;
+    return OXG_OK;
+  }
   if ((rc = sort_slots(ctx, L, x, T, ranked, true))) return rc;
   const oxg::MoeDeviceWeights w = device_weights(L);
   oxg::PrefillIO io{};
@@ -510,9 +657,16 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y) 
 int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, int mode) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
+  const bool mxf_prefill = L.mxf_ok && oxg::mxf_prefill_supported(d.hidden, d.intermediate, d.n_experts);
+  if ((mode == OXG_MODE_MXF4 && T > oxg::kMaxMxfTokens) ||
+      (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && mxf_prefill))
+    return forward_prefill(ctx, L, x, T, y, true);
   if (mode == OXG_MODE_PREFILL || (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && L.prefill_ok))
-    return forward_prefill(ctx, L, x, T, y);
-  if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y);
+    return forward_prefill(ctx, L, x, T, y, false);
+  const bool mxf = mode == OXG_MODE_MXF4 ||
+                   (mode == OXG_MODE_AUTO && L.mxf_ok &&
+                    oxg::mxf_decode_supported(d.hidden, d.intermediate, T, d.top_k));
+  if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y, mxf);
   bool ranked = false;
   int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked);
   if (rc) return rc;
@@ -569,8 +723,18 @@ int check_forward_args(oxg_ctx *ctx, int layer, const void *x, int T, const void
                 layer, L->expert_begin, L->expert_begin + L->expert_count);
   if (T < 0) return fail(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0, got %d", T);
   if (T > 0 && (!x || !y)) return fail(ctx, OXG_ERR_INVALID_ARG, "x and y must be non-NULL");
-  if (mode != OXG_MODE_AUTO && mode != OXG_MODE_DECODE && mode != OXG_MODE_PREFILL)
+  if (mode != OXG_MODE_AUTO && mode != OXG_MODE_DECODE && mode != OXG_MODE_PREFILL &&
+      mode != OXG_MODE_MXF4)
     return fail(ctx, OXG_ERR_INVALID_ARG, "unknown mode %d", mode);
+  if (mode == OXG_MODE_MXF4 &&
+      (!L->mxf_ok ||
+       (T <= oxg::kMaxMxfTokens
+            ? !oxg::mxf_decode_supported(L->dims.hidden, L->dims.intermediate, T, L->dims.top_k)
+            : !oxg::mxf_prefill_supported(L->dims.hidden, L->dims.intermediate, L->dims.n_experts))))
+    return fail(ctx, OXG_ERR_UNSUPPORTED,
+                "MXF4 mode needs hidden and intermediate multiples of 64 (>= 128), at most 256 experts and no "
+                "E8M0 scale 255; got n_tokens %d, scales in [%u, %u]",
+                T, L->scale_min, L->scale_max);
   if (mode == OXG_MODE_PREFILL && !L->prefill_ok)
     return fail(ctx, OXG_ERR_UNSUPPORTED,
                 "prefill mode needs hidden and intermediate multiples of 64 and E8M0 scales "
@@ -760,6 +924,12 @@ int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe
   };
   const size_t o_rw = take(n_rw), o_rb = take(n_rb), o_w1 = take(n_w1), o_s1 = take(n_s1),
                o_b1 = take(n_b1), o_w2 = take(n_w2), o_s2 = take(n_s2), o_b2 = take(n_b2);
+  const size_t n_a1 = oxg::sf_atoms_bytes((int)E, (int)(2 * I), (int)H, 128);
+  const size_t n_a2 = oxg::sf_atoms_bytes((int)E, (int)H, (int)I, 128);
+  const size_t n_p1 = oxg::sf_atoms_bytes((int)E, (int)(2 * I), (int)H, oxg::kMxfPrefillTileN);
+  const size_t n_p2 = oxg::sf_atoms_bytes((int)E, (int)H, (int)I, oxg::kMxfPrefillTileN);
+  const size_t o_q1 = take(n_w1 + 64), o_a1 = take(n_a1), o_q2 = take(n_w2 + 64), o_a2 = take(n_a2);
+  const size_t o_p1 = take(n_p1), o_p2 = take(n_p2);
   const size_t stage_bytes = n_w1 > n_w2 ? n_w1 : n_w2;
 
   if ((size_t)layer >= ctx->layers.size()) ctx->layers.resize(layer + 1);
@@ -785,6 +955,12 @@ int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe
   L.w2 = (uint8_t *)(base + o_w2);
   L.s2 = (uint8_t *)(base + o_s2);
   L.b2 = (uint16_t *)(base + o_b2);
+  L.q1 = (uint8_t *)(base + o_q1);
+  L.a1 = (uint8_t *)(base + o_a1);
+  L.q2 = (uint8_t *)(base + o_q2);
+  L.a2 = (uint8_t *)(base + o_a2);
+  L.p1 = (uint8_t *)(base + o_p1);
+  L.p2 = (uint8_t *)(base + o_p2);
   cudaStream_t s = ctx->stream;
   // the shard's slices of the caller's arrays (all experts, expert-major)
   const uint8_t *w1_src = (const uint8_t *)w->w1_blocks + (size_t)eb * 2 * I * (H / 2);
@@ -802,12 +978,24 @@ int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe
     if ((e = cudaMemcpyAsync(L.b2, b2_src, n_b2, cudaMemcpyDefault, s))) return e;
     if ((e = cudaMemcpyAsync(stage, w1_src, n_w1, cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w1, E * 2 * I, (int)H, s))) return e;
+    if ((e = cudaMemcpyAsync(L.q1, stage, n_w1, cudaMemcpyDeviceToDevice, s))) return e;
+    if ((e = cudaMemsetAsync(L.q1 + n_w1, 0, 64, s))) return e;
     if ((e = cudaMemcpyAsync(stage, s1_src, E * 2 * I * (H / 32), cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s1, E * 2 * I, (int)H, s))) return e;
+    if ((e = oxg::launch_sf_atoms((const uint8_t *)stage, (int)E, (int)(2 * I), (int)H, 128, L.a1, s))) return e;
+    if ((e = oxg::launch_sf_atoms((const uint8_t *)stage, (int)E, (int)(2 * I), (int)H, oxg::kMxfPrefillTileN,
+                                  L.p1, s)))
+      return e;
     if ((e = cudaMemcpyAsync(stage, w2_src, n_w2, cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_relayout_codes((const uint8_t *)stage, L.w2, E * H, (int)I, s))) return e;
+    if ((e = cudaMemcpyAsync(L.q2, stage, n_w2, cudaMemcpyDeviceToDevice, s))) return e;
+    if ((e = cudaMemsetAsync(L.q2 + n_w2, 0, 64, s))) return e;
     if ((e = cudaMemcpyAsync(stage, s2_src, E * H * (I / 32), cudaMemcpyDefault, s))) return e;
     if ((e = oxg::launch_pad_scales((const uint8_t *)stage, L.s2, E * H, (int)I, s))) return e;
+    if ((e = oxg::launch_sf_atoms((const uint8_t *)stage, (int)E, (int)H, (int)I, 128, L.a2, s))) return e;
+    if ((e = oxg::launch_sf_atoms((const uint8_t *)stage, (int)E, (int)H, (int)I, oxg::kMxfPrefillTileN, L.p2,
+                                  s)))
+      return e;
     // scale range over both matrices (padding bytes are zero and ignored)
     const unsigned init[2] = {255u, 0u};
     if ((e = cudaMemcpyAsync(stage, init, sizeof(init), cudaMemcpyHostToDevice, s))) return e;
@@ -820,6 +1008,7 @@ int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe
     L.scale_max = mm[1];
     L.prefill_ok = H % 64 == 0 && I % 64 == 0 &&
                    (mm[1] == 0u || (mm[0] >= 104u && mm[1] <= 140u));
+    L.mxf_ok = H % 64 == 0 && I % 64 == 0 && H >= 128 && I >= 128 && mm[1] <= 254u;
     return cudaSuccess;
   };
   st = body();

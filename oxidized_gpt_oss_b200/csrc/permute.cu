@@ -12,6 +12,7 @@
 // each warp and a per-expert prefix over the 32 warps.
 #include "common.cuh"
 #include "kernels.h"
+#include "mxf.cuh"
 
 namespace oxg {
 namespace {
@@ -21,7 +22,7 @@ constexpr int kPermMaxExperts = 256;
 
 __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     const int32_t *__restrict__ idx, int n_slots, int E, int32_t *__restrict__ counts,
-    int32_t *__restrict__ offsets, int32_t *__restrict__ perm, int32_t *__restrict__ slot_pos) {
+    int32_t *__restrict__ offsets, int32_t *__restrict__ perm, int32_t *__restrict__ slot_pos, int pad) {
   __shared__ int hist[kPermMaxExperts];
   __shared__ int base[kPermMaxExperts];
   __shared__ int chunk_total[kPermMaxExperts];
@@ -40,7 +41,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
       offsets[e] = run;
       base[e] = run;
       counts[e] = hist[e];
-      run += hist[e];
+      run += (hist[e] + pad - 1) / pad * pad;
     }
     offsets[E] = run;
   }
@@ -88,6 +89,54 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
 // which is exactly the stable order permute_kernel produces. kScatterSub CTAs
 // share each router CTA's slots; a warp per slot also copies the token's row
 // into the prefill operand (f16 x * 2^-sigma) when xp is given.
+// One token row x (bf16, H elements, 16-byte aligned) as the block-scaled
+// operand row p: two E4M3 terms in planes xq and xq + plane (row stride H)
+// and their scale bytes in the atoms of row tile p / 128 (planes xsf and
+// xsf + sf_plane); blocks past H in the last 128-wide k-tile get scale 0.
+// One warp; a 32-element block is 4 lanes' 8-element chunks.
+__device__ __forceinline__ void stage_row_e4m3(const uint16_t *__restrict__ src, uint8_t *__restrict__ xq,
+                                               size_t plane, uint8_t *__restrict__ xsf, size_t sf_plane,
+                                               int p, int H, int lane) {
+  const int nch = H / 8, k_tiles = (H + mxf::kTileK - 1) / mxf::kTileK;
+  const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+  uint8_t *arow = xsf + (size_t)(p >> 7) * k_tiles * mxf::kAtomBytes;
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const int c = c0 + lane;
+    const bool ok = c < nch;
+    const uint4 v = ok ? s4[c] : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t mx = 0u;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) mx = max(mx, max((w4[u] << 16) & 0x7FFFFFFFu, w4[u] & 0x7FFF0000u));
+    mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+    if (!ok) continue;
+    const int sb = mxf::term_scale_byte(mx);
+    uint32_t hi[2], lo[2];
+#pragma unroll
+    for (int u = 0; u < 4; u += 2) {
+      uint32_t t0[2], t1[2];
+      mxf::split_terms2<2>(bf16_to_f32(w4[u] & 0xFFFFu), bf16_to_f32(w4[u] >> 16), sb, t0);
+      mxf::split_terms2<2>(bf16_to_f32(w4[u + 1] & 0xFFFFu), bf16_to_f32(w4[u + 1] >> 16), sb, t1);
+      hi[u >> 1] = t0[0] | (t1[0] << 16);
+      lo[u >> 1] = t0[1] | (t1[1] << 16);
+    }
+    *reinterpret_cast<uint2 *>(xq + (size_t)p * H + 8 * c) = make_uint2(hi[0], hi[1]);
+    *reinterpret_cast<uint2 *>(xq + plane + (size_t)p * H + 8 * c) = make_uint2(lo[0], lo[1]);
+    if ((c & 3) == 0) {
+      const int kb = c >> 2;
+      const size_t o = (size_t)(kb >> 2) * mxf::kAtomBytes + mxf::atom_offset(p & 127, kb & 3);
+      arow[o] = (uint8_t)sb;
+      arow[sf_plane + o] = (uint8_t)(sb - 5);
+    }
+  }
+  for (int kb = H / 32 + lane; kb < 4 * k_tiles; kb += 32) {
+    const size_t o = (size_t)(kb >> 2) * mxf::kAtomBytes + mxf::atom_offset(p & 127, kb & 3);
+    arow[o] = 0;
+    arow[sf_plane + o] = 0;
+  }
+}
+
 constexpr int kScatterSub = 4;
 constexpr int kScatterThreads = 256;
 constexpr int kScatterTokens = 64;  // tokens per router CTA
@@ -98,7 +147,8 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
     const int32_t *__restrict__ local_rank, int T, int k, int E, int32_t *__restrict__ counts,
     int32_t *__restrict__ offsets, int32_t *__restrict__ perm, int32_t *__restrict__ slot_pos,
     const uint16_t *__restrict__ x, const int32_t *__restrict__ sigma, int H,
-    uint16_t *__restrict__ xp, float *__restrict__ pos_scale) {
+    uint16_t *__restrict__ xp, float *__restrict__ pos_scale, int pad, uint8_t *__restrict__ xq,
+    uint8_t *__restrict__ xsf, int rows_cap) {
   __shared__ int base_s[kScatterMaxE], tot_s[kScatterMaxE];
   const int c = blockIdx.x / kScatterSub, sub = blockIdx.x % kScatterSub;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -121,7 +171,7 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
         counts[e] = tot_s[e];
         offsets[e] = run;
       }
-      run += tot_s[e];
+      run += (tot_s[e] + pad - 1) / pad * pad;
     }
     if (blockIdx.x == 0) offsets[E] = run;
   }
@@ -142,6 +192,10 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
       if (lane == 0) pos_scale[p] = __uint_as_float((uint32_t)(127 + sg) << 23);
       stage_row_f16(x + (size_t)t * H, xp + (size_t)p * H, H, sg, lane);
     }
+    if (xq) {
+      const size_t sf_plane = (size_t)(rows_cap / 128) * ((H + 127) / 128) * mxf::kAtomBytes;
+      stage_row_e4m3(x + (size_t)(sl / k) * H, xq, (size_t)rows_cap * H, xsf, sf_plane, p, H, lane);
+    }
   }
 }
 
@@ -149,9 +203,36 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
 
 cudaError_t launch_permute(const int32_t *idx, int n_slots, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
-                           cudaStream_t stream) {
-  if (E > kPermMaxExperts || E <= 0) return cudaErrorInvalidValue;
-  permute_kernel<<<1, kPermThreads, 0, stream>>>(idx, n_slots, E, counts, offsets, perm, slot_pos);
+                           cudaStream_t stream, int pad) {
+  if (E > kPermMaxExperts || E <= 0 || pad < 1) return cudaErrorInvalidValue;
+  permute_kernel<<<1, kPermThreads, 0, stream>>>(idx, n_slots, E, counts, offsets, perm, slot_pos, pad);
+  return cudaGetLastError();
+}
+
+namespace {
+// The block-scaled prefill operand for routings sorted by permute_kernel
+// (padded positions): a warp per slot.
+__global__ void __launch_bounds__(256) gather_e4m3_kernel(const uint16_t *__restrict__ x,
+                                                          const int32_t *__restrict__ slot_pos, int S, int k,
+                                                          int H, uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
+                                                          int rows_cap) {
+  const int lane = threadIdx.x & 31;
+  const size_t sf_plane = (size_t)(rows_cap / 128) * ((H + 127) / 128) * mxf::kAtomBytes;
+  for (int sl = blockIdx.x * 8 + (threadIdx.x >> 5); sl < S; sl += gridDim.x * 8) {
+    const int p = slot_pos[sl];
+    if (p < 0) continue;
+    stage_row_e4m3(x + (size_t)(sl / k) * H, xq, (size_t)rows_cap * H, xsf, sf_plane, p, H, lane);
+  }
+}
+}  // namespace
+
+cudaError_t launch_gather_e4m3(const uint16_t *x, const int32_t *slot_pos, int S, int k, int H,
+                               const ScatterTerms &terms, cudaStream_t stream) {
+  if (S <= 0) return cudaSuccess;
+  if (H % 32 || ((uintptr_t)x & 15) || ((uintptr_t)terms.xq & 15) || terms.rows_cap % 128)
+    return cudaErrorInvalidValue;
+  const int blocks = (S + 7) / 8 < 4096 ? (S + 7) / 8 : 4096;
+  gather_e4m3_kernel<<<blocks, 256, 0, stream>>>(x, slot_pos, S, k, H, terms.xq, terms.xsf, terms.rows_cap);
   return cudaGetLastError();
 }
 
@@ -159,14 +240,18 @@ cudaError_t launch_scatter(const int32_t *cta_hist, int n_cta, const int32_t *id
                            const int32_t *local_rank, int T, int k, int E, int32_t *counts,
                            int32_t *offsets, int32_t *perm, int32_t *slot_pos, const uint16_t *x,
                            const int32_t *sigma, int H, uint16_t *xp, float *pos_scale,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const ScatterTerms *terms) {
   if (T == 0) return cudaSuccess;
   if (E > kScatterMaxE || E <= 0 || n_cta != (T + kScatterTokens - 1) / kScatterTokens)
     return cudaErrorInvalidValue;
   if (xp && (H % 8 || ((uintptr_t)x & 15) || ((uintptr_t)xp & 15))) return cudaErrorInvalidValue;
+  const int pad = terms ? 128 : 1;
+  if (terms && (H % 32 || ((uintptr_t)x & 15) || ((uintptr_t)terms->xq & 15) || terms->rows_cap % 128 ||
+                (size_t)T * k + (size_t)E * 127 > (size_t)terms->rows_cap))
+    return cudaErrorInvalidValue;
   scatter_kernel<<<n_cta * kScatterSub, kScatterThreads, 0, stream>>>(
       cta_hist, n_cta, idx, local_rank, T, k, E, counts, offsets, perm, slot_pos, x, sigma, H, xp,
-      pos_scale);
+      pos_scale, pad, terms ? terms->xq : nullptr, terms ? terms->xsf : nullptr, terms ? terms->rows_cap : 0);
   return cudaGetLastError();
 }
 

@@ -17,6 +17,7 @@
 // kernel. The counter is left at zero for the next call.
 #include "common.cuh"
 #include "kernels.h"
+#include "mxf.cuh"
 
 namespace oxg {
 namespace {
@@ -76,6 +77,41 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) route_small_kernel(RouteSma
           const uint32_t m2 = max((q[i].z << 16) & 0x7FFFFFFFu, q[i].z & 0x7FFF0000u);
           const uint32_t m3 = max((q[i].w << 16) & 0x7FFFFFFFu, q[i].w & 0x7FFF0000u);
           m = max(m, max(max(m0, m1), max(m2, m3)));
+        }
+      }
+    }
+    // x as two E4M3 terms per 32-element block (4 lanes hold one block):
+    // chunk iteration i of every token is done by the CTA of expert i mod E
+    if (a.xq) {
+#pragma unroll
+      for (int i = 0; i < kMaxChunks; ++i) {
+        if (i % (int)gridDim.x != e) continue;
+        const int c = lane + 32 * i;
+        const uint32_t w4[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+        uint32_t mx = 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx = max(mx, max((w4[u] << 16) & 0x7FFFFFFFu, w4[u] & 0x7FFF0000u));
+        mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+        mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+        if (c < nch) {
+          const int sb = mxf::term_scale_byte(mx);
+          uint32_t hi[2], lo[2];
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            uint32_t t0[2], t1[2];
+            mxf::split_terms2<2>(bf16_to_f32(w4[u] & 0xFFFFu), bf16_to_f32(w4[u] >> 16), sb, t0);
+            mxf::split_terms2<2>(bf16_to_f32(w4[u + 1] & 0xFFFFu), bf16_to_f32(w4[u + 1] >> 16), sb, t1);
+            hi[u >> 1] = t0[0] | (t1[0] << 16);
+            lo[u >> 1] = t0[1] | (t1[1] << 16);
+          }
+          *reinterpret_cast<uint2 *>(a.xq + (size_t)(2 * t) * H + 8 * c) = make_uint2(hi[0], hi[1]);
+          *reinterpret_cast<uint2 *>(a.xq + (size_t)(2 * t + 1) * H + 8 * c) = make_uint2(lo[0], lo[1]);
+          if ((c & 3) == 0) {
+            const int kb = c >> 2;
+            uint8_t *atom = a.xsf + (size_t)(kb >> 2) * mxf::kAtomBytes;
+            atom[mxf::atom_offset(2 * t, kb & 3)] = (uint8_t)sb;
+            atom[mxf::atom_offset(2 * t + 1, kb & 3)] = (uint8_t)(sb - 5);
+          }
         }
       }
     }
