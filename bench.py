@@ -277,8 +277,10 @@ def run_moe(args, ws, rank, local):
     xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
     ys = [torch.empty((T, H), dtype=torch.float32, device=device) for _ in range(2)]
 
+    mode = {"auto": abi.OXG_MODE_AUTO, "mxf4": abi.OXG_MODE_MXF4, "f16": abi.OXG_MODE_DECODE}[args.path]
+
     def step(i):
-        layers[i % len(layers)].forward(xs[i % n_x], out=ys[i % 2])
+        layers[i % len(layers)].forward(xs[i % n_x], out=ys[i % 2], mode=mode)
 
     # distinct experts each step reads (routing is deterministic per (layer, x))
     distinct = {}
@@ -343,12 +345,12 @@ def run_moe(args, ws, rank, local):
     xh = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in xs_np]
     yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
     for i in range(args.warmup):
-        layers[i % len(layers)].forward_host(xh[i % n_x], yh)
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
     barrier(ws)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(args.steps):
-        layers[i % len(layers)].forward_host(xh[i % n_x], yh)
+        layers[i % len(layers)].forward_host(xh[i % n_x], yh, mode=mode)
     e2e_ms = (time.perf_counter() - t0) * 1e3
     barrier(ws)
     e2e_ms = max_over_ranks(e2e_ms, ws)
@@ -407,7 +409,7 @@ def run_prefill(args, ws, rank, local):
     xs_np = [synth.activations(1000 * rank + i, T, H) for i in range(n_x)]
     xs = [torch.from_numpy(x.view(np.int16)).to(device) for x in xs_np]
     y = torch.empty((T, H), dtype=torch.float32, device=device)
-    mode = abi.OXG_MODE_MXF4 if args.path == "mxf4" else abi.OXG_MODE_PREFILL
+    mode = {"auto": abi.OXG_MODE_AUTO, "mxf4": abi.OXG_MODE_MXF4, "f16": abi.OXG_MODE_PREFILL}[args.path]
     rows_done = [0]  # expert rows this rank computed (varies with the routing under EP)
 
     count_rows = [False]  # in the profiled pass: ask each step how many rows it received
@@ -636,9 +638,10 @@ def main():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
-    ap.add_argument("--path", choices=["mxf4", "f16"], default="mxf4",
-                    help="prefill expert kernels on one GPU: block-scaled (E2M1 straight into tcgen05) or the "
-                         "f16-dequant tcgen05 GEMMs")
+    ap.add_argument("--path", choices=["auto", "mxf4", "f16"], default="auto",
+                    help="expert kernels on one GPU: the library's choice, the block-scaled tcgen05 kernels "
+                         "(E2M1 straight into the tensor cores), or the f16-operand kernels (tcgen05 GEMMs for "
+                         "prefill, mma.sync for decode)")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="moe_prefill on N > 1 GPUs: exchange over peer memory in the library's kernels "
                          "(default) or by NCCL all-to-all")

@@ -52,9 +52,10 @@ typedef enum {
 enum { OXG_SCALE_E8M0 = 0, OXG_SCALE_BF16 = 1 };
 /* OXG_MODE_DECODE: the in-register-dequant mma.sync expert kernels;
  * OXG_MODE_MXF4: the block-scaled tcgen05 expert kernels (E2M1 weights and
- * E8M0 scales straight from HBM into the tensor cores; T <= 8 tokens, hidden
- * and intermediate multiples of 64, no scale byte 255). OXG_MODE_AUTO picks
- * MXF4 when it applies, then DECODE for T <= 64, else PREFILL. */
+ * E8M0 scales straight from HBM into the tensor cores: decode kernels for
+ * T <= 8 tokens, CTA-pair GEMMs above; hidden and intermediate multiples of
+ * 64, no scale byte 255). OXG_MODE_AUTO: DECODE for T <= 64; above, PREFILL
+ * when every scale is 0 or in [104, 140], else MXF4. */
 enum { OXG_MODE_AUTO = 0, OXG_MODE_DECODE = 1, OXG_MODE_PREFILL = 2, OXG_MODE_MXF4 = 3 };
 enum { OXG_PRECISION_PARITY = 0 };
 

@@ -92,8 +92,10 @@ struct RouteSmallArgs {
   int n_bands;
   // optional (block-scaled expert path): x as two E4M3 terms per element,
   // rows 2t + term of xq [2T, H], and their UE8M0 scale atoms xsf
-  // [ceil(H/128)][512] (row 2t + term, one byte per 32-element block)
+  // [ceil(H/128)][512] (row 2t + term, one byte per 32-element block), and
+  // per expert the bit mask of the tokens routed to it (T <= 32)
   uint8_t *xq, *xsf;
+  uint32_t *tok_mask;
 };
 // pdl: launch with programmatic stream serialisation (overlaps the previous
 // kernel's tail; the kernel waits for it before touching memory).
@@ -116,6 +118,7 @@ struct MxfWeights {
 };
 struct MxfScratch {
   const int32_t *active, *n_active, *counts, *offsets, *idx, *slot_pos;
+  const uint32_t *tok_mask;  // per expert: bit t set if token t is routed to it
   const float *wts;
   const uint8_t *xq, *xsf;   // from route_small
   uint8_t *hq, *hsf;         // [4 T k, I] terms, [E][ceil(I/128)][512] atoms
@@ -137,8 +140,8 @@ cudaError_t launch_mxf_mlp2(const MxfWeights &w, const MxfScratch &s, int T, int
 
 // ---- block-scaled prefill GEMMs (moe_mxf_prefill.cu) ---------------------------
 // Operand buffers: x terms [2][rows_cap][H] with atoms [2][rows_cap/128][ceil(H/128)][512]
-// (from launch_scatter / launch_gather_e4m3), h terms [3][rows_cap][I] with
-// atoms [3][rows_cap/128][ceil(I/128)][512], y_slot [rows_cap][H] f32;
+// (from launch_scatter / launch_gather_e4m3), h terms [4][rows_cap][I] with
+// atoms [4][rows_cap/128][ceil(I/128)][512], y_slot [rows_cap][H] f32;
 // counts/offsets with every expert's first position a multiple of 128.
 struct MxfPrefillIO {
   const int32_t *counts, *offsets;

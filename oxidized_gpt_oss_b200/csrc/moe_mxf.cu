@@ -12,8 +12,8 @@
 // items; each item runs the whole K of its rows:
 //   warp 0     TMA producer: per 128-wide k-step, the 128 x 128 E2M1 weight
 //              tile (8 KB from HBM), the activation tile (all tokens' E4M3
-//              terms, L2-resident), and the two 512-byte scale atoms, into a
-//              ring of shared-memory stages;
+//              terms, L2-resident), and the two 512-byte scale atoms; two
+//              k-steps per shared-memory stage, one barrier each;
 //   warp 1     TMEM owner and MMA issuer: copies the scale atoms to TMEM
 //              (tcgen05.cp) and issues 4 MMAs of M=128, N=nb, K=32 per
 //              k-step into one of two accumulator buffers;
@@ -47,7 +47,11 @@ using namespace mxf;
 
 constexpr int kThreadsM = 192;
 constexpr int kMaxStagesM = 10;
-constexpr int kSmemBudgetM = 220 * 1024;
+// k-tiles per pipeline stage: each stage's copies complete on one barrier,
+// and TMA streams markedly faster with >= 16 KB per barrier than with the
+// 8 KB of one 128 x 128 E2M1 tile (64 bytes per row)
+constexpr int kStepsPerStage = 2;
+constexpr int kSmemBudgetM = 225 * 1024;
 constexpr int kAccCols = 32;                   // one accumulator buffer (N <= 32)
 constexpr int kSfaCol = 2 * kAccCols, kSfbCol = kSfaCol + 4;
 constexpr int kTmemColsM = 128;
@@ -60,9 +64,11 @@ struct MxfDecodeArgs {
   int T, k, H, I;
   int rows;                 // weight rows per expert (2I or H)
   int row_tiles, k_tiles, k_main;
+  int sf_item_bytes;        // one item's scale atoms: k_tiles weight atoms, then k_tiles activation atoms
   int nb;                   // MMA N
   int stages, stage_bytes;
   const int32_t *active, *n_active, *counts, *offsets, *idx, *slot_pos;
+  const uint32_t *tok_mask;
   const float *wts;
   const uint8_t *sfa;       // weight scale atoms [E][row_tiles][k_tiles][512]
   const uint8_t *sfb;       // mode 1: x atoms [k_tiles][512]; mode 2: h atoms [E][k_tiles][512]
@@ -77,11 +83,15 @@ struct MxfDecodeArgs {
 };
 
 __global__ void __launch_bounds__(kThreadsM, 1)
-    mxf_decode_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a_tail,
+    mxf_decode_kernel(const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_a_tail, const __grid_constant__ CUtensorMap tm_b2,
                       const __grid_constant__ CUtensorMap tm_b, const MxfDecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  // [stages x (A tiles, B tiles)][2 item scale buffers]
+  uint8_t *sf_items = sm + a.stages * a.stage_bytes;
   __shared__ uint64_t full_[kMaxStagesM], empty_[kMaxStagesM], acc_full[2], acc_empty[2], mma_done, pair_bar[2];
+  __shared__ uint64_t ifull[2], iempty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ uint32_t pair_max[2][4][kMaxMxfTokens];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,11 +108,17 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     mbar_init(&mma_done, 1);
     mbar_init(&pair_bar[0], 2);
     mbar_init(&pair_bar[1], 2);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ifull[b], 1);
+      mbar_init(&iempty[b], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_a2);
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_a_tail);
+    prefetch_tmap(&tm_b2);
     prefetch_tmap(&tm_b);
   }
   if (warp == 1) {
@@ -127,22 +143,38 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       uint32_t ph = 0;
       int issued = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int j = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++j) {
         const int e = a.active[item / a.row_tiles], rt = item % a.row_tiles;
         const int row0 = e * a.rows + rt * kTileM;
         const int brow0 = a.mode == 1 ? 0 : 4 * a.offsets[e];
         const uint8_t *sfa = a.sfa + (size_t)(e * a.row_tiles + rt) * a.k_tiles * kAtomBytes;
         const uint8_t *sfb = a.mode == 1 ? a.sfb : a.sfb + (size_t)e * a.k_tiles * kAtomBytes;
-        for (int ks = 0; ks < a.k_tiles; ++ks) {
+        // the item's scale atoms, both operands, two bulk copies into one of
+        // two item buffers
+        const int ib = j & 1;
+        if (!(ok = mbar_wait(&iempty[ib], (((uint32_t)j >> 1) & 1u) ^ 1u, a.err, 8))) break;
+        const uint32_t half = (uint32_t)a.sf_item_bytes / 2;
+        mbar_arrive_expect_tx(&ifull[ib], 2u * half);
+        bulk_load(sf_items + ib * a.sf_item_bytes, sfa, half, &ifull[ib]);
+        bulk_load(sf_items + ib * a.sf_item_bytes + half, sfb, half, &ifull[ib]);
+        for (int kp = 0; kp < a.k_tiles;) {
+          // main k-tiles two at a time through the 3-D maps (one copy per
+          // operand), a last odd main tile alone, then the tail tile
+          const int nt = kp + 1 < a.k_main ? 2 : 1;
           if (!(ok = mbar_wait(&empty_[s], ph ^ 1u, a.err, 1))) break;
           uint8_t *st = sm + s * a.stage_bytes;
-          mbar_arrive_expect_tx(&full_[s], (uint32_t)kATileTx + b_bytes + 2u * kAtomBytes);
-          if (ks < a.k_main) tma_load_2d(st, &tm_a, &full_[s], ks * kTileK, row0);
-          else tma_load_2d(st, &tm_a_tail, &full_[s], 0, row0);
-          tma_load_2d(st + kATileBytes, &tm_b, &full_[s], ks * kTileK, brow0);
-          bulk_load(st + kATileBytes + b_bytes, sfa + (size_t)ks * kAtomBytes, kAtomBytes, &full_[s]);
-          bulk_load(st + kATileBytes + b_bytes + kAtomBytes, sfb + (size_t)ks * kAtomBytes, kAtomBytes,
-                    &full_[s]);
+          uint8_t *sb = st + kStepsPerStage * kATileBytes;
+          mbar_arrive_expect_tx(&full_[s], (uint32_t)nt * ((uint32_t)kATileTx + b_bytes));
+          if (nt == 2) {
+            tma_load_3d(st, &tm_a2, &full_[s], 0, row0, kp);
+            tma_load_3d(sb, &tm_b2, &full_[s], 0, brow0, kp);
+          } else {
+            if (kp < a.k_main) tma_load_2d(st, &tm_a, &full_[s], kp * kTileK, row0);
+            else tma_load_2d(st, &tm_a_tail, &full_[s], 0, row0);
+            tma_load_2d(sb, &tm_b, &full_[s], kp * kTileK, brow0);
+          }
+          kp += nt;
           ++issued;
           if (++s == a.stages) {
             s = 0;
@@ -168,26 +200,39 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++j) {
         const int buf = j & 1;
         if (!(ok = mbar_wait(&acc_empty[buf], (((uint32_t)j >> 1) & 1u) ^ 1u, a.err, 3))) break;
+        if (!(ok = mbar_wait(&ifull[buf], ((uint32_t)j >> 1) & 1u, a.err, 9))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * kAccCols);
-        for (int ks = 0; ks < a.k_tiles; ++ks) {
+        const uint32_t sfi = smem_addr(sf_items + buf * a.sf_item_bytes);
+        const uint32_t half = (uint32_t)a.sf_item_bytes / 2;
+        for (int kp = 0; kp < a.k_tiles;) {
+          const int n = kp + 1 < a.k_main ? 2 : 1;
           if (!(ok = mbar_wait(&full_[s], ph, a.err, 4))) break;
           tc_fence_after();
           const uint32_t st = smem_addr(sm + s * a.stage_bytes);
-          utccp_atom(sfa_t, st + kATileBytes + b_bytes);
-          utccp_atom(sfb_t, st + kATileBytes + b_bytes + kAtomBytes);
-          const uint64_t ad = desc_sw128_kmajor(st), bd = desc_sw128_kmajor(st + kATileBytes);
+          for (int i = 0; i < n; ++i) {
+            const uint32_t sa = st + i * kATileBytes;
+            const uint32_t sb = st + kStepsPerStage * kATileBytes + i * b_bytes;
+            const uint32_t sf = sfi + (uint32_t)(kp + i) * kAtomBytes;
+            utccp_atom(sfa_t, sf);
+            utccp_atom(sfb_t, sf + half);
+            const uint64_t ad = desc_sw128_kmajor(sa), bd = desc_sw128_kmajor(sb);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_mxf(d, ad + 2 * kk, bd + 2 * kk, idesc_e2m1_e4m3(kTileM, a.nb, kk, kk),
-                     sfa_t | ((uint32_t)kk << 30), sfb_t | ((uint32_t)kk << 30), (ks | kk) != 0);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_mxf(d, ad + 2 * kk, bd + 2 * kk, idesc_e2m1_e4m3(kTileM, a.nb, kk, kk),
+                       sfa_t | ((uint32_t)kk << 30), sfb_t | ((uint32_t)kk << 30), (kp | i | kk) != 0);
+          }
           umma_commit(&empty_[s]);
           if (++s == a.stages) {
             s = 0;
             ph ^= 1u;
           }
+          kp += n;
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok) {
+          umma_commit(&iempty[buf]);
+          umma_commit(&acc_full[buf]);
+        }
       }
       umma_commit(&mma_done);
       mbar_wait(&mma_done, 0, a.err, 5);
@@ -214,6 +259,8 @@ __global__ void __launch_bounds__(kThreadsM, 1)
         // ---- gate/up + SwiGLU -> 4 E4M3 terms of h for the routed tokens ----
         const float bias = bf16_to_f32(a.bias[(size_t)e * a.rows + m]);
         const int off = a.offsets[e];
+        // expert e's positions are its tokens in token order (stable grouping)
+        const uint32_t tmask = __ldg(a.tok_mask + e);
         float h[kMaxMxfTokens];
         int pos[kMaxMxfTokens];
 #pragma unroll
@@ -221,10 +268,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
           const float v = __uint_as_float(r[2 * t]) + __uint_as_float(r[2 * t + 1]) + bias;
           const float u = __shfl_down_sync(0xFFFFFFFFu, v, 1);
           h[t] = (lane & 1) ? 0.f : swiglu_clamped_fast(v, u, a.alpha, a.limit);
-          pos[t] = -1;
-          if (t < a.T)
-            for (int jj = 0; jj < a.k; ++jj)
-              if (__ldg(a.idx + t * a.k + jj) == e) pos[t] = __ldg(a.slot_pos + t * a.k + jj);
+          pos[t] = (tmask >> t) & 1u ? off + __popc(tmask & ((1u << t) - 1u)) : -1;
           uint32_t mx = __float_as_uint(h[t]) & 0x7FFFFFFFu;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
@@ -356,25 +400,51 @@ cudaError_t make_map(CUtensorMap *m, const void *base, bool e2m1, uint64_t cols,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// 3-D map over k-tiles: dims (128 elements of one k-tile, rows, k-tiles)
+// with row stride row_bytes and k-tile stride 64 bytes (E2M1) or 128 bytes;
+// box (128, box_rows, kStepsPerStage): consecutive whole k-tiles, each landing
+// as its own 128-byte-swizzled tile.
+cudaError_t make_map3(CUtensorMap *m, const void *base, bool e2m1, uint64_t rows, uint64_t row_bytes,
+                      uint64_t k_tiles, uint32_t box_rows) {
+  EncodeTiledFnM fn = encode_fn_m();
+  if (!fn) return cudaErrorNotSupported;
+  cuuint64_t dims[3] = {128u, rows, k_tiles}, strides[2] = {row_bytes, e2m1 ? 64u : 128u};
+  cuuint32_t box[3] = {128u, box_rows, (cuuint32_t)kStepsPerStage}, es[3] = {1u, 1u, 1u};
+  CUresult r = fn(m, e2m1 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+                  const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_mxf(MxfDecodeArgs &a, const uint8_t *codes, int E, const uint8_t *b_base,
                        uint64_t b_rows, int grid, bool pdl, cudaStream_t stream) {
   const int K = a.mode == 1 ? a.H : a.I;
   a.k_tiles = (K + kTileK - 1) / kTileK;
   a.k_main = K / kTileK;
   a.row_tiles = (a.rows + kTileM - 1) / kTileM;
-  a.stage_bytes = (kATileBytes + a.nb * 128 + 2 * kAtomBytes + 1023) / 1024 * 1024;
-  a.stages = std::min(kMaxStagesM, kSmemBudgetM / a.stage_bytes);
-  CUtensorMap ta, tt, tb;
+  a.stage_bytes = (kStepsPerStage * (kATileBytes + a.nb * 128) + 1023) / 1024 * 1024;
+  a.sf_item_bytes = 2 * a.k_tiles * kAtomBytes;
+  a.stages = std::min(kMaxStagesM, (kSmemBudgetM - 2 * a.sf_item_bytes) / a.stage_bytes);
+  if (a.stages < 2) return cudaErrorInvalidValue;
+  CUtensorMap ta2, ta, tt, tb2, tb;
   const uint64_t wrows = (uint64_t)E * a.rows;
   cudaError_t st = make_map(&ta, codes, true, (uint64_t)a.k_main * kTileK, wrows, (uint64_t)K / 2, kTileM);
   if (st) return st;
+  if ((st = make_map(&tb, b_base, false, (uint64_t)K, b_rows, (uint64_t)K, (uint32_t)a.nb))) return st;
   if (a.k_main < a.k_tiles)
     st = make_map(&tt, codes + (size_t)a.k_main * (kTileK / 2), true, kTileK, wrows, (uint64_t)K / 2, kTileM);
   else
     tt = ta;
   if (st) return st;
-  if ((st = make_map(&tb, b_base, false, (uint64_t)K, b_rows, (uint64_t)K, (uint32_t)a.nb))) return st;
-  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024;
+  if (a.k_main >= 2) {
+    // pairs of main k-tiles: dims (128 codes | bytes of a k-tile, rows, k-tile)
+    if ((st = make_map3(&ta2, codes, true, wrows, (uint64_t)K / 2, (uint64_t)a.k_main, kTileM))) return st;
+    if ((st = make_map3(&tb2, b_base, false, b_rows, (uint64_t)K, (uint64_t)a.k_main, (uint32_t)a.nb))) return st;
+  } else {
+    ta2 = ta;
+    tb2 = tb;
+  }
+  const size_t smem = (size_t)a.stages * a.stage_bytes + 2 * (size_t)a.sf_item_bytes + 1024;
   static bool attr_set = false;
   if (!attr_set) {
     if ((st = cudaFuncSetAttribute(mxf_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -392,7 +462,7 @@ cudaError_t launch_mxf(MxfDecodeArgs &a, const uint8_t *codes, int E, const uint
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mxf_decode_kernel, ta, tt, tb, a);
+  return cudaLaunchKernelEx(&cfg, mxf_decode_kernel, ta2, ta, tt, tb2, tb, a);
 }
 
 }  // namespace
@@ -432,6 +502,7 @@ cudaError_t launch_mxf_mlp1(const MxfWeights &w, const MxfScratch &s, int T, int
   a.offsets = s.offsets;
   a.idx = s.idx;
   a.slot_pos = s.slot_pos;
+  a.tok_mask = s.tok_mask;
   a.wts = s.wts;
   a.sfa = w.a1;
   a.sfb = s.xsf;

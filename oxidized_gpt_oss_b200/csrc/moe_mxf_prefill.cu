@@ -8,7 +8,10 @@
 // N = 192 weight rows, 96 loaded by each CTA), each side with one UE8M0
 // scale per 32 elements of K, accumulating in f32 in TMEM:
 //   GEMM1  D[slots, 192 rows of W1_e] = sum over x's 2 terms   -> bias, SwiGLU -> h terms
-//   GEMM2  D[slots, 192 rows of W2_e] = sum over h's 3 terms   -> bias -> y_slot (f32)
+//   GEMM2  D[slots, 192 rows of W2_e] = sum over h's 4 terms   -> bias -> y_slot (f32)
+// Every pipeline stage holds two activation terms with one weight tile, so
+// GEMM2 runs each 128-wide k-step as two passes (terms 0-1, then 2-3, the
+// weight tile loaded for both) and keeps four 46 KB stages in flight.
 // The activation rows of each expert start at a multiple of 128 (padded
 // positions), so a CTA's 128 rows share one scale atom per k-step.
 //
@@ -25,7 +28,7 @@
 //              buffer 1 (one TMEM lane quarter each), so each warp has two
 //              tiles' worth of MMA time for its tile. GEMM1: bias + SwiGLU
 //              on gate/up column pairs, then h (32 features per block,
-//              thread-local) as three E4M3 terms + scales for GEMM2; GEMM2:
+//              thread-local) as four E4M3 terms + scales for GEMM2; GEMM2:
 //              bias, f32 rows to y_slot.
 // Every mbarrier wait is bounded; a timeout records a code in the error word
 // and the pair winds down.
@@ -49,7 +52,8 @@ constexpr int PNH = PN / 2;            // weight rows each CTA loads
 constexpr int kEpiWarpsX = 8;
 constexpr int kThreadsX = (2 + kEpiWarpsX) * 32;
 constexpr int kTmemColsX = 512;
-constexpr int kSfaColX = 2 * PN;          // up to 3 terms x 4 columns
+constexpr int kTermsX = 2;                // activation terms per stage
+constexpr int kSfaColX = 2 * PN;          // kTermsX terms x 4 columns
 constexpr int kSfbColX = kSfaColX + 16;   // 2 atoms x 4 columns
 constexpr int kMaxExpertsX = 256;
 constexpr int kBTx = PNH * kTileK / 2;    // bytes the TMA moves for a CTA's weight half
@@ -63,7 +67,7 @@ struct MxfPrefillArgs {
   const int32_t *counts, *offsets;  // offsets padded to multiples of 128
   const uint16_t *bias;   // [E][rows]
   float alpha, limit;
-  // GEMM1 out: h terms [3][rows_cap][I], atoms [3][rows_cap/128][ceil(I/128)][512]
+  // GEMM1 out: h terms [4][rows_cap][I], atoms [4][rows_cap/128][ceil(I/128)][512]
   uint8_t *hq, *hsf;
   int I, rows_cap;
   // GEMM2 out
@@ -123,7 +127,8 @@ __global__ void __launch_bounds__(kThreadsX, 1)
     mxf_prefill_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_wt, const __grid_constant__ CUtensorMap tm_sfa,
                        const __grid_constant__ CUtensorMap tm_sfb, const MxfPrefillArgs a) {
-  constexpr int NT = GEMM == 1 ? 2 : 3;  // activation terms
+  constexpr int NT = kTermsX;             // activation terms per stage
+  constexpr int PASSES = GEMM == 1 ? 1 : 2;  // stages per k-step (x: 2 terms, h: 4)
   using S = StageX<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *tiles = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -198,7 +203,8 @@ __global__ void __launch_bounds__(kThreadsX, 1)
         const int arow = c.row0 + (int)rank * PM;
         const int wrow = c.e * a.rows + c.nt * PN + (int)rank * PNH;
         const int atile = arow / PM;
-        for (int ks = 0; ks < a.k_tiles; ++ks) {
+        for (int step = 0; step < a.k_tiles * PASSES; ++step) {
+          const int ks = step / PASSES, t0 = (step % PASSES) * NT;
           if (r > 0) {
             if (!(ok = mbar_wait_cl(&empty_[s], (r - 1) & 1, a.err, 1))) break;
             if (rank == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&empty_[s]), 1));
@@ -206,13 +212,14 @@ __global__ void __launch_bounds__(kThreadsX, 1)
           uint8_t *st = tiles + s * S::BYTES;
           if (rank == 0) mbar_arrive_expect_tx(&full_[s], S::TX_PAIR);
 #pragma unroll
-          for (int t = 0; t < NT; ++t) tma_load_3d_pair(st + t * kATileBytes, &tm_act, full_cl(s), ks * kTileK, arow, t);
+          for (int t = 0; t < NT; ++t)
+            tma_load_3d_pair(st + t * kATileBytes, &tm_act, full_cl(s), ks * kTileK, arow, t0 + t);
           if (ks < a.k_main) tma_load_2d_pair(st + S::A, &tm_w, full_cl(s), ks * kTileK, wrow);
           else tma_load_2d_pair(st + S::A, &tm_wt, full_cl(s), 0, wrow);
 #pragma unroll
           for (int t = 0; t < NT; ++t)
             tma_load_2d_pair(st + S::A + S::B + t * kAtomBytes, &tm_sfa, full_cl(s), 0,
-                             2 * ((t * rt_cap + atile) * a.k_tiles + ks));
+                             2 * (((t0 + t) * rt_cap + atile) * a.k_tiles + ks));
           tma_load_2d_pair(st + S::A + S::B + S::SFA, &tm_sfb, full_cl(s), 0,
                            4 * ((c.e * a.n_tiles + c.nt) * a.k_tiles + ks));
           last_round[s] = r;
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreadsX, 1)
         if (rr > 0 && !(ok = mbar_wait_cl(&acc_empty[buf], (rr - 1) & 1, a.err, 3))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * PN);
-        for (int ks = 0; ks < a.k_tiles; ++ks) {
+        for (int step = 0; step < a.k_tiles * PASSES; ++step) {
           if (!(ok = mbar_wait_cl(&full_[s], phase, a.err, 2))) break;
           tc_fence_after();
           const uint32_t st = smem_addr(tiles + s * S::BYTES);
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(kThreadsX, 1)
               umma_mxf_pair(d, desc_sw128_kmajor(st + t * kATileBytes) + 2 * kk, bd + 2 * kk,
                             idesc_e4m3_e2m1(2 * PM, PN, kk, kk),
                             (tmem + kSfaColX + 4 * t) | ((uint32_t)kk << 30), sfb_t | ((uint32_t)kk << 30),
-                            (ks | kk | t) != 0);
+                            (step | kk | t) != 0);
           umma_commit_pair(empty0 + (uint32_t)(s * sizeof(uint64_t)));
           if (++s == STAGES) {
             s = 0;
@@ -313,17 +320,17 @@ __global__ void __launch_bounds__(kThreadsX, 1)
           }
           if (row_ok) {
             const int sb = term_scale_byte(mx);
-            uint32_t w[3][8];
+            uint32_t w[4][8];
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
-              uint32_t t0[3], t1[3];
-              split_terms2<3>(h[i], h[i + 1], sb, t0);
-              split_terms2<3>(h[i + 2], h[i + 3], sb, t1);
+              uint32_t t0[4], t1[4];
+              split_terms2<4>(h[i], h[i + 1], sb, t0);
+              split_terms2<4>(h[i + 2], h[i + 3], sb, t1);
 #pragma unroll
-              for (int t = 0; t < 3; ++t) w[t][i >> 2] = t0[t] | (t1[t] << 16);
+              for (int t = 0; t < 4; ++t) w[t][i >> 2] = t0[t] | (t1[t] << 16);
             }
 #pragma unroll
-            for (int t = 0; t < 3; ++t) {
+            for (int t = 0; t < 4; ++t) {
               uint4 *dst = reinterpret_cast<uint4 *>(a.hq + t * plane + (size_t)p * a.I + f0);
               dst[0] = make_uint4(w[t][0], w[t][1], w[t][2], w[t][3]);
               dst[1] = make_uint4(w[t][4], w[t][5], w[t][6], w[t][7]);
@@ -331,12 +338,12 @@ __global__ void __launch_bounds__(kThreadsX, 1)
             const int fb = f0 >> 5;
             const size_t o = (size_t)(fb >> 2) * kAtomBytes + atom_offset(p & 127, fb & 3);
 #pragma unroll
-            for (int t = 0; t < 3; ++t) arow[t * sf_plane + o] = (uint8_t)(sb - 5 * t);
+            for (int t = 0; t < 4; ++t) arow[t * sf_plane + o] = (uint8_t)(sb - 5 * t);
             if (f0 + 32 == a.I)  // scale 0 for the blocks past I in the last k-tile
               for (int kb = a.I / 32; kb < 4 * kt2; ++kb) {
                 const size_t o2 = (size_t)(kb >> 2) * kAtomBytes + atom_offset(p & 127, kb & 3);
 #pragma unroll
-                for (int t = 0; t < 3; ++t) arow[t * sf_plane + o2] = 0;
+                for (int t = 0; t < 4; ++t) arow[t * sf_plane + o2] = 0;
               }
           }
         }
@@ -402,7 +409,8 @@ cudaError_t encode(CUtensorMap *m, CUtensorMapDataType ty, int rank, const void 
 template <int GEMM, int STAGES>
 cudaError_t launch_x(MxfPrefillArgs &a, const uint8_t *act, const uint8_t *act_sf, const uint8_t *codes,
                      const uint8_t *w_sf, int n_sms, cudaStream_t stream) {
-  constexpr int NT = GEMM == 1 ? 2 : 3;
+  constexpr int NT = kTermsX;
+  constexpr int PLANES = GEMM == 1 ? 2 : 4;  // activation term planes
   a.k_tiles = (a.K + kTileK - 1) / kTileK;
   a.k_main = a.K / kTileK;
   a.n_tiles = (a.rows + PN - 1) / PN;
@@ -410,7 +418,7 @@ cudaError_t launch_x(MxfPrefillArgs &a, const uint8_t *act, const uint8_t *act_s
   CUtensorMap t_act, t_w, t_wt, t_sfa, t_sfb;
   cudaError_t st;
   {
-    cuuint64_t dims[3] = {(cuuint64_t)a.K, (cuuint64_t)a.rows_cap, (cuuint64_t)NT};
+    cuuint64_t dims[3] = {(cuuint64_t)a.K, (cuuint64_t)a.rows_cap, (cuuint64_t)PLANES};
     cuuint64_t strides[2] = {(cuuint64_t)a.K, (cuuint64_t)a.K * a.rows_cap};
     cuuint32_t box[3] = {128u, (cuuint32_t)PM, 1u};
     if ((st = encode(&t_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -433,8 +441,8 @@ cudaError_t launch_x(MxfPrefillArgs &a, const uint8_t *act, const uint8_t *act_s
     }
   }
   {
-    // activation scale atoms [NT][rows_cap/128][k_tiles][512] as 256-byte rows
-    cuuint64_t dims[2] = {256u, (cuuint64_t)NT * (a.rows_cap / PM) * a.k_tiles * 2};
+    // activation scale atoms [PLANES][rows_cap/128][k_tiles][512] as 256-byte rows
+    cuuint64_t dims[2] = {256u, (cuuint64_t)PLANES * (a.rows_cap / PM) * a.k_tiles * 2};
     cuuint64_t strides[1] = {256u};
     cuuint32_t box[2] = {256u, 2u};
     if ((st = encode(&t_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act_sf, dims, strides, box,
@@ -505,7 +513,7 @@ cudaError_t launch_mxf_prefill(const MxfWeights &w, const uint8_t *p_atoms, cons
   a.K = w.I;
   a.rows = w.H;
   a.bias = w.b2;
-  return launch_x<2, 3>(a, io.hq, io.hsf, w.q2, p_atoms, n_sms, stream);
+  return launch_x<2, 4>(a, io.hq, io.hsf, w.q2, p_atoms, n_sms, stream);
 }
 
 }  // namespace oxg

@@ -69,6 +69,7 @@ struct Scratch {
   // block-scaled decode operands: x and h as E4M3 terms and their scale
   // atoms; zeroed whenever the layout changes (no stale NaN scale bytes)
   uint8_t *xq = nullptr, *xsf = nullptr, *hq = nullptr, *hsf = nullptr;
+  uint32_t *tok_mask = nullptr;
   size_t xq_bytes = 0, xsf_bytes = 0, hq_bytes = 0, hsf_bytes = 0;
   size_t layout_key = 0;
   // block-scaled prefill operands (padded positions, rows_cap rows per plane)
@@ -255,8 +256,10 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_idx = take(S * 4), *p_wts = take(S * 4), *p_sigma = take((size_t)T * 4);
   char *p_logits = take((size_t)T * d.n_experts * 4);
   char *p_counts = take((size_t)d.n_experts * 4), *p_offsets = take(((size_t)d.n_experts + 1) * 4);
-  char *p_perm = take(S * 4), *p_slot = take(S * 4);
+  // positions run up to rows_cap when each expert's first position is padded
+  // to a multiple of 128 (block-scaled prefill)
   const int rows_cap = oxg::mxf_rows_cap((int)S, d.n_experts);
+  char *p_perm = take(std::max(S, (size_t)rows_cap) * 4), *p_slot = take(S * 4);
   char *p_h = take(S * d.intermediate * 4), *p_y = take(std::max(S, (size_t)rows_cap) * d.hidden * 4);
   char *p_xs = take((size_t)T * d.hidden * 2), *p_ys = take((size_t)T * d.hidden * 4);
   char *p_xp = take(S * d.hidden * 2), *p_hhi = take(S * d.intermediate * 2);
@@ -266,15 +269,17 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   const size_t hq_b = 4 * S * d.intermediate;
   const size_t hsf_b = (size_t)d.n_experts * ((d.intermediate + 127) / 128) * 512;
   char *p_xq = take(xq_b), *p_xsf = take(xsf_b), *p_hq = take(hq_b), *p_hsf = take(hsf_b);
+  char *p_tmask = take((size_t)d.n_experts * 4);
   const size_t rt = (size_t)rows_cap / 128, kt1 = (d.hidden + 127) / 128, kt2 = (d.intermediate + 127) / 128;
   char *p_pxq = take(2 * (size_t)rows_cap * d.hidden), *p_pxsf = take(2 * rt * kt1 * 512);
-  char *p_phq = take(3 * (size_t)rows_cap * d.intermediate), *p_phsf = take(3 * rt * kt2 * 512);
+  char *p_phq = take(4 * (size_t)rows_cap * d.intermediate), *p_phsf = take(4 * rt * kt2 * 512);
   if (s && base) {
     s->pxq = (uint8_t *)p_pxq;
     s->pxsf = (uint8_t *)p_pxsf;
     s->phq = (uint8_t *)p_phq;
     s->phsf = (uint8_t *)p_phsf;
     s->rows_cap = rows_cap;
+    s->tok_mask = (uint32_t *)p_tmask;
     s->xq = (uint8_t *)p_xq;
     s->xsf = (uint8_t *)p_xsf;
     s->hq = (uint8_t *)p_hq;
@@ -518,6 +523,7 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
   if (mxf) {
     ra.xq = ctx->ws.xq;
     ra.xsf = ctx->ws.xsf;
+    ra.tok_mask = ctx->ws.tok_mask;
   }
   OXG_CUDA(ctx, launch(ctx, "route_small", [&] { return oxg::launch_route_small(ra, ctx->stream, true); }),
            "route_small launch");
@@ -530,6 +536,7 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
     ms.offsets = ctx->ws.offsets;
     ms.idx = ctx->ws.idx;
     ms.slot_pos = ctx->ws.slot_pos;
+    ms.tok_mask = ctx->ws.tok_mask;
     ms.wts = ctx->ws.wts;
     ms.xq = ctx->ws.xq;
     ms.xsf = ctx->ws.xsf;
@@ -657,15 +664,17 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, 
 int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, int mode) {
   const oxg_moe_dims &d = L.dims;
   const int S = T * d.top_k;
+  // AUTO: the measured-faster kernels first. Prefill: the f16 tcgen05 GEMMs
+  // when every scale is f16-exact, else the block-scaled GEMMs (any scale).
+  // Decode: the mma.sync kernels (the block-scaled decode kernels are
+  // selected with OXG_MODE_MXF4).
   const bool mxf_prefill = L.mxf_ok && oxg::mxf_prefill_supported(d.hidden, d.intermediate, d.n_experts);
   if ((mode == OXG_MODE_MXF4 && T > oxg::kMaxMxfTokens) ||
-      (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && mxf_prefill))
+      (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && !L.prefill_ok && mxf_prefill))
     return forward_prefill(ctx, L, x, T, y, true);
   if (mode == OXG_MODE_PREFILL || (mode == OXG_MODE_AUTO && T > oxg::kMaxRouteTokens && L.prefill_ok))
     return forward_prefill(ctx, L, x, T, y, false);
-  const bool mxf = mode == OXG_MODE_MXF4 ||
-                   (mode == OXG_MODE_AUTO && L.mxf_ok &&
-                    oxg::mxf_decode_supported(d.hidden, d.intermediate, T, d.top_k));
+  const bool mxf = mode == OXG_MODE_MXF4;
   if (T <= oxg::kMaxRouteTokens) return forward_small(ctx, L, x, T, y, mxf);
   bool ranked = false;
   int rc = route(ctx, L, x, T, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits, &ranked);

@@ -218,6 +218,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) route_small_kernel(RouteSma
     a.perm[p] = s;
     a.slot_pos[s] = p;
   }
+  // per expert, the tokens routed to it as a bit mask (block-scaled path, T <= 32)
+  if (a.tok_mask && T <= 32)
+    for (int x = tid; x < E; x += blockDim.x) {
+      uint32_t m = 0u;
+      for (int s2 = 0; s2 < S; ++s2) m |= idx_s[s2] == x ? 1u << (s2 / k) : 0u;
+      a.tok_mask[x] = m;
+    }
   for (int b = tid; b < a.n_bands; b += blockDim.x) a.band_done[b] = 0u;
   if (tid == 0) *a.done = 0u;
   __threadfence();

@@ -145,6 +145,14 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, ui
       "l"(tmap), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, uint64_t *bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(smem_dst)),
+      "l"(tmap), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 // Tile load into this CTA's shared memory whose completion (transaction
 // bytes) is signalled on the mbarrier at shared::cluster address `bar_cl`,
 // which may belong to the other CTA of the pair (cta_group::2).

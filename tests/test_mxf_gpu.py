@@ -24,6 +24,7 @@ def _run(d, x_np, mode):
     layer = MoELayer(d)
     x = torch.from_numpy(x_np.view(np.int16)).cuda()
     y = layer.forward(x, mode=mode)
+    layer.ctx.sync()  # raises if a kernel reported a pipeline timeout
     idx, w, _ = layer.route(x)
     torch.cuda.synchronize()
     return layer, y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy()
@@ -83,19 +84,29 @@ def test_wide_scales_and_activation_range(cuda_ctx):
     assert np.all(rel < 1e-3), rel
 
 
-def test_deterministic_and_auto_picks_it(cuda_ctx):
+def test_deterministic_and_auto_prefill_fallback(cuda_ctx):
     import torch
     d = synth.moe_layer(seed=41, hidden=512, intermediate=384, n_experts=16, top_k=4)
     x = synth.activations(41, 8, 512)
     layer, y1, _, _ = _run(d, x, abi.OXG_MODE_MXF4)
     xt = torch.from_numpy(x.view(np.int16)).cuda()
+    y2 = layer.forward(xt, mode=abi.OXG_MODE_MXF4).cpu().numpy()
+    assert np.array_equal(y1, y2)
+    # scales outside the f16-exact window: AUTO prefill takes the block-scaled GEMMs
+    d = synth.moe_layer(seed=42, hidden=256, intermediate=256, n_experts=16, top_k=4, scale_range=(95, 145))
+    x = synth.activations(42, 96, 256)
+    layer, y3, idx, w = _run(d, x, abi.OXG_MODE_AUTO)
     layer.ctx.profile(True)
     layer.ctx.profile_reset()
-    y2 = layer.forward(xt).cpu().numpy()  # AUTO
-    launched = {n: layer.ctx.profile_read(n)[1] for n in ("mxf_mlp1", "mxf_mlp2", "moe_mlp1_decode")}
+    layer.forward(torch.from_numpy(x.view(np.int16)).cuda())
+    launched = {n: layer.ctx.profile_read(n)[1] for n in ("mxf_gemm1", "mxf_gemm2", "moe_mlp1_prefill")}
     layer.ctx.profile(False)
-    assert np.array_equal(y1, y2)
-    assert launched == {"mxf_mlp1": 1, "mxf_mlp2": 1, "moe_mlp1_decode": 0}, launched
+    assert launched == {"mxf_gemm1": 1, "mxf_gemm2": 1, "moe_mlp1_prefill": 0}, launched
+    # weights up to 6 * 2^18: outputs ~1e8, so the bar is relative here
+    y_ref = oracle.moe_forward_spec(oracle.Weights(d), x, idx=idx, wts=w, acc64=True)
+    rel = np.abs(y3 - y_ref).max(axis=1) / np.maximum(np.abs(y_ref).max(axis=1), 1e-30)
+    assert np.all(rel < 1e-3), rel.max()
+    assert np.abs(y3 - y_ref).sum() / np.abs(y_ref).sum() <= MEAN_REL
 
 
 def test_unsupported_requests_are_refused(cuda_ctx):
@@ -106,9 +117,12 @@ def test_unsupported_requests_are_refused(cuda_ctx):
     x = torch.from_numpy(synth.activations(51, 4, 128).view(np.int16)).cuda()
     with pytest.raises(abi.OxgError):
         layer.forward(x, mode=abi.OXG_MODE_MXF4)
+    # an E8M0 scale of 255 (NaN as a block scale; +inf in the reference's dequantisation)
     d = synth.moe_layer(seed=52, hidden=128, intermediate=128, n_experts=8, top_k=4)
+    d["w2_scales"] = d["w2_scales"].copy()
+    d["w2_scales"][3, 5, 1] = 255
     layer = MoELayer(d)
-    x = torch.from_numpy(synth.activations(52, 9, 128).view(np.int16)).cuda()  # T > 8
+    x = torch.from_numpy(synth.activations(52, 4, 128).view(np.int16)).cuda()
     with pytest.raises(abi.OxgError):
         layer.forward(x, mode=abi.OXG_MODE_MXF4)
 
