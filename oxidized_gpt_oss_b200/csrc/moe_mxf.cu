@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     int j = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
       const int buf = j & 1;
-      if (!mbar_wait(&acc_full[buf], ((uint32_t)j >> 1) & 1u, a.err, 6)) break;
+      // every lane waits; the warp leaves together if any lane timed out
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], ((uint32_t)j >> 1) & 1u, a.err, 6))) break;
       tc_fence_after();
       uint32_t r[32];
       tmem_ld_32_async(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAccCols), r);
@@ -278,7 +279,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
         // run at most one item ahead of its partner, so two buffers suffice)
         __syncwarp();
         if (lane == 0) mbar_arrive(&pair_bar[q >> 1]);
-        if (!mbar_wait(&pair_bar[q >> 1], (uint32_t)j & 1u, a.err, 7)) break;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&pair_bar[q >> 1], (uint32_t)j & 1u, a.err, 7))) break;
         const int fl = ml >> 1;                  // feature inside the tile's 64
         const int f = rt * (kTileM / 2) + fl;    // intermediate feature
         const int fb = f >> 5;                   // its 32-feature block
