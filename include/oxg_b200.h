@@ -149,6 +149,13 @@ OXG_API int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int 
 OXG_API int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int n_tokens,
                                  float *y_host, int mode, int precision);
 
+/* Tokens per chunk for oxg_moe_forward_host on batches of at least twice
+ * that many tokens: the chunks' host->device copies, kernels and
+ * device->host copies overlap on three streams (results per token are the
+ * same as one forward). 0: automatic (2048), < 0: never chunk, else > 64.
+ * No counterpart in the reference (its forward runs on the host). */
+OXG_API int oxg_ctx_set_host_chunk(oxg_ctx *ctx, int tokens);
+
 /* Routing tap (src/moe.rs:40-73): idx_dev [n_tokens, k] int32 expert ids in
  * selection order, w_dev [n_tokens, k] f32 softmax weights; logits_dev
  * [n_tokens, E] f32 may be NULL. */

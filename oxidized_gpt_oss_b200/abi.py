@@ -64,6 +64,7 @@ SIGNATURES = {
     "oxg_last_error": (ctypes.c_char_p, [_CTX]),
     "oxg_ctx_set_stream": (_I, [_CTX, _P]),
     "oxg_ctx_get_stream": (_P, [_CTX]),
+    "oxg_ctx_set_host_chunk": (_I, [_CTX, _I]),
     "oxg_sync": (_I, [_CTX]),
     "oxg_dequant_mxfp4": (_I, [_CTX, _P, _SZ, _P, _SZ, _I, _SZ, _SZ, _P]),
     "oxg_swiglu": (_I, [_CTX, _P, _P, _SZ, ctypes.c_float, ctypes.c_float, _P]),
@@ -145,6 +146,10 @@ class Context:
 
     def sync(self) -> None:
         check(self.lib.oxg_sync(self.handle), self.handle)
+
+    def set_host_chunk(self, tokens: int) -> None:
+        """Tokens per chunk of host-buffer forwards (0: automatic, < 0: off)."""
+        check(self.lib.oxg_ctx_set_host_chunk(self.handle, int(tokens)), self.handle)
 
     def profile(self, on: bool = True) -> None:
         check(self.lib.oxg_profile_enable(self.handle, int(on)), self.handle)

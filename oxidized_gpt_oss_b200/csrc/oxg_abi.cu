@@ -50,6 +50,11 @@ struct Layer {
 // Completion counters at the start of the scratch: zeroed when the scratch is
 // allocated and left at zero by every forward that uses them.
 constexpr int kMaxBands = 1024;
+// Tokens per chunk of a host-buffer forward (oxg_moe_forward_host) when the
+// caller has not set one: at 2048 tokens a gpt-oss-20b chunk still runs the
+// prefill GEMMs near their full rate, and the first copy in and last copy out
+// that cannot overlap stay short.
+constexpr int kHostChunkTokens = 2048;
 constexpr size_t kCounterBytes = (2 + kMaxBands) * sizeof(uint32_t);  // done, err, bands
 
 struct Scratch {
@@ -155,6 +160,15 @@ struct oxg_ctx {
     int32_t *seg = nullptr;  // counts [256] then offsets [257]
   } ep;
   std::vector<int32_t> seg_host;
+  // Host-buffer forwards of large batches run in token chunks whose copies
+  // overlap the neighbouring chunks' compute (oxg_moe_forward_host).
+  struct {
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t x_ready[2] = {}, x_free[2] = {}, y_ready[2] = {}, y_free[2] = {};
+    void *buf = nullptr;
+    size_t bytes = 0;
+    int chunk = 0;  // tokens per chunk; 0: automatic, < 0: never chunk
+  } pipe;
   // Expert parallelism over peer memory (oxg_ep_init / oxg_ep_connect).
   struct {
     bool init = false, connected = false;
@@ -832,6 +846,17 @@ int oxg_ctx_destroy(oxg_ctx *ctx) {
   for (Layer &L : ctx->layers) free_layer(L);
   if (ctx->ws.base) cudaFree(ctx->ws.base);
   if (ctx->ep.base) cudaFree(ctx->ep.base);
+  if (ctx->pipe.h2d) cudaStreamSynchronize(ctx->pipe.h2d);
+  if (ctx->pipe.d2h) cudaStreamSynchronize(ctx->pipe.d2h);
+  for (int b = 0; b < 2; ++b) {
+    if (ctx->pipe.x_ready[b]) cudaEventDestroy(ctx->pipe.x_ready[b]);
+    if (ctx->pipe.x_free[b]) cudaEventDestroy(ctx->pipe.x_free[b]);
+    if (ctx->pipe.y_ready[b]) cudaEventDestroy(ctx->pipe.y_ready[b]);
+    if (ctx->pipe.y_free[b]) cudaEventDestroy(ctx->pipe.y_free[b]);
+  }
+  if (ctx->pipe.h2d) cudaStreamDestroy(ctx->pipe.h2d);
+  if (ctx->pipe.d2h) cudaStreamDestroy(ctx->pipe.d2h);
+  if (ctx->pipe.buf) cudaFree(ctx->pipe.buf);
   p2p_release(ctx);
   ctx->prof.destroy();
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -1078,6 +1103,83 @@ int oxg_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y,
   return forward_device(ctx, *L, x, T, y, mode);
 }
 
+namespace {
+// Chunked host-buffer forward: chunk c's x copy (stream h2d), compute
+// (ctx->stream) and y copy (stream d2h), with two staging buffers per
+// direction, so chunk c+1's copy in and chunk c-1's copy out run during chunk
+// c's kernels. Every token's result is the same as in one forward: routing,
+// expert rows and combine are per token, and chunks stay on the prefill
+// kernels (chunk > 64 tokens).
+int forward_host_chunked(oxg_ctx *ctx, Layer &L, const uint16_t *x_host, int T, float *y_host, int mode,
+                         int chunk) {
+  auto &P = ctx->pipe;
+  const size_t H = L.dims.hidden;
+  // n chunks of floor or ceil(T / n) tokens, every one at least `chunk`
+  const int n = T / chunk, Tc = (T + n - 1) / n;
+  const size_t xb = align_up((size_t)Tc * H * 2, 256), yb = align_up((size_t)Tc * H * 4, 256);
+  const size_t need = 2 * (xb + yb);
+  if (!P.h2d) {
+    OXG_CUDA(ctx, cudaStreamCreateWithFlags(&P.h2d, cudaStreamNonBlocking), "cudaStreamCreate(h2d)");
+    OXG_CUDA(ctx, cudaStreamCreateWithFlags(&P.d2h, cudaStreamNonBlocking), "cudaStreamCreate(d2h)");
+    for (int b = 0; b < 2; ++b) {
+      OXG_CUDA(ctx, cudaEventCreateWithFlags(&P.x_ready[b], cudaEventDisableTiming), "cudaEventCreate");
+      OXG_CUDA(ctx, cudaEventCreateWithFlags(&P.x_free[b], cudaEventDisableTiming), "cudaEventCreate");
+      OXG_CUDA(ctx, cudaEventCreateWithFlags(&P.y_ready[b], cudaEventDisableTiming), "cudaEventCreate");
+      OXG_CUDA(ctx, cudaEventCreateWithFlags(&P.y_free[b], cudaEventDisableTiming), "cudaEventCreate");
+    }
+  }
+  if (P.bytes < need) {
+    if (P.buf) cudaFree(P.buf);
+    P.buf = nullptr;
+    P.bytes = 0;
+    OXG_CUDA(ctx, cudaMalloc(&P.buf, need), "cudaMalloc(host pipeline staging)");
+    P.bytes = need;
+  }
+  char *base = (char *)P.buf;
+  uint16_t *xs[2] = {(uint16_t *)base, (uint16_t *)(base + xb)};
+  float *ys[2] = {(float *)(base + 2 * xb), (float *)(base + 2 * xb + yb)};
+  int rc = ensure_scratch(ctx, L.dims, Tc);
+  if (rc) return rc;
+  // nothing earlier on the compute stream may still use the staging buffers
+  OXG_CUDA(ctx, cudaEventRecord(P.y_ready[0], ctx->stream), "cudaEventRecord");
+  OXG_CUDA(ctx, cudaStreamWaitEvent(P.h2d, P.y_ready[0], 0), "cudaStreamWaitEvent");
+  for (int c = 0; c < n; ++c) {
+    const int b = c & 1;
+    const int t0 = (int)((long long)c * T / n), tc = (int)((long long)(c + 1) * T / n) - t0;
+    if (c >= 2) OXG_CUDA(ctx, cudaStreamWaitEvent(P.h2d, P.x_free[b], 0), "cudaStreamWaitEvent");
+    OXG_CUDA(ctx, cudaMemcpyAsync(xs[b], x_host + (size_t)t0 * H, (size_t)tc * H * 2, cudaMemcpyDefault, P.h2d),
+             "copy x to device");
+    OXG_CUDA(ctx, cudaEventRecord(P.x_ready[b], P.h2d), "cudaEventRecord");
+    OXG_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, P.x_ready[b], 0), "cudaStreamWaitEvent");
+    if (c >= 2) OXG_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, P.y_free[b], 0), "cudaStreamWaitEvent");
+    rc = forward_device(ctx, L, xs[b], tc, ys[b], mode);
+    if (rc) {
+      cudaStreamSynchronize(P.h2d);
+      cudaStreamSynchronize(P.d2h);
+      return rc;
+    }
+    OXG_CUDA(ctx, cudaEventRecord(P.x_free[b], ctx->stream), "cudaEventRecord");
+    OXG_CUDA(ctx, cudaEventRecord(P.y_ready[b], ctx->stream), "cudaEventRecord");
+    OXG_CUDA(ctx, cudaStreamWaitEvent(P.d2h, P.y_ready[b], 0), "cudaStreamWaitEvent");
+    OXG_CUDA(ctx, cudaMemcpyAsync(y_host + (size_t)t0 * H, ys[b], (size_t)tc * H * 4, cudaMemcpyDefault, P.d2h),
+             "copy y to host");
+    OXG_CUDA(ctx, cudaEventRecord(P.y_free[b], P.d2h), "cudaEventRecord");
+  }
+  OXG_CUDA(ctx, cudaStreamSynchronize(P.d2h), "cudaStreamSynchronize");
+  OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return read_pipeline_error(ctx);
+}
+}  // namespace
+
+int oxg_ctx_set_host_chunk(oxg_ctx *ctx, int tokens) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  if (tokens > 0 && tokens <= oxg::kMaxRouteTokens)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "host chunks must hold more than %d tokens (or 0: automatic, < 0: off)",
+                oxg::kMaxRouteTokens);
+  ctx->pipe.chunk = tokens;
+  return OXG_OK;
+}
+
 int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T, float *y_host,
                          int mode, int precision) {
   Layer *L = nullptr;
@@ -1085,6 +1187,15 @@ int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host, int T,
   if (rc) return rc;
   if (T == 0) return OXG_OK;
   DeviceGuard g(ctx->device);
+  {
+    // large batches: chunked, copies overlapped
+    const int Tc = ctx->pipe.chunk > 0 ? ctx->pipe.chunk : kHostChunkTokens;
+    if (ctx->pipe.chunk >= 0 && T >= 2 * Tc) {
+      ctx->last_layer = layer;
+      ctx->ep_tokens = -1;
+      return forward_host_chunked(ctx, *L, x_host, T, y_host, mode, Tc);
+    }
+  }
   rc = ensure_scratch(ctx, L->dims, T);
   if (rc) return rc;
   ctx->last_layer = layer;

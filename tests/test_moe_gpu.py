@@ -171,3 +171,24 @@ def test_bad_arguments_are_errors(cuda_ctx):
     lib = abi.load()
     st = lib.oxg_moe_forward(cuda_ctx.handle, 999, None, 1, None, 0, 0)
     assert st == abi.OXG_ERR_STATE
+
+
+def test_host_forward_in_chunks_matches_one_forward(cuda_ctx):
+    """Large host-buffer batches run in chunks with overlapped copies: every
+    token's output is bit-identical to the single forward."""
+    import torch
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    d = synth.moe_layer(seed=17, hidden=512, intermediate=512, n_experts=32, top_k=4)
+    layer = MoELayer(d)
+    x = synth.activations(17, 601, 512)
+    y_dev = layer.forward(torch.from_numpy(x.view(np.int16)).cuda()).cpu().numpy()
+    layer.ctx.set_host_chunk(-1)
+    y_one = layer.forward_host(x).numpy().copy()
+    for chunk in (150, 200):  # 4 chunks of 150-151 tokens; 3 of 200-201
+        layer.ctx.set_host_chunk(chunk)
+        y_chunks = layer.forward_host(x).numpy()
+        assert np.array_equal(y_chunks, y_one), chunk
+    layer.ctx.set_host_chunk(0)
+    assert np.array_equal(y_one, y_dev)
+    with pytest.raises(Exception):
+        layer.ctx.set_host_chunk(32)
