@@ -152,7 +152,7 @@ OXG_API int oxg_moe_forward_host(oxg_ctx *ctx, int layer, const uint16_t *x_host
 /* Tokens per chunk for oxg_moe_forward_host on batches of at least twice
  * that many tokens: the chunks' host->device copies, kernels and
  * device->host copies overlap on three streams (results per token are the
- * same as one forward). 0: automatic (2048), < 0: never chunk, else > 64.
+ * same as one forward). 0: automatic (1600), < 0: never chunk, else > 64.
  * No counterpart in the reference (its forward runs on the host). */
 OXG_API int oxg_ctx_set_host_chunk(oxg_ctx *ctx, int tokens);
 

@@ -19,13 +19,18 @@ cudaError_t launch_swiglu(const float *gate, const float *up, size_t n, float al
                           float *out, cudaStream_t stream);
 
 // ---- weight re-layout (relayout.cu) ----------------------------------------
-// Packed codes [rows, K/2] in the checkpoint order -> the "word-transposed"
-// order the MoE kernels read (described in relayout.cu). scales [rows, K/32]
-// -> [rows, kb_pad] with kb_pad = round_up(K/32, 4), padding bytes zero.
-cudaError_t launch_relayout_codes(const uint8_t *src, uint8_t *dst, size_t rows, int K,
-                                  cudaStream_t stream);
-cudaError_t launch_pad_scales(const uint8_t *src, uint8_t *dst, size_t rows, int K,
-                              cudaStream_t stream);
+// Packed codes [rows, K/2] and scales [rows, K/32] in the checkpoint order ->
+// the "tile chunk" order the f16 MoE kernels read (described in relayout.cu):
+// one run of tile_item_bytes(K) bytes per 16-row tile, codes and scales of
+// each 128-element group together. pair_adj selects the row pairing (1: the
+// gate/up interleaved mlp1 rows 2g, 2g + 1; 0: rows g, g + 8). Either source
+// may be null (that half is not written). rows % 16 == 0, K % 32 == 0.
+__host__ __device__ inline size_t tile_item_bytes(int K) {
+  const int nb = K / 32, tail = nb % 4;
+  return (size_t)(nb / 4) * 1088 + (tail ? 256 * tail + 64 : 0);
+}
+cudaError_t launch_tile_weights(const uint8_t *codes, const uint8_t *scales, uint8_t *dst,
+                                size_t rows, int K, int pair_adj, cudaStream_t stream);
 
 // ---- routing (router.cu) ----------------------------------------------------
 // logits may be null. sigma[T] receives the per-token power-of-two exponent
@@ -163,10 +168,10 @@ struct MoeDeviceWeights {
   int H, I, E, k;
   float alpha, limit;
   const uint16_t *router_w, *router_b;
-  const uint8_t *w1, *s1;  // relaid codes [E, 2I, H/2], padded scales [E, 2I, kb1]
-  const uint16_t *b1;      // [E, 2I]
-  const uint8_t *w2, *s2;  // [E, H, I/2], [E, H, kb2]
-  const uint16_t *b2;      // [E, H]
+  const uint8_t *w1;    // tile chunks (codes + scales) of [E, 2I, H], gate/up pairing
+  const uint16_t *b1;   // [E, 2I]
+  const uint8_t *w2;    // tile chunks of [E, H, I], rows g / g + 8 pairing
+  const uint16_t *b2;   // [E, H]
 };
 
 // mlp1 + bias + clamped SwiGLU for every (expert, slot) -> h [n_slots, I] f32

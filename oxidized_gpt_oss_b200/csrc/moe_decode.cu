@@ -11,12 +11,13 @@
 // Design (HBM-bound: every expert weight byte is read once per step):
 //  * A warp computes 16 weight rows x 8 token columns with mma.m16n8k16
 //    (f16 in, f32 out); CTAs are 16 warps, one per SM.
-//  * Weight codes stream from HBM in the word-transposed order of
-//    relayout.cu, so one 16-byte copy gives a lane the A-operand codes of all
-//    four blocks of a 128-element group. Each warp runs one continuous
-//    cp.async pipeline through a shared-memory ring (6 groups in flight per
-//    lane, ~120 KB per SM) across all the tiles it processes, so HBM latency
-//    is covered without holding registers and without a refill gap between
+//  * Weights stream from HBM in the tile-chunk order of relayout.cu: a 16-row
+//    tile is one contiguous run, 1088 bytes (codes + scales) per 128-element
+//    group, and one 16-byte copy per lane and row half gives a lane the
+//    A-operand codes of all four blocks of the group. Each warp runs one
+//    continuous cp.async pipeline through a shared-memory ring (6 groups in
+//    flight per lane) across all the tiles it processes, so HBM latency is
+//    covered without holding registers and without a refill gap between
 //    tiles. cvt.rn.f16x2.e2m1x2 turns two codes into two exact f16 values;
 //    the E8M0 scale of each 32-element block multiplies that block's f32 MMA
 //    result (an exact power of two).
@@ -43,18 +44,18 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-// Per-warp ring of weight groups in flight: kStages slots of
-// 2 rows x 32 lanes x 16 B of codes + 2 x 32 x 4 B of scales.
+// Per-warp ring of weight groups in flight: kStages slots of one group's
+// chunk (2 row halves x 32 lanes x 16 B of codes + 64 B of scales).
 constexpr int kStages = 6;
-constexpr int kStageBytes = 1280;
+constexpr int kStageBytes = 1088;
 constexpr int kRingBytes = kWarps * kStages * kStageBytes;
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
 struct DecodeArgs {
-  const uint8_t *codes;   // relaid codes [E, rows, K/2]
-  const uint8_t *scales;  // padded scales [E, rows, kb_pad]
+  const uint8_t *codes;   // tile chunks of [E, rows, K] (codes + scales)
   const uint16_t *bias;   // [E, rows] bf16
-  int K, rows, kb_pad;
+  int K, rows;
+  size_t item_bytes;      // bytes of one 16-row tile
   // mlp1 input: x [T, K] bf16, token of position p = perm[p] / topk
   const uint16_t *x;
   const int32_t *perm;
@@ -91,41 +92,37 @@ __device__ __forceinline__ int frag_off(int nt, int nb, int blk, int s, int g, i
   return ((((nt * nb + blk) * 2 + s) * 8 + g) * 4 + q) * bytes;
 }
 
-struct TileRows {
-  const uint8_t *ca, *cb, *sa, *sb;  // codes and scales of the lane's rows a and b
-};
-
-// Streams the weight rows of n_items 16-row tiles through the warp's ring.
-// item_rows(i) gives the lane's two rows of item i; block_fn(blk, wa, wb,
-// s_a, s_b) consumes one 32-element block (code words of rows a/b, their
-// scales); done_fn(i) runs after the last block of item i.
-template <class ItemRows, class BlockFn, class DoneFn>
-__device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, ItemRows item_rows,
+// Streams the chunks of n_items 16-row tiles through the warp's ring.
+// item_ptr(i) gives the first byte of item i's tile; block_fn(blk, wa, wb,
+// s_a, s_b) consumes one 32-element block (code words of the lane's rows a/b,
+// their scales); done_fn(i) runs after the last block of item i.
+template <class ItemPtr, class BlockFn, class DoneFn>
+__device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, ItemPtr item_ptr,
                                              BlockFn block_fn, DoneFn done_fn) {
   if (n_items <= 0) return;
-  const int lane = threadIdx.x & 31, q = lane & 3;
+  const int lane = threadIdx.x & 31, g = lane >> 2;
   const int nb = K / 32, full = nb / 4, tail = nb % 4, ngroups = full + (tail ? 1 : 0);
-  // Issue side: runs kStages groups ahead of the consumer; the rows of the
-  // item being issued are computed once per item.
+  // Issue side: runs kStages groups ahead of the consumer.
   int i_item = 0, i_grp = 0, i_slot = 0;
-  TileRows ir = item_rows(0);
+  const uint8_t *ip = item_ptr(0);
   auto issue_next = [&]() {
     if (i_item < n_items) {
       uint8_t *st = ring + i_slot * kStageBytes;
+      const uint8_t *ch = ip + (size_t)i_grp * 1088;
       if (i_grp < full) {
-        cp_async_16(st + lane * 16, ir.ca + i_grp * 64 + q * 16);
-        cp_async_16(st + 512 + lane * 16, ir.cb + i_grp * 64 + q * 16);
+        cp_async_16(st + lane * 16, ch + lane * 16);
+        cp_async_16(st + 512 + lane * 16, ch + 512 + lane * 16);
+        if (lane < 4) cp_async_16(st + 1024 + lane * 16, ch + 1024 + lane * 16);
       } else {
         for (int b = 0; b < tail; ++b) {
-          cp_async_4(st + lane * 16 + b * 4, ir.ca + i_grp * 64 + (q * tail + b) * 4);
-          cp_async_4(st + 512 + lane * 16 + b * 4, ir.cb + i_grp * 64 + (q * tail + b) * 4);
+          cp_async_4(st + lane * 16 + b * 4, ch + lane * 4 * tail + b * 4);
+          cp_async_4(st + 512 + lane * 16 + b * 4, ch + 128 * tail + lane * 4 * tail + b * 4);
         }
+        if (lane < 4) cp_async_16(st + 1024 + lane * 16, ch + 256 * tail + lane * 16);
       }
-      cp_async_4(st + 1024 + lane * 4, ir.sa + i_grp * 4);
-      cp_async_4(st + 1152 + lane * 4, ir.sb + i_grp * 4);
       if (++i_grp == ngroups) {
         i_grp = 0;
-        if (++i_item < n_items) ir = item_rows(i_item);
+        if (++i_item < n_items) ip = item_ptr(i_item);
       }
     }
     cp_async_commit();
@@ -140,8 +137,8 @@ __device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, 
     const uint8_t *st = ring + c_slot * kStageBytes;
     const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
     const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
-    const uint32_t sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + lane * 4);
-    const uint32_t sxb = *reinterpret_cast<const uint32_t *>(st + 1152 + lane * 4);
+    const uint32_t sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + g * 4);
+    const uint32_t sxb = *reinterpret_cast<const uint32_t *>(st + 1056 + g * 4);
     issue_next();
     const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
     const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
@@ -181,7 +178,7 @@ __device__ __forceinline__ void a_operands(uint32_t wa, uint32_t wb, uint32_t (&
 // beyond `valid` are zero.
 template <int NT, class RowOf>
 __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int nb, int valid,
-                                        RowOf row_of) {
+                                        RowOf row_of, const int32_t *sigma) {
   const int K = a.K;
   const int units = NT * 8 * (K / 8);
   for (int u = threadIdx.x; u < units; u += kThreads) {
@@ -190,7 +187,7 @@ __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int 
     uint32_t o0 = 0, o1 = 0, o2 = 0, o3 = 0;
     if (tok < valid) {
       const int t = row_of(tok);
-      const float inv = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
+      const float inv = __uint_as_float((uint32_t)(127 - sigma[t]) << 23);
       const uint4 v = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + k0);
       o0 = pack_f16x2(bf16_to_f32(v.x & 0xFFFFu) * inv, bf16_to_f32(v.x >> 16) * inv);
       o1 = pack_f16x2(bf16_to_f32(v.y & 0xFFFFu) * inv, bf16_to_f32(v.y >> 16) * inv);
@@ -225,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
     act_of[a.active[i]] = i;
   }
   for (int i = tid; i < n_act * 8; i += kThreads) col_pos[i] = -1;
-  stage_x<1>(a, smem, nb, T, [](int tok) { return tok; });
+  stage_x<1>(a, smem, nb, T, [](int tok) { return tok; }, a.sigma);
   if (tid < 8) tok_scale[tid] = tid < T ? __uint_as_float((uint32_t)(127 + a.sigma[tid]) << 23) : 1.f;
   __syncthreads();
   for (int p = tid; p < T * k; p += kThreads) {
@@ -240,11 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
   const int n_items = wg < total ? (total - wg + W - 1) / W : 0;
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  auto item_rows = [&](int i) {
+  auto item_ptr = [&](int i) {
     const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
-    const size_t r_a = (size_t)act_s[ai] * a.rows + 2 * (tile * 8 + g);
-    return TileRows{a.codes + r_a * (K / 2), a.codes + (r_a + 1) * (K / 2),
-                    a.scales + r_a * a.kb_pad, a.scales + (r_a + 1) * a.kb_pad};
+    return a.codes + ((size_t)act_s[ai] * n_tiles + tile) * a.item_bytes;
   };
   auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
     uint32_t A0[4], A1[4];
@@ -278,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
     acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
   };
   uint8_t *ring = smem + nb * 2 * 32 * 8 + warp * (kStages * kStageBytes);
-  stream_items(n_items, K, ring, item_rows, block_fn, done_fn);
+  stream_items(n_items, K, ring, item_ptr, block_fn, done_fn);
 }
 
 // ---------------------------------------------------------------------------
@@ -307,7 +302,7 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
   for (int tok0 = 0; tok0 < n_e; tok0 += kTokPerPass) {
     // ---- stage this pass's activations in fragment order ----
     if (MODE == 1) {
-      stage_x<NT>(a, smem, nb, n_e - tok0, [&](int tok) { return a.perm[pos0 + tok0 + tok] / a.topk; });
+      stage_x<NT>(a, smem, nb, n_e - tok0, [&](int tok) { return a.perm[pos0 + tok0 + tok] / a.topk; }, a.sigma);
       if (tid < NT * 8) {
         float sc = 1.f;
         if (tok0 + tid < n_e)
@@ -353,15 +348,7 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
 #pragma unroll
     for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     auto tile_of = [&](int i) { return t_begin + warp + i * kWarps; };
-    auto item_rows = [&](int i) {
-      const int tile = tile_of(i);
-      const int row_a = MODE == 1 ? 2 * (tile * 8 + g) : tile * 16 + g;
-      const int row_b = MODE == 1 ? row_a + 1 : row_a + 8;
-      return TileRows{a.codes + (rbase + row_a) * (size_t)(K / 2),
-                      a.codes + (rbase + row_b) * (size_t)(K / 2),
-                      a.scales + (rbase + row_a) * (size_t)a.kb_pad,
-                      a.scales + (rbase + row_b) * (size_t)a.kb_pad};
-    };
+    auto item_ptr = [&](int i) { return a.codes + ((size_t)e * (a.rows / 16) + tile_of(i)) * a.item_bytes; };
     auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
       uint32_t A0[4], A1[4];
       a_operands(wa, wb, A0, A1);
@@ -422,7 +409,7 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
 #pragma unroll
       for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     };
-    stream_items(n_items, K, ring, item_rows, block_fn, done_fn);
+    stream_items(n_items, K, ring, item_ptr, block_fn, done_fn);
     __syncthreads();
   }
 }
@@ -539,11 +526,10 @@ DecodeArgs mlp1_args(const MoeDeviceWeights &w, const uint16_t *x, const int32_t
                      float *h) {
   DecodeArgs a{};
   a.codes = w.w1;
-  a.scales = w.s1;
   a.bias = w.b1;
   a.K = w.H;
   a.rows = 2 * w.I;
-  a.kb_pad = (w.H / 32 + 3) / 4 * 4;
+  a.item_bytes = tile_item_bytes(w.H);
   a.x = x;
   a.perm = perm;
   a.sigma = sigma;
@@ -562,11 +548,10 @@ DecodeArgs mlp2_args(const MoeDeviceWeights &w, const float *h, const int32_t *c
                      const int32_t *offsets, float *y_slot) {
   DecodeArgs a{};
   a.codes = w.w2;
-  a.scales = w.s2;
   a.bias = w.b2;
   a.K = w.I;
   a.rows = w.H;
-  a.kb_pad = (w.I / 32 + 3) / 4 * 4;
+  a.item_bytes = tile_item_bytes(w.I);
   a.h = h;
   a.topk = w.k;
   a.counts = counts;

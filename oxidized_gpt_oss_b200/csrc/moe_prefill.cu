@@ -67,10 +67,11 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxExpertsP = 256;
 
 struct PrefillArgs {
-  const uint8_t *codes;   // relaid codes [E, rows, K/2]
-  const uint8_t *scales;  // padded scales [E, rows, kb_pad]
+  const uint8_t *codes;   // tile chunks of [E, rows, K] (codes + scales, relayout.cu)
   const uint16_t *bias;   // [E, rows]
-  int K, rows, kb_pad;
+  int K, rows;
+  size_t item_bytes;      // bytes of one 16-row tile
+  int pair_adj;           // row pairing of the tile chunks (1: rows 2g, 2g + 1)
   const int32_t *counts, *offsets;
   int n_segments;  // runs of slot rows sharing one expert (counts/offsets index)
   int weight_mod;  // segment v multiplies by the layer's local expert v % weight_mod
@@ -281,25 +282,30 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     // Thread gt of group grp owns kTasks (row, q) pairs of each of its weight
     // tiles: row (gt + t * kGroupThreads) / 4, 16-byte chunks q (block 2hf of
     // the k-step pair) and 4 + q (block 2hf + 1). Its codes (8 B: word q of
-    // the two blocks, adjacent in the relaid order) and the two scale bytes
-    // are loaded into registers kLead of its k-steps before use.
+    // the two blocks, adjacent in the tile-chunk order) and the two scale
+    // bytes are loaded into registers kLead of its k-steps before use.
     const int ct = converter_index(warp) * 32 + lane;
     const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
     const int q = gt & 3;
     const int full = a.K / 128;  // complete 4-block groups per row
-    const int row_bytes = a.K / 2;
+    const int tail = (a.K / 32) % 4;
+    // The tasks' rows are 32 apart, so they share the tile row lr = row % 16
+    // and with it the offsets inside each group chunk (part p, lane row gr).
+    static_assert(kGroupThreads / 4 == 32, "task rows must be a whole number of tiles apart");
+    const int lr = (gt >> 2) & 15;
+    const int pp = a.pair_adj ? (lr & 1) : (lr >> 3), gr = a.pair_adj ? (lr >> 1) : (lr & 7);
+    const int c_full = pp * 512 + (4 * gr + q) * 16, s_full = 1024 + pp * 32 + 4 * gr;
+    const int c_tail = pp * 128 * tail + (4 * gr + q) * 4 * tail, s_tail = 256 * tail + pp * 32 + 4 * gr;
     // issue cursor: this group's k-steps as (item, ks), kGroups steps apart
     int i_item = pair, i_ks = grp;
-    // task t's row is row0 + t * (kGroupThreads / 4): codes at crow + t * cstep
-    const uint8_t *crow = a.codes, *srow = a.scales;
-    const int cstep = (kGroupThreads / 4) * row_bytes, sstep = (kGroupThreads / 4) * a.kb_pad;
+    // task t's row is row0 + t * 32: its tile starts at crow + t * cstep
+    const uint8_t *crow = a.codes;
+    const size_t cstep = 2 * a.item_bytes;
     int n_rows_ok = 0;  // tasks 0 .. n_rows_ok - 1 lie inside the matrix
     auto set_rows = [&](int item) {
       const Coords c = coords(item);
       const int R0 = c.m0 + (int)rank * BM + (gt >> 2);
-      const size_t erow = (size_t)(c.e % a.weight_mod) * a.rows + R0;
-      crow = a.codes + erow * row_bytes;
-      srow = a.scales + erow * a.kb_pad;
+      crow = a.codes + ((size_t)(c.e % a.weight_mod) * (a.rows / 16) + (R0 >> 4)) * a.item_bytes;
       n_rows_ok = R0 < a.rows ? min(kTasks, (a.rows - R0 + kGroupThreads / 4 - 1) / (kGroupThreads / 4)) : 0;
     };
     auto normalise = [&]() {
@@ -312,14 +318,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     if (i_item < total) set_rows(i_item);
     auto load_step = [&](uint2 (&cw)[kTasks], uint32_t (&sw)[kTasks]) {
       const int G = i_ks >> 1, hf = i_ks & 1;
-      const int off = G < full ? G * 64 + q * 16 + hf * 8 : G * 64 + q * 8;
+      const int off = G * 1088 + (G < full ? c_full + hf * 8 : c_tail);
+      const int soff = G * 1088 + (G < full ? s_full : s_tail) + 2 * hf;
 #pragma unroll
       for (int t = 0; t < kTasks; ++t) {
         cw[t] = make_uint2(0u, 0u);
         sw[t] = 0u;
         if (i_item < total && t < n_rows_ok) {
           cw[t] = __ldg(reinterpret_cast<const uint2 *>(crow + t * cstep + off));
-          sw[t] = __ldg(reinterpret_cast<const unsigned short *>(srow + t * sstep + G * 4 + 2 * hf));
+          sw[t] = __ldg(reinterpret_cast<const unsigned short *>(crow + t * cstep + soff));
         }
       }
       if (i_item < total) {
@@ -621,8 +628,7 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
     return cudaErrorInvalidValue;
   // the converters load 8-byte code words and 2-byte scale pairs, the
   // epilogue stores 4-byte h pairs
-  if (((uintptr_t)w.w1 & 7) || ((uintptr_t)w.s1 & 3) || ((uintptr_t)io.h_hi & 3) ||
-      ((uintptr_t)io.h_lo & 3))
+  if (((uintptr_t)w.w1 & 15) || ((uintptr_t)io.h_hi & 3) || ((uintptr_t)io.h_lo & 3))
     return cudaErrorInvalidValue;
   CUtensorMap m0, m1;
   cudaError_t st = make_tmap(&m0, io.xp, io.S, w.H, BNH);
@@ -630,11 +636,11 @@ cudaError_t launch_prefill_mlp1(const MoeDeviceWeights &w, const PrefillIO &io, 
   m1 = m0;
   PrefillArgs a{};
   a.codes = w.w1;
-  a.scales = w.s1;
   a.bias = w.b1;
   a.K = w.H;
   a.rows = 2 * w.I;
-  a.kb_pad = (w.H / 32 + 3) / 4 * 4;
+  a.item_bytes = tile_item_bytes(w.H);
+  a.pair_adj = 1;
   a.counts = io.counts;
   a.offsets = io.offsets;
   a.n_segments = io.n_segments;
@@ -657,7 +663,7 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   if (w.H % BK || w.I % BK || io.n_segments > kMaxExpertsP || io.n_segments < 1 ||
       io.weight_mod < 1)
     return cudaErrorInvalidValue;
-  if (((uintptr_t)w.w2 & 7) || ((uintptr_t)w.s2 & 3)) return cudaErrorInvalidValue;
+  if ((uintptr_t)w.w2 & 15) return cudaErrorInvalidValue;
   CUtensorMap m0, m1;
   cudaError_t st = make_tmap(&m0, io.h_hi, io.S, w.I, BNH);
   if (st != cudaSuccess) return st;
@@ -665,11 +671,11 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   if (st != cudaSuccess) return st;
   PrefillArgs a{};
   a.codes = w.w2;
-  a.scales = w.s2;
   a.bias = w.b2;
   a.K = w.I;
   a.rows = w.H;
-  a.kb_pad = (w.I / 32 + 3) / 4 * 4;
+  a.item_bytes = tile_item_bytes(w.I);
+  a.pair_adj = 0;
   a.counts = io.counts;
   a.offsets = io.offsets;
   a.n_segments = io.n_segments;
