@@ -180,12 +180,12 @@ struct MoeDeviceWeights {
 cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
                                    const int32_t *perm, const int32_t *sigma,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *h,
+                                   int expert_base, int n_local_experts, float *h, int *err,
                                    cudaStream_t stream);
 // mlp2 + bias -> y_slot [n_slots, H] f32 (position order)
 cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *y_slot,
+                                   int expert_base, int n_local_experts, float *y_slot, int *err,
                                    cudaStream_t stream);
 // Scheduled variants (decode fast path): blockIdx.y walks the active-expert
 // list written by the routing kernel, the grid is sized to one resident
@@ -197,9 +197,12 @@ struct DecodeSched {
   int bands2;      // per-expert bands of the mlp2 kernel
   int n_sms;       // persistent grid of the all-token mlp1 kernel
   bool pdl;
+  int *err;        // error word (bounded waits of the weight streams)
 };
 // Bands (CTAs per expert) so that expected_active experts fill n_sms SMs.
 int decode_bands(int rows, int expected_active, int n_sms);
+// mlp2's fused combine counts finished experts per row band in band_done,
+// which must hold max(bands2, min(H / 16, n_sms)) zeroed counters.
 // mlp1 + bias + clamped SwiGLU. With T <= 8 all tokens are staged once per
 // CTA and a persistent grid of n_sms CTAs walks (active expert, tile) pairs;
 // idx is the routing [T, k]. Otherwise one CTA per (active expert, band).

@@ -38,17 +38,36 @@
 //    and 2j+1 (one MMA per k-step); otherwise each half takes its own MMA.
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace oxg {
 namespace {
 
-constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
-// Per-warp ring of weight groups in flight: kStages slots of one group's
+// Per-warp ring of weight groups in flight: STAGES slots of one group's
 // chunk (2 row halves x 32 lanes x 16 B of codes + 64 B of scales).
-constexpr int kStages = 6;
 constexpr int kStageBytes = 1088;
-constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+// CTA shapes (warps, ring stages): the all-token mlp1 kernel, the per-expert
+// kernel (mlp1 above 8 tokens, mlp2 above 8 tokens) and mlp2 for at most 8
+// tokens (persistent grid, packed h stage).
+#ifndef OXG_DEC_W1
+#define OXG_DEC_W1 28
+#define OXG_DEC_S1 5
+#endif
+#ifndef OXG_DEC_W2
+#define OXG_DEC_W2 16
+#define OXG_DEC_S2 6
+#endif
+#ifndef OXG_DEC_BULK
+#define OXG_DEC_BULK 0
+#endif
+constexpr bool kBulk = OXG_DEC_BULK != 0;
+#ifndef OXG_DEC_W3
+#define OXG_DEC_W3 32
+#define OXG_DEC_S3 5
+#endif
+constexpr int kW1 = OXG_DEC_W1, kS1 = OXG_DEC_S1;
+constexpr int kW2 = OXG_DEC_W2, kS2 = OXG_DEC_S2;
+constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
 struct DecodeArgs {
@@ -74,6 +93,10 @@ struct DecodeArgs {
   // blockIdx.x is one of `bands` equal bands of an expert's 16-row tiles
   const int32_t *active, *n_active;
   int bands;
+  // dyn_bands: a 1-D grid of gridDim.x CTAs split on the device into
+  // min(tiles, gridDim.x / n_active) bands per active expert (every SM busy
+  // whatever the number of active experts); `bands` is then unused
+  int dyn_bands;
   int pdl;  // launched as a programmatic dependent: wait before reading inputs
   int T;
   // mlp2 only: fused weighted combine when band_done is set
@@ -81,6 +104,7 @@ struct DecodeArgs {
   const int32_t *slot_pos;
   const float *wts;
   float *y;
+  int *err;  // error word: bounded waits that ran out record their code here
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -92,24 +116,46 @@ __device__ __forceinline__ int frag_off(int nt, int nb, int blk, int s, int g, i
   return ((((nt * nb + blk) * 2 + s) * 8 + g) * 4 + q) * bytes;
 }
 
+// A warp's ring of STAGES group slots. Bulk mode: lane 0 fetches each group
+// chunk with one cp.async.bulk (TMA engine) that completes on the slot's
+// mbarrier; phase holds the parity each slot waits for next. Otherwise the
+// lanes copy their own 16-byte pieces with cp.async.
+struct WarpRing {
+  uint8_t *ring;
+  uint64_t *bars;
+  uint32_t phase;
+};
+constexpr int kErrDecodeWait = 21;  // error word: a decode weight copy did not land
+
 // Streams the chunks of n_items 16-row tiles through the warp's ring.
-// item_ptr(i) gives the first byte of item i's tile; block_fn(blk, wa, wb,
-// s_a, s_b) consumes one 32-element block (code words of the lane's rows a/b,
-// their scales); done_fn(i) runs after the last block of item i.
-template <class ItemPtr, class BlockFn, class DoneFn>
-__device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, ItemPtr item_ptr,
-                                             BlockFn block_fn, DoneFn done_fn) {
-  if (n_items <= 0) return;
+// item_ptr(i) gives the first byte of item i's tile; group_fn(blk0, nblk,
+// wa, wb, sxa, sxb) consumes one group of nblk <= 4 blocks starting at block
+// blk0 (the code words of the lane's rows a/b per block, and their four scale
+// bytes); done_fn(i) runs after the last group of item i. Returns
+// false (error word set) if a bulk copy did not complete within the wait
+// budget; the copies still in flight have then been waited for (bounded).
+template <int STAGES, bool BULK, class ItemPtr, class GroupFn, class DoneFn>
+__device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, int *err, ItemPtr item_ptr,
+                                             GroupFn group_fn, DoneFn done_fn) {
+  if (n_items <= 0) return true;
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int nb = K / 32, full = nb / 4, tail = nb % 4, ngroups = full + (tail ? 1 : 0);
-  // Issue side: runs kStages groups ahead of the consumer.
-  int i_item = 0, i_grp = 0, i_slot = 0;
+  const uint32_t tail_bytes = 256u * tail + 64u;
+  // Issue side: runs STAGES groups ahead of the consumer.
+  int i_item = 0, i_grp = 0, i_slot = 0, pending = 0;
   const uint8_t *ip = item_ptr(0);
   auto issue_next = [&]() {
     if (i_item < n_items) {
-      uint8_t *st = ring + i_slot * kStageBytes;
+      uint8_t *st = wr.ring + i_slot * kStageBytes;
       const uint8_t *ch = ip + (size_t)i_grp * 1088;
-      if (i_grp < full) {
+      if (BULK) {
+        if (lane == 0) {
+          const uint32_t bytes = i_grp < full ? 1088u : tail_bytes;
+          sm100::mbar_arrive_expect_tx(&wr.bars[i_slot], bytes);
+          sm100::bulk_copy(st, ch, bytes, &wr.bars[i_slot]);
+        }
+        ++pending;
+      } else if (i_grp < full) {
         cp_async_16(st + lane * 16, ch + lane * 16);
         cp_async_16(st + 512 + lane * 16, ch + 512 + lane * 16);
         if (lane < 4) cp_async_16(st + 1024 + lane * 16, ch + 1024 + lane * 16);
@@ -125,41 +171,92 @@ __device__ __forceinline__ void stream_items(int n_items, int K, uint8_t *ring, 
         if (++i_item < n_items) ip = item_ptr(i_item);
       }
     }
-    cp_async_commit();
-    if (++i_slot == kStages) i_slot = 0;
+    if (!BULK) cp_async_commit();
+    if (++i_slot == STAGES) i_slot = 0;
   };
 #pragma unroll
-  for (int u = 0; u < kStages; ++u) issue_next();
+  for (int u = 0; u < STAGES; ++u) issue_next();
   int c_item = 0, c_grp = 0, c_slot = 0;
+  bool ok = true;
 #pragma unroll 1
   while (c_item < n_items) {
-    cp_async_wait<kStages - 1>();
-    const uint8_t *st = ring + c_slot * kStageBytes;
-    const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
-    const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
-    const uint32_t sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + g * 4);
-    const uint32_t sxb = *reinterpret_cast<const uint32_t *>(st + 1056 + g * 4);
-    issue_next();
-    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
-    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
-    if (c_grp < full) {
+    const uint8_t *st = wr.ring + c_slot * kStageBytes;
+    uint32_t wa[4], wb[4], sxa, sxb;
+    if (BULK) {
+      const bool landed = sm100::mbar_wait(&wr.bars[c_slot], (wr.phase >> c_slot) & 1u, err, kErrDecodeWait);
+      if (!__all_sync(0xFFFFFFFFu, landed)) {
+        ok = false;
+        break;
+      }
+      wr.phase ^= 1u << c_slot;
+      --pending;
+      // a bulk copy lands the chunk as stored: narrow groups keep their
+      // packed layout (4 * tail bytes per lane and row half)
+      if (c_grp < full) {
+        const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
+        const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
+        wa[0] = va.x; wa[1] = va.y; wa[2] = va.z; wa[3] = va.w;
+        wb[0] = vb.x; wb[1] = vb.y; wb[2] = vb.z; wb[3] = vb.w;
+        sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + g * 4);
+        sxb = *reinterpret_cast<const uint32_t *>(st + 1056 + g * 4);
+      } else {
 #pragma unroll
-      for (int b = 0; b < 4; ++b)
-        block_fn(c_grp * 4 + b, wa[b], wb[b], e8m0_to_f32(sxa >> (8 * b)), e8m0_to_f32(sxb >> (8 * b)));
+        for (int b = 0; b < 3; ++b) {
+          wa[b] = b < tail ? *reinterpret_cast<const uint32_t *>(st + lane * 4 * tail + 4 * b) : 0u;
+          wb[b] = b < tail ? *reinterpret_cast<const uint32_t *>(st + 128 * tail + lane * 4 * tail + 4 * b) : 0u;
+        }
+        wa[3] = wb[3] = 0u;
+        sxa = *reinterpret_cast<const uint32_t *>(st + 256 * tail + g * 4);
+        sxb = *reinterpret_cast<const uint32_t *>(st + 256 * tail + 32 + g * 4);
+      }
+      // the slot's reads are done before the async proxy refills it
+      sm100::fence_proxy_async_smem();
+      __syncwarp();
     } else {
-#pragma unroll
-      for (int b = 0; b < 3; ++b)
-        if (b < tail)
-          block_fn(c_grp * 4 + b, wa[b], wb[b], e8m0_to_f32(sxa >> (8 * b)), e8m0_to_f32(sxb >> (8 * b)));
+      cp_async_wait<STAGES - 1>();
+      const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
+      const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
+      wa[0] = va.x; wa[1] = va.y; wa[2] = va.z; wa[3] = va.w;
+      wb[0] = vb.x; wb[1] = vb.y; wb[2] = vb.z; wb[3] = vb.w;
+      sxa = *reinterpret_cast<const uint32_t *>(st + 1024 + g * 4);
+      sxb = *reinterpret_cast<const uint32_t *>(st + 1056 + g * 4);
     }
+    issue_next();
+    if (c_grp < full)
+      group_fn(c_grp * 4, 4, wa, wb, sxa, sxb);
+    else
+      group_fn(c_grp * 4, tail, wa, wb, sxa, sxb);
     if (++c_grp == ngroups) {
       done_fn(c_item);
       c_grp = 0;
       ++c_item;
     }
-    if (++c_slot == kStages) c_slot = 0;
+    if (++c_slot == STAGES) c_slot = 0;
   }
-  cp_async_wait<0>();
+  if (BULK) {
+    // after a failed wait: the copies still in flight land (or time out)
+    // before the warp leaves, so none writes into a reused shared buffer
+    for (; pending > 0; --pending) {
+      sm100::mbar_wait(&wr.bars[c_slot], (wr.phase >> c_slot) & 1u, err, kErrDecodeWait);
+      wr.phase ^= 1u << c_slot;
+      if (++c_slot == STAGES) c_slot = 0;
+    }
+    __syncwarp();
+  } else {
+    cp_async_wait<0>();
+  }
+  return ok;
+}
+
+// Per-warp barriers of the bulk ring: initialised once per CTA by the warp's
+// lane 0 (all phases start at parity 0).
+template <int STAGES>
+__device__ __forceinline__ WarpRing make_ring(uint8_t *ring, uint64_t *bars) {
+  if ((threadIdx.x & 31) == 0)
+    for (int u = 0; u < STAGES; ++u) sm100::mbar_init(&bars[u], 1);
+  sm100::fence_mbar_init();
+  __syncwarp();
+  return WarpRing{ring, bars, 0u};
 }
 
 // Decodes two rows' code words into the m16n8k16 A operands of the block's
@@ -173,6 +270,44 @@ __device__ __forceinline__ void a_operands(uint32_t wa, uint32_t wb, uint32_t (&
   A1[0] = fa[2]; A1[1] = fb[2]; A1[2] = fa[3]; A1[3] = fb[3];
 }
 
+// One group of nblk <= 4 blocks against n-tile nt of the staged activations
+// (KF bytes per fragment: 8 = one f16 pair per k-step, 16 = f16 hi and lo
+// pairs), block by block: decode the A operands, the block's MMAs, then its
+// E8M0 scales applied in f32. (Decoding all four blocks first and running
+// their MMA chains side by side measured slower: 55 vs 52 us for mlp1.)
+template <int KF>
+__device__ __forceinline__ void mma_group(const uint8_t *bsm, int nb, int nt, int blk0, int nblk,
+                                          const uint32_t (&wa)[4], const uint32_t (&wb)[4], uint32_t sxa,
+                                          uint32_t sxb, int g, int q, float (&acc)[4]) {
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    if (b < nblk) {
+      const int blk = blk0 + b;
+      uint32_t A0[4], A1[4];
+      a_operands(wa[b], wb[b], A0, A1);
+      float d[4];
+      if (KF == 8) {
+        const uint2 b0 = *reinterpret_cast<const uint2 *>(bsm + frag_off(nt, nb, blk, 0, g, q, 8));
+        const uint2 b1 = *reinterpret_cast<const uint2 *>(bsm + frag_off(nt, nb, blk, 1, g, q, 8));
+        mma_f16_16816(d, A0, b0.x, b0.y, zero4);
+        mma_f16_16816(d, A1, b1.x, b1.y, d);
+      } else {
+        const uint4 b0 = *reinterpret_cast<const uint4 *>(bsm + frag_off(nt, nb, blk, 0, g, q, 16));
+        const uint4 b1 = *reinterpret_cast<const uint4 *>(bsm + frag_off(nt, nb, blk, 1, g, q, 16));
+        mma_f16_16816(d, A0, b0.x, b0.y, zero4);
+        mma_f16_16816(d, A0, b0.z, b0.w, d);
+        mma_f16_16816(d, A1, b1.x, b1.y, d);
+        mma_f16_16816(d, A1, b1.z, b1.w, d);
+      }
+      const float s_a = e8m0_to_f32(sxa >> (8 * b)), s_b = e8m0_to_f32(sxb >> (8 * b));
+      acc[0] = fmaf(s_a, d[0], acc[0]);
+      acc[1] = fmaf(s_a, d[1], acc[1]);
+      acc[2] = fmaf(s_b, d[2], acc[2]);
+      acc[3] = fmaf(s_b, d[3], acc[3]);
+    }
+}
+
 // Stages tokens [tok0, tok0 + n) of x (rows of `x` given by row_of(tok))
 // as f16 x * 2^-sigma into fragment order, 8 tokens per n-tile; tokens
 // beyond `valid` are zero.
@@ -181,7 +316,7 @@ __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int 
                                         RowOf row_of, const int32_t *sigma) {
   const int K = a.K;
   const int units = NT * 8 * (K / 8);
-  for (int u = threadIdx.x; u < units; u += kThreads) {
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
     const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
     const int blk = k0 >> 5, qq = (k0 & 31) >> 3, nt = tok >> 3, gg = tok & 7;
     uint32_t o0 = 0, o1 = 0, o2 = 0, o3 = 0;
@@ -202,12 +337,15 @@ __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int 
 // ---------------------------------------------------------------------------
 // mlp1 over all tokens (T <= 8): persistent grid over (active expert, tile).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeArgs a) {
+template <int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float tok_scale[8];
   __shared__ int act_s[kMaxAllTokActive];
   __shared__ int act_of[256];
   __shared__ int col_pos[kMaxAllTokActive * 8];  // position of (active expert, token), or -1
+  __shared__ uint64_t ring_bars[WARPS * STAGES];
 
   if (a.pdl) pdl_wait();
   const int K = a.K, nb = K / 32;
@@ -232,28 +370,16 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
   __syncthreads();
   if (a.pdl) pdl_launch();
 
-  const int W = gridDim.x * kWarps, wg = blockIdx.x * kWarps + warp;
+  const int W = gridDim.x * WARPS, wg = blockIdx.x * WARPS + warp;
   const int total = n_act * n_tiles;
   const int n_items = wg < total ? (total - wg + W - 1) / W : 0;
-  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   auto item_ptr = [&](int i) {
     const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
     return a.codes + ((size_t)act_s[ai] * n_tiles + tile) * a.item_bytes;
   };
-  auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
-    uint32_t A0[4], A1[4];
-    a_operands(wa, wb, A0, A1);
-    const uint2 b0 = *reinterpret_cast<const uint2 *>(smem + frag_off(0, nb, blk, 0, g, q, 8));
-    const uint2 b1 = *reinterpret_cast<const uint2 *>(smem + frag_off(0, nb, blk, 1, g, q, 8));
-    float d[4];
-    mma_f16_16816(d, A0, b0.x, b0.y, zero4);
-    mma_f16_16816(d, A1, b1.x, b1.y, d);
-    acc[0] = fmaf(s_a, d[0], acc[0]);
-    acc[1] = fmaf(s_a, d[1], acc[1]);
-    acc[2] = fmaf(s_b, d[2], acc[2]);
-    acc[3] = fmaf(s_b, d[3], acc[3]);
-  };
+  auto group_fn = [&](int blk0, int nblk, const uint32_t(&wa)[4], const uint32_t(&wb)[4], uint32_t sxa,
+                      uint32_t sxb) { mma_group<8>(smem, nb, 0, blk0, nblk, wa, wb, sxa, sxb, g, q, acc); };
   auto done_fn = [&](int i) {
     const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
     const int e = act_s[ai];
@@ -272,8 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
     }
     acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
   };
-  uint8_t *ring = smem + nb * 2 * 32 * 8 + warp * (kStages * kStageBytes);
-  stream_items(n_items, K, ring, item_ptr, block_fn, done_fn);
+  WarpRing wr = make_ring<STAGES>(smem + nb * 2 * 32 * 8 + warp * (STAGES * kStageBytes),
+                                  ring_bars + warp * STAGES);
+  stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn);
 }
 
 // ---------------------------------------------------------------------------
@@ -284,9 +411,13 @@ __global__ void __launch_bounds__(kThreads, 1) mlp1_alltok_kernel(const DecodeAr
 //   MODE 1: mlp1 + bias + clamped SwiGLU -> a.out = h
 //   MODE 2: mlp2 + bias -> a.out = y_slot
 // PACKED (MODE 2, n_e <= 4): f16 hi/lo of token j in MMA columns 2j / 2j+1.
-template <int MODE, int NT, bool PACKED>
-__device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, float *tok_scale,
-                                            int e, int n_e, int pos0, int t_begin, int t_end) {
+// The activation stage occupies the first stage_bytes of smem (the kernel's
+// layout: NT n-tiles of 8-byte fragments for mlp1 and packed mlp2, 16-byte
+// ones otherwise); the warps' rings follow it.
+template <int MODE, int NT, bool PACKED, int WARPS, int STAGES>
+__device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, int stage_bytes, float *tok_scale,
+                                            uint64_t *ring_bars, int e, int n_e, int pos0, int t_begin,
+                                            int t_end) {
   constexpr int kTokPerPass = PACKED ? 4 : NT * 8;
   constexpr int kFrag = (MODE == 1 || PACKED) ? 8 : 16;  // bytes per staged fragment
   constexpr int kNT = PACKED ? 1 : NT;
@@ -294,10 +425,11 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const size_t rbase = (size_t)e * a.rows;
-  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-  uint8_t *ring = smem + NT * nb * 2 * 32 * (MODE == 1 ? 8 : 16) + warp * (kStages * kStageBytes);
-  // tiles of this warp: t_begin + warp, t_begin + warp + kWarps, ...
-  const int n_items = t_begin + warp < t_end ? (t_end - t_begin - warp + kWarps - 1) / kWarps : 0;
+  constexpr int kThreads = WARPS * 32;
+  WarpRing wr = make_ring<STAGES>(smem + stage_bytes + warp * (STAGES * kStageBytes), ring_bars + warp * STAGES);
+  bool ok = true;
+  // tiles of this warp: t_begin + warp, t_begin + warp + WARPS, ...
+  const int n_items = t_begin + warp < t_end ? (t_end - t_begin - warp + WARPS - 1) / WARPS : 0;
 
   for (int tok0 = 0; tok0 < n_e; tok0 += kTokPerPass) {
     // ---- stage this pass's activations in fragment order ----
@@ -347,32 +479,13 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
     float acc[kNT][4];
 #pragma unroll
     for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    auto tile_of = [&](int i) { return t_begin + warp + i * kWarps; };
+    auto tile_of = [&](int i) { return t_begin + warp + i * WARPS; };
     auto item_ptr = [&](int i) { return a.codes + ((size_t)e * (a.rows / 16) + tile_of(i)) * a.item_bytes; };
-    auto block_fn = [&](int blk, uint32_t wa, uint32_t wb, float s_a, float s_b) {
-      uint32_t A0[4], A1[4];
-      a_operands(wa, wb, A0, A1);
+    auto group_fn = [&](int blk0, int nblk, const uint32_t(&wa)[4], const uint32_t(&wb)[4], uint32_t sxa,
+                        uint32_t sxb) {
 #pragma unroll
-      for (int nt = 0; nt < kNT; ++nt) {
-        float d[4];
-        if (kFrag == 8) {
-          const uint2 b0 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 0, g, q, 8));
-          const uint2 b1 = *reinterpret_cast<const uint2 *>(smem + frag_off(nt, nb, blk, 1, g, q, 8));
-          mma_f16_16816(d, A0, b0.x, b0.y, zero4);
-          mma_f16_16816(d, A1, b1.x, b1.y, d);
-        } else {
-          const uint4 b0 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 0, g, q, 16));
-          const uint4 b1 = *reinterpret_cast<const uint4 *>(smem + frag_off(nt, nb, blk, 1, g, q, 16));
-          mma_f16_16816(d, A0, b0.x, b0.y, zero4);
-          mma_f16_16816(d, A0, b0.z, b0.w, d);
-          mma_f16_16816(d, A1, b1.x, b1.y, d);
-          mma_f16_16816(d, A1, b1.z, b1.w, d);
-        }
-        acc[nt][0] = fmaf(s_a, d[0], acc[nt][0]);
-        acc[nt][1] = fmaf(s_a, d[1], acc[nt][1]);
-        acc[nt][2] = fmaf(s_b, d[2], acc[nt][2]);
-        acc[nt][3] = fmaf(s_b, d[3], acc[nt][3]);
-      }
+      for (int nt = 0; nt < kNT; ++nt)
+        mma_group<kFrag>(smem, nb, nt, blk0, nblk, wa, wb, sxa, sxb, g, q, acc[nt]);
     };
     auto done_fn = [&](int i) {
       const int tile = tile_of(i);
@@ -409,20 +522,39 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
 #pragma unroll
       for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     };
-    stream_items(n_items, K, ring, item_ptr, block_fn, done_fn);
+    if (ok) ok = stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn);
     __syncthreads();
   }
 }
 
-template <int MODE, int NT>
-__global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeArgs a) {
+// Bytes of the per-expert kernel's activation stage: NT n-tiles of K / 32
+// blocks x 2 k-steps x 32 lanes of 8-byte (mlp1, packed mlp2) or 16-byte
+// (mlp2 with separate hi / lo columns) fragments.
+__host__ __device__ constexpr int decode_stage_bytes(int mode, int nt, bool packed_only, int K) {
+  return nt * (K / 32) * 2 * 32 * ((mode == 1 || packed_only) ? 8 : 16);
+}
+
+// PACKED_ONLY (mlp2): h is always staged as f16 hi/lo column pairs, four
+// tokens per pass, so the stage needs half the shared memory and the ring
+// gets the rest.
+template <int MODE, int NT, int WARPS, int STAGES, bool PACKED_ONLY>
+__global__ void __launch_bounds__(WARPS * 32, 1) moe_decode_kernel(const DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float tok_scale[NT * 8];
   __shared__ int band_last;
+  __shared__ uint64_t ring_bars[WARPS * STAGES];
 
   if (a.pdl) pdl_wait();
-  int e;
-  if (a.active) {
+  const int n_tiles = a.rows / 16;
+  int e, band = blockIdx.x, bands = a.bands;
+  if (a.dyn_bands) {
+    const int n_act = *a.n_active;
+    bands = min(n_tiles, (int)gridDim.x / max(n_act, 1));
+    if (bands < 1 || (int)blockIdx.x >= n_act * bands) return;
+    e = a.active[blockIdx.x / bands];
+    band = blockIdx.x % bands;
+  } else if (a.active) {
     if ((int)blockIdx.y >= *a.n_active) return;
     e = a.active[blockIdx.y];
   } else {
@@ -431,15 +563,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeArg
   const int n_e = a.counts[e];
   if (n_e == 0) return;
   const int pos0 = a.offsets[e];
-  const int n_tiles = a.rows / 16;
-  const int t_begin = (int)(((long long)blockIdx.x * n_tiles) / a.bands);
-  const int t_end = (int)(((long long)(blockIdx.x + 1) * n_tiles) / a.bands);
+  const int t_begin = (int)(((long long)band * n_tiles) / bands);
+  const int t_end = (int)(((long long)(band + 1) * n_tiles) / bands);
   const int tid = threadIdx.x;
 
-  if (MODE == 2 && n_e <= 4)
-    expert_band<MODE, NT, true>(a, smem, tok_scale, e, n_e, pos0, t_begin, t_end);
+  // shared memory: the activation stage, then the rings (launch size
+  // stage_bytes + WARPS * STAGES * kStageBytes)
+  const int stage_bytes = decode_stage_bytes(MODE, NT, PACKED_ONLY, a.K);
+  if (MODE == 2 && (PACKED_ONLY || n_e <= 4))
+    expert_band<MODE, NT, true, WARPS, STAGES>(a, smem, stage_bytes, tok_scale, ring_bars, e, n_e, pos0, t_begin,
+                                               t_end);
   else
-    expert_band<MODE, NT, false>(a, smem, tok_scale, e, n_e, pos0, t_begin, t_end);
+    expert_band<MODE, NT, false, WARPS, STAGES>(a, smem, stage_bytes, tok_scale, ring_bars, e, n_e, pos0, t_begin,
+                                                t_end);
 
   // ---- mlp2: the last expert to finish a band of rows combines it ----
   // out[t, r] = sum_j wts[t, j] * y_slot[slot_pos[t, j], r], j in order (the
@@ -448,21 +584,45 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeArg
   if (MODE == 2 && a.band_done) {
     if (tid == 0) {
       __threadfence();
-      band_last = atomicAdd(&a.band_done[blockIdx.x], 1u) == (unsigned)(*a.n_active - 1);
+      band_last = atomicAdd(&a.band_done[band], 1u) == (unsigned)(*a.n_active - 1);
     }
     __syncthreads();
     if (band_last) {
       __threadfence();
-      const int r0 = t_begin * 16, nr = (t_end - t_begin) * 16;
-      for (int i = tid; i < nr * a.T; i += kThreads) {
-        const int t = i / nr, r = r0 + i % nr;
-        float acc = 0.f;
-        for (int j = 0; j < a.topk; ++j) {
-          const int p = a.slot_pos[t * a.topk + j];
-          if (p < 0) continue;
-          acc = fmaf(a.wts[t * a.topk + j], __ldcg(a.out + (size_t)p * a.out_ld + r), acc);
+      // the routing of all T tokens into shared memory (the activation stage
+      // is free now), then 4 rows per thread with every slot row load of a
+      // token issued together
+      const int S = a.T * a.topk;
+      int *sp_s = reinterpret_cast<int *>(smem);
+      float *w_s = reinterpret_cast<float *>(smem) + S;
+      for (int i = tid; i < S; i += kThreads) {
+        sp_s[i] = __ldcg(a.slot_pos + i);
+        w_s[i] = __ldcg(a.wts + i);
+      }
+      __syncthreads();
+      const int r0 = t_begin * 16, nq = (t_end - t_begin) * 4;  // float4 columns of the band
+      for (int i = tid; i < nq * a.T; i += kThreads) {
+        const int t = i / nq, r = r0 + 4 * (i % nq);
+        float4 v[4];
+        int p[4];
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = 0; j0 < a.topk; j0 += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            p[u] = j0 + u < a.topk ? sp_s[t * a.topk + j0 + u] : -1;
+            if (p[u] >= 0) v[u] = __ldcg(reinterpret_cast<const float4 *>(a.out + (size_t)p[u] * a.out_ld + r));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (p[u] >= 0) {
+              const float w = w_s[t * a.topk + j0 + u];
+              acc.x = fmaf(w, v[u].x, acc.x);
+              acc.y = fmaf(w, v[u].y, acc.y);
+              acc.z = fmaf(w, v[u].z, acc.z);
+              acc.w = fmaf(w, v[u].w, acc.w);
+            }
         }
-        a.y[(size_t)t * a.out_ld + r] = acc;
+        *reinterpret_cast<float4 *>(a.y + (size_t)t * a.out_ld + r) = acc;
       }
     }
   }
@@ -493,7 +653,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
 }
 
 template <class Kern>
-cudaError_t launch_ex(Kern fn, dim3 grid, size_t smem, bool pdl, cudaStream_t stream,
+cudaError_t launch_ex(Kern fn, dim3 grid, int threads, size_t smem, bool pdl, cudaStream_t stream,
                       const DecodeArgs &a) {
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -501,7 +661,7 @@ cudaError_t launch_ex(Kern fn, dim3 grid, size_t smem, bool pdl, cudaStream_t st
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -514,12 +674,12 @@ cudaError_t launch_ex(Kern fn, dim3 grid, size_t smem, bool pdl, cudaStream_t st
 
 template <int MODE, int NT>
 cudaError_t launch_decode(const DecodeArgs &a, int grid_y, cudaStream_t stream) {
-  const int nb = a.K / 32;
-  const size_t smem = (size_t)NT * nb * 2 * 32 * (MODE == 1 ? 8 : 16) + kRingBytes;
-  return launch_ex(moe_decode_kernel<MODE, NT>, dim3(a.bands, grid_y), smem, a.pdl, stream, a);
+  const size_t smem = (size_t)decode_stage_bytes(MODE, NT, false, a.K) + (size_t)kW2 * kS2 * kStageBytes;
+  return launch_ex(moe_decode_kernel<MODE, NT, kW2, kS2, false>, dim3(a.bands, grid_y), kW2 * 32, smem, a.pdl,
+                   stream, a);
 }
 
-int bands_for_tpw(int rows, int tpw) { return (rows / 16 + kWarps * tpw - 1) / (kWarps * tpw); }
+int bands_for_tpw(int rows, int tpw) { return (rows / 16 + kW2 * tpw - 1) / (kW2 * tpw); }
 
 DecodeArgs mlp1_args(const MoeDeviceWeights &w, const uint16_t *x, const int32_t *perm,
                      const int32_t *sigma, const int32_t *counts, const int32_t *offsets,
@@ -570,21 +730,23 @@ DecodeArgs mlp2_args(const MoeDeviceWeights &w, const float *h, const int32_t *c
 cudaError_t launch_moe_mlp1_decode(const MoeDeviceWeights &w, const uint16_t *x,
                                    const int32_t *perm, const int32_t *sigma,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *h,
+                                   int expert_base, int n_local_experts, float *h, int *err,
                                    cudaStream_t stream) {
   if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
   DecodeArgs a = mlp1_args(w, x, perm, sigma, counts, offsets, h);
   a.expert_base = expert_base;
+  a.err = err;
   return launch_decode<1, 1>(a, n_local_experts, stream);
 }
 
 cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
                                    const int32_t *counts, const int32_t *offsets, int n_slots,
-                                   int expert_base, int n_local_experts, float *y_slot,
+                                   int expert_base, int n_local_experts, float *y_slot, int *err,
                                    cudaStream_t stream) {
   if (n_slots == 0 || n_local_experts == 0) return cudaSuccess;
   DecodeArgs a = mlp2_args(w, h, counts, offsets, y_slot);
   a.expert_base = expert_base;
+  a.err = err;
   return launch_decode<2, 1>(a, n_local_experts, stream);
 }
 
@@ -607,9 +769,10 @@ cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
   a.pdl = s.pdl;
   a.T = T;
   a.idx = idx;
+  a.err = s.err;
   if (T <= 8 && T * w.k <= kMaxAllTokActive && w.E <= 256) {
-    const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + kRingBytes;
-    return launch_ex(mlp1_alltok_kernel, dim3(s.n_sms), smem, a.pdl, stream, a);
+    const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1 * kS1 * kStageBytes;
+    return launch_ex(mlp1_alltok_kernel<kW1, kS1>, dim3(s.n_sms), kW1 * 32, smem, a.pdl, stream, a);
   }
   a.bands = s.bands1;
   return launch_decode<1, 1>(a, s.max_active, stream);
@@ -626,11 +789,18 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
   a.n_active = s.n_active;
   a.bands = s.bands2;
   a.pdl = s.pdl;
+  a.err = s.err;
   a.band_done = band_done;
   a.T = T;
   a.slot_pos = slot_pos;
   a.wts = wts;
   a.y = y;
+  if (T <= 8 && s.max_active <= s.n_sms) {
+    // persistent grid, bands per expert from the device's active count
+    a.dyn_bands = 1;
+    const size_t smem = (size_t)decode_stage_bytes(2, 1, true, a.K) + (size_t)kW3 * kS3 * kStageBytes;
+    return launch_ex(moe_decode_kernel<2, 1, kW3, kS3, true>, dim3(s.n_sms), kW3 * 32, smem, a.pdl, stream, a);
+  }
   return launch_decode<2, 1>(a, s.max_active, stream);
 }
 

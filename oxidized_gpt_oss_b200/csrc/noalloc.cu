@@ -146,12 +146,12 @@ extern "C" int oxg_moe_forward_noalloc(oxg_ctx *ctx, int layer, const uint16_t *
       break;
     }
     if ((st = oxg::launch_moe_mlp1_decode(w, x, c.perm, c.sigma, c.counts, c.offsets, S, 0, w.E,
-                                          c.h, stream)) != cudaSuccess) {
+                                          c.h, nullptr, stream)) != cudaSuccess) {
       rc = cuda_error(ctx, st, "mlp1 launch");
       break;
     }
     if ((st = oxg::launch_moe_mlp2_decode(w, c.h, c.counts, c.offsets, S, 0, w.E, c.y_slot,
-                                          stream)) != cudaSuccess) {
+                                          nullptr, stream)) != cudaSuccess) {
       rc = cuda_error(ctx, st, "mlp2 launch");
       break;
     }

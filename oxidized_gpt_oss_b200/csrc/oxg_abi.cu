@@ -512,7 +512,12 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
   sched.bands2 = oxg::decode_bands(d.hidden, exp_active, ctx->n_sms);
   sched.n_sms = ctx->n_sms;
   sched.pdl = true;
-  const int n_bands = mxf ? 4 * ((d.hidden + 127) / 128) : sched.bands2;
+  sched.err = ctx->ws.err;
+  // counters the mlp2 kernel's fused combine uses (zeroed by route_small):
+  // per 128-row band quarter (block-scaled), per band (f16; at most 8 tokens
+  // the bands are chosen on the device, at most one per 16-row tile and SM)
+  const int n_bands = mxf ? 4 * ((d.hidden + 127) / 128)
+                          : std::max(sched.bands2, std::min(d.hidden / 16, ctx->n_sms));
   if (n_bands > kMaxBands) return fail(ctx, OXG_ERR_UNSUPPORTED, "too many row bands (%d)", n_bands);
   oxg::RouteSmallArgs ra{};
   ra.x = x;
@@ -584,6 +589,7 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
                                                ctx->ws.wts, ctx->ws.y_slot, y, ctx->stream);
            }),
            "mlp2 launch");
+  ctx->prefill_pending = true;  // the weight streams report wait timeouts in the error word
   return OXG_OK;
 }
 
@@ -699,12 +705,12 @@ int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, i
   OXG_CUDA(ctx, launch(ctx, "moe_mlp1_decode", [&] {
              return oxg::launch_moe_mlp1_decode(w, x, ctx->ws.perm, ctx->ws.sigma, ctx->ws.counts,
                                                 ctx->ws.offsets, S, 0, d.n_experts, ctx->ws.h,
-                                                ctx->stream);
+                                                ctx->ws.err, ctx->stream);
            }),
            "mlp1 launch");
   OXG_CUDA(ctx, launch(ctx, "moe_mlp2_decode", [&] {
              return oxg::launch_moe_mlp2_decode(w, ctx->ws.h, ctx->ws.counts, ctx->ws.offsets, S,
-                                                0, d.n_experts, ctx->ws.y_slot, ctx->stream);
+                                                0, d.n_experts, ctx->ws.y_slot, ctx->ws.err, ctx->stream);
            }),
            "mlp2 launch");
   OXG_CUDA(ctx, launch(ctx, "combine", [&] {
@@ -712,6 +718,7 @@ int forward_device(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, i
                                         d.hidden, d.top_k, y, ctx->stream);
            }),
            "combine launch");
+  ctx->prefill_pending = true;
   return OXG_OK;
 }
 

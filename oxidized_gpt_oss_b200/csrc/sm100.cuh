@@ -61,13 +61,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits for the phase of parity `parity` to complete; returns false (and
-// records `code` in *err) if it does not within the budget.
+// records `code` in *err when err is not null) if it does not within the
+// budget.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
   if (mbar_test_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > kWaitBudgetCycles) {
-      atomicCAS(err, 0, code);
+      if (err) atomicCAS(err, 0, code);
       return false;
     }
   }
@@ -136,6 +137,16 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, int
 // proxy (tensor cores, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Contiguous global -> shared copy by the TMA engine (no tensor map):
+// addresses 16-byte aligned, bytes a multiple of 16; completes `bytes`
+// transaction bytes on the mbarrier.
+__device__ __forceinline__ void bulk_copy(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar,
                                             int c0, int c1) {
