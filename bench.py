@@ -187,6 +187,24 @@ def run_reference(args):
         unit = "GB/s"
         sample = f"{rows} rows x {c1} cols of mlp1 per step ({per_step_bytes} B algorithmic)"
         config = {"workload": "dequant_layer", "rows": 32 * 5760 + 32 * 2880, "cols": 2880}
+    elif args.workload == "model_decode":
+        # bounded sample: one decode token through one MoE block per step
+        # (the reference's algorithm), scaled to the model's 24 layers
+        d = synth.moe_layer(seed=0)
+        x = synth.activations(0, 1, d["hidden"])
+        L = oracle.RefLayer(oracle.Weights(d), x)
+        L.forward(x, nthreads=1)
+        n = max(1, min(args.steps, 8))
+        t0 = time.perf_counter()
+        for _ in range(n):
+            L.forward(x, nthreads=1)
+        per_token = (time.perf_counter() - t0) / n * synth.GPT_OSS_20B_MODEL["n_layers"]
+        value, unit = 1.0 / per_token, "tokens/s"
+        dt = per_token * args.steps
+        threads = 1
+        sample = (f"{n} decode tokens through one MoE block (reference algorithm, single thread) x "
+                  f"{synth.GPT_OSS_20B_MODEL['n_layers']} layers; attention and LM head not counted")
+        config = model_config(args, synth.GPT_OSS_20B_MODEL, args.prompt)
     else:
         # bounded sample of the workload's tokens: one per host thread
         T = min(args.tokens, max(threads, 1))
@@ -626,13 +644,175 @@ def run_dequant(args, ws, rank, local):
     return out
 
 
+MODEL_KERNELS = ("embed_norm", "linear_qkv", "qkv_rope", "attention", "linear_o", "residual_norm", "route_small",
+                 "moe_mlp1_decode", "moe_mlp2_decode", "lm_head", "argmax")
+
+
+def model_config(args, d, prompt):
+    return {"workload": "gpt_oss_20b_decode", "layers": d["n_layers"], "hidden": d["hidden"],
+            "heads": f"{d['n_heads']}q/{d['n_kv_heads']}kv x {d['head_dim']}", "vocab": d["vocab"],
+            "sliding_window": d["sliding_window"], "experts": d["n_experts"], "top_k": d["top_k"],
+            "batch": 1, "prompt_tokens": prompt, "decode_steps": args.steps,
+            "weights": "random init: attention/embeddings bf16, experts mxfp4 e2m1 + e8m0[118,126]",
+            "l2": "inputs larger than L2: every step streams ~3.7 GB of weights",
+            "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "single"}
+
+
+def run_model(args, ws, rank, local):
+    """Greedy decode of the full 24-layer gpt-oss-20b architecture, batch 1:
+    a prompt of ``--prompt`` tokens, then ``--steps`` timed one-token steps
+    (each: embedding, 24 x (attention + MoE block), LM head, argmax fed back on
+    the device)."""
+    import torch
+    from oxidized_gpt_oss_b200 import synth
+    from oxidized_gpt_oss_b200.model import GPTModel
+
+    device = torch.device("cuda", local)
+    over = {} if args.model_layers is None else {"n_layers": args.model_layers}
+    m = synth.model_weights_device(seed=rank, device=device, **over)
+    d = m["dims"]
+    P = args.prompt
+    max_seq = P + args.warmup + args.steps + 8
+    g = GPTModel(m, max_seq=max_seq, max_tokens=min(P, 2048))
+    del m
+    torch.cuda.empty_cache()
+    ctx = g.ctx
+    rng = np.random.default_rng(1234 + rank)
+    prompt = rng.integers(0, d["vocab"], P).astype(np.int32)
+    prompt_dev = torch.from_numpy(prompt).to(device)
+    first = torch.zeros(1, dtype=torch.int32, device=device)
+    toks = torch.zeros(args.steps, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record(stream)
+    g.forward_device(prompt_dev, 1, None, first)
+    ev[1].record(stream)
+    warm = g.decode(args.warmup).clone() if args.warmup else torch.zeros(0, dtype=torch.int32, device=device)
+    torch.cuda.synchronize()
+    g.sync()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    launches0 = ctx.launches()
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        torch.cuda.synchronize()
+        ev[2].record(stream)
+        g.decode(args.steps, out=toks)  # one eager step, then replays of the captured step
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+    g.sync()
+    ms = ev[2].elapsed_time(ev[3])
+    launches = ctx.launches() - launches0
+    ms_max = max_over_ranks(ms, ws)
+    seq = np.concatenate([first.cpu().numpy(), warm.cpu().numpy(), toks.cpu().numpy()])
+
+    # per-kernel device time: eager steps (library CUDA events around each
+    # launch), each queued behind a GPU sleep so no host gap enters a bracket
+    w0 = args.warmup
+    g.reset_kv_cache()
+    g.forward_device(prompt_dev, 1, None, first)
+    cur = first.clone()
+    nxt = torch.zeros(1, dtype=torch.int32, device=device)
+    torch.cuda.synchronize()
+    ctx.profile(True)
+    ctx.profile_reset()
+    n_prof = 8
+    for i in range(n_prof):
+        torch.cuda._sleep(40_000_000)
+        g.forward_device(cur, 1, None, nxt)
+        cur.copy_(nxt)
+        torch.cuda.synchronize()
+    k_ms = {n: ctx.profile_read(n) for n in MODEL_KERNELS}
+    k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
+    ctx.profile(False)
+    same = int(cur.item()) == int(seq[n_prof])
+
+    # algorithmic HBM bytes of one step (weights streamed once, KV read once)
+    H, V, L = d["hidden"], d["vocab"], d["n_layers"]
+    nh, nkv, hd, W = d["n_heads"], d["n_kv_heads"], d["head_dim"], d["sliding_window"]
+    Nq, Nkv = nh * hd, nkv * hd
+    qkv_b = (Nq + 2 * Nkv) * H * 2
+    o_b = H * Nq * 2
+    mlp1_w = 2 * d["intermediate"] * H // 2 + 2 * d["intermediate"] * H // 32 + 2 * d["intermediate"] * 2
+    mlp2_w = H * d["intermediate"] // 2 + H * d["intermediate"] // 32 + H * 2
+    head_b = V * H * 2 + V * 4
+    pos_mid = P + w0 + args.steps / 2
+    kv_b = sum(2 * nkv * hd * 2 * (min(W, pos_mid) if (li % 2 == 0 and W) else pos_mid) for li in range(L))
+    per_kernel_bytes = {"linear_qkv": L * qkv_b, "linear_o": L * o_b, "moe_mlp1_decode": L * d["top_k"] * mlp1_w,
+                        "moe_mlp2_decode": L * d["top_k"] * mlp2_w, "lm_head": head_b, "attention": kv_b}
+    step_bytes = sum(per_kernel_bytes.values()) + L * d["n_experts"] * H * 2
+    hbm, hbm_kind = peaks()
+    kern = {}
+    for n, (t, cnt) in k_ms.items():
+        per_step_ms = t / n_prof
+        e = {"us_per_step": per_step_ms * 1e3, "launches_per_step": cnt / n_prof}
+        if n in per_kernel_bytes:
+            e["gbs"] = per_kernel_bytes[n] / (per_step_ms * 1e-3) / 1e9
+        kern[n] = e
+    dom = max((n for n in kern if n in per_kernel_bytes), key=lambda n: kern[n]["us_per_step"])
+    dom_ms, dom_n = k_ms[dom]
+    achieved = per_kernel_bytes[dom] * n_prof / (dom_ms * 1e-3) / 1e9
+
+    # end to end through oxg_model_generate: host prompt in, host tokens out
+    n_new = w0 + args.steps + 1
+    g.generate(prompt[: min(P, 64)], 2)  # warm the call path
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out_tokens = g.generate(prompt, n_new)
+    e2e_s = time.perf_counter() - t0
+    e2e_same = out_tokens == seq.tolist()
+
+    out = {"metric": METRIC, "value": ws * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 activations and attention weights, mxfp4 experts, f32 accumulate",
+           "data": "synthetic", "config": model_config(args, d, P),
+           "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "peak_kind": hbm_kind,
+                        "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                        "algorithmic_bytes_per_launch": per_kernel_bytes[dom] / max(dom_n / n_prof, 1),
+                        "avg_launch_us": dom_ms / max(dom_n, 1) * 1e3},
+           "step": {"hbm_gbs": step_bytes / (ms / args.steps * 1e-3) / 1e9,
+                    "frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / hbm, "bytes": step_bytes,
+                    "kernels": kern, "prefill_ms": prefill_ms, "prefill_tokens": P,
+                    "eager_steps_match_graph_steps": same, "generate_matches_device_loop": e2e_same,
+                    "kernel_times": "eager steps queued behind a GPU sleep, library CUDA events per launch"},
+           "e2e": {"value": n_new / e2e_s, "unit": "tokens/s",
+                   "what": f"oxg_model_generate: {P}-token host prompt, {n_new} greedy tokens to the host "
+                           f"(prompt prefill included)",
+                   "h2d_bytes_per_step": P * 4 / n_new, "d2h_bytes_per_step": 4},
+           "gpu_launches": launches,
+           "clocks": clk.summary()}
+    if rank == 0 and ws == 1:
+        out["cpu_baseline"] = cpu_baseline_model(d)
+    g.release()
+    return out
+
+
+def cpu_baseline_model(d):
+    """The reference's algorithm for one decode token through one MoE block
+    (REF-FAITHFUL oracle, single thread), scaled to the model's layers;
+    attention and the LM head are left out, so this bounds the reference's
+    CPU decode rate from above."""
+    from oxidized_gpt_oss_b200 import synth
+    d0 = synth.moe_layer(seed=0)
+    x = synth.activations(0, 1, d0["hidden"])
+    b = cpu_baseline_moe(d0, x, 1)
+    per_token_s = d["n_layers"] / b["value"]
+    return {"value": 1.0 / per_token_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"one token through one MoE block (the reference's algorithm, single thread, "
+                      f"{1.0 / b['value']:.2f} s) x {d['n_layers']} layers; attention and LM head not counted"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant"], default="moe_prefill")
+    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant", "model_decode"],
+                    default="moe_prefill")
+    ap.add_argument("--prompt", type=int, default=2048, help="model_decode: prompt tokens")
+    ap.add_argument("--model-layers", type=int, default=None, help="model_decode: layers (default 24)")
     ap.add_argument("--no-decode", action="store_true",
                     help="moe_prefill on one GPU: skip the decode measurement added to the line")
     ap.add_argument("--tokens", type=int, default=None,
@@ -660,7 +840,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe}[args.workload]
+        run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe,
+               "model_decode": run_model}[args.workload]
         out = run(args, ws, rank, local)
         if args.workload == "moe_prefill" and ws == 1 and not args.no_decode:
             # the metric's decode half (tokens/s and HBM GB/s at 8 tokens), same process

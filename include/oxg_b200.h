@@ -260,6 +260,86 @@ OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
 OXG_API int oxg_moe_forward_noalloc(oxg_ctx *ctx, int layer, const uint16_t *x_dev,
                                     int n_tokens, float *y_dev);
 
+/* ---- Full decoder (gpt-oss-20b architecture) --------------------------------
+ * The transformer around the MoE block, for greedy generation on one GPU:
+ * embedding, per layer RMSNorm -> q/k/v projections + RoPE -> attention
+ * (GQA, sliding window on even layers, learned sinks) -> o projection +
+ * residual -> RMSNorm -> MoE block (the layer's oxg_moe_upload) + residual,
+ * final RMSNorm, LM head, argmax. Replaces GPTModel (src/model.rs:19-27,
+ * 713-741), TransformerLayer::forward (src/model.rs:848-887),
+ * Attention::forward (src/model.rs:899-1084) and InferenceEngine's greedy
+ * loop (src/inference.rs:62-97). Activations are bf16 into every matrix
+ * product and f32 in the residual stream; K/V are cached as bf16. */
+
+typedef struct {
+  int n_layers;        /* 24 */
+  int hidden;          /* H = 2880; multiple of 64, equal to the MoE layers' hidden */
+  int n_heads;         /* 64 query heads */
+  int n_kv_heads;      /* 8; n_heads / n_kv_heads <= 16 */
+  int head_dim;        /* 64 (the only supported value) */
+  int vocab;           /* 201088 */
+  int sliding_window;  /* 128: even-indexed layers see keys p-127..p (src/config.rs:93-101); 0: none */
+  int max_seq;         /* KV-cache capacity in positions */
+  int max_tokens;      /* largest n_tokens of one oxg_model_forward (prompts are chunked) */
+  float rope_theta;    /* 150000 (src/config.rs:122) */
+  float rms_eps;       /* 1e-5 (src/model.rs:433) */
+} oxg_model_dims;
+
+/* One layer's attention weights (host or device pointers, bf16 unless noted;
+ * checkpoint names of src/model.rs:148-412). */
+typedef struct {
+  const uint16_t *attn_norm;       /* [H] "input_layernorm.weight" */
+  const uint16_t *wq, *wk, *wv;    /* [n_heads*64, H], [n_kv_heads*64, H] x 2 "self_attn.{q,k,v}_proj.weight" */
+  const uint16_t *bq, *bk, *bv;    /* biases [rows] or NULL (zero) */
+  const uint16_t *wo;              /* [H, n_heads*64] "self_attn.o_proj.weight" */
+  const uint16_t *bo;              /* [H] or NULL */
+  const uint16_t *sinks;           /* [n_heads] learned sink logits, or NULL for none */
+  const uint16_t *mlp_norm;        /* [H] "post_attention_layernorm.weight" */
+} oxg_attn_weights;
+
+/* Allocates the KV cache, RoPE tables and activations for `dims` (replacing
+ * any earlier model on the context). */
+OXG_API int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims);
+/* Token embedding [V, H], LM head [V, H] ("lm_head.weight"; pass the
+ * embedding again for tied weights) and final norm [H] (src/model.rs:98-138). */
+OXG_API int oxg_model_upload_embeddings(oxg_ctx *ctx, const uint16_t *embed, const uint16_t *unembed,
+                                        const uint16_t *final_norm);
+OXG_API int oxg_model_upload_attention(oxg_ctx *ctx, int layer, const oxg_attn_weights *w);
+/* Empties the KV cache (GPTModel::reset_kv_cache, src/model.rs:743-747). */
+OXG_API int oxg_model_reset(oxg_ctx *ctx);
+/* Number of positions in the KV cache. */
+OXG_API int oxg_model_position(oxg_ctx *ctx, int *pos);
+/* GPTModel::forward (src/model.rs:713-741) on device data: appends n_tokens
+ * tokens (int32 ids, device) at the current position, and for the last
+ * n_logits of them (0 <= n_logits <= min(n_tokens, 128)) writes the logits
+ * [n_logits, V] f32 to logits_dev and the greedy choice (argmax, ties to the
+ * last index as src/sampler.rs:7-16) to next_dev [n_logits]; either output may
+ * be NULL. Asynchronous on the context's stream; a token id outside [0, V)
+ * is reported by the next oxg_sync. */
+OXG_API int oxg_model_forward(oxg_ctx *ctx, const int32_t *tokens_dev, int n_tokens, int n_logits,
+                              float *logits_dev, int32_t *next_dev);
+/* The decode loop of src/inference.rs:77-92 at temperature 0 on the device:
+ * n_steps one-token steps, each feeding the previous greedy token back,
+ * starting from the greedy token of the last oxg_model_forward (which must
+ * have had n_logits >= 1) or of the last step; tokens_dev [n_steps] receives
+ * the new tokens. The step is captured once as a CUDA graph and replayed
+ * (the first step of a call runs eagerly; the capture is redone when layers
+ * or the scratch were reallocated). Asynchronous. */
+OXG_API int oxg_model_decode(oxg_ctx *ctx, int n_steps, int32_t *tokens_dev);
+/* InferenceEngine::generate_chat's loop at temperature 0 (src/inference.rs:62-97)
+ * from host memory: empties the cache, runs the prompt (in chunks of
+ * max_tokens), then n_new - 1 one-token steps that feed each greedy token back
+ * on the device; writes the n_new generated ids to tokens_host. Synchronous. */
+OXG_API int oxg_model_generate(oxg_ctx *ctx, const int32_t *prompt_host, int n_prompt, int n_new,
+                               int32_t *tokens_host);
+/* Routing tap (the expert ids src/moe.rs:51-73 chooses, per layer): while
+ * set, every oxg_model_forward of at most max_tokens tokens copies each
+ * layer's chosen experts [n_tokens, k] (int32, selection order) to
+ * idx_dev + layer * max_tokens * k. NULL switches it off. Graph-replayed
+ * decode steps do not record. */
+OXG_API int oxg_model_route_tap(oxg_ctx *ctx, int32_t *idx_dev, int max_tokens);
+OXG_API int oxg_model_release(oxg_ctx *ctx);
+
 /* ---- measurement (no reference counterpart: the reference's only timing is
  * the --bench wall clock of src/main.rs:159-164) --------------------------- */
 

@@ -50,6 +50,18 @@ class MoeWeights(ctypes.Structure):
                                                "w2_blocks", "w2_scales", "b2")]
 
 
+class ModelDims(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int),
+                ("sliding_window", ctypes.c_int), ("max_seq", ctypes.c_int), ("max_tokens", ctypes.c_int),
+                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+
+class AttnWeights(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo", "bo",
+                                               "sinks", "mlp_norm")]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
@@ -85,6 +97,16 @@ SIGNATURES = {
     "oxg_moe_forward_ep": (_I, [_CTX, _I, _P, _I, _P]),
     "oxg_ep_close": (_I, [_CTX]),
     "oxg_ep_last_received": (_I, [_CTX, ctypes.POINTER(ctypes.c_longlong)]),
+    "oxg_model_init": (_I, [_CTX, ctypes.POINTER(ModelDims)]),
+    "oxg_model_upload_embeddings": (_I, [_CTX, _P, _P, _P]),
+    "oxg_model_upload_attention": (_I, [_CTX, _I, ctypes.POINTER(AttnWeights)]),
+    "oxg_model_reset": (_I, [_CTX]),
+    "oxg_model_position": (_I, [_CTX, ctypes.POINTER(ctypes.c_int)]),
+    "oxg_model_forward": (_I, [_CTX, _P, _I, _I, _P, _P]),
+    "oxg_model_generate": (_I, [_CTX, _P, _I, _I, _P]),
+    "oxg_model_decode": (_I, [_CTX, _I, _P]),
+    "oxg_model_route_tap": (_I, [_CTX, _P, _I]),
+    "oxg_model_release": (_I, [_CTX]),
     "oxg_profile_enable": (_I, [_CTX, _I]),
     "oxg_profile_read": (_I, [_CTX, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_int)]),

@@ -1,0 +1,67 @@
+// model.h — host-side launchers of the transformer kernels around the MoE
+// block (model.cu). Internal to the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace oxg {
+
+// Residual update fused with the RMS norm, one row per CTA (see model.cu).
+struct NormArgs {
+  float *res = nullptr;             // [rows, H] f32 residual stream (updated in place)
+  int rows = 0, H = 0;
+  const int32_t *tokens = nullptr;  // embedding mode: token ids [rows]
+  const uint16_t *embed = nullptr;  // [V, H] bf16
+  int V = 0;
+  const float *add = nullptr;       // add mode: S partial arrays, add_stride floats apart
+  int S = 1;
+  size_t add_stride = 0;
+  const uint16_t *add_bias = nullptr;  // [H] bf16 or null
+  const uint16_t *gamma = nullptr;     // [H] bf16
+  float eps = 1e-5f;
+  uint16_t *out = nullptr;          // [rows, H] bf16
+  int *err = nullptr;               // receives 60 on a token id outside [0, V)
+};
+cudaError_t launch_residual_norm(const NormArgs &a, cudaStream_t stream);
+
+// Linear layer out[s][t][n] = sum_{k in split s} x[t][k] W[n][k] (bf16 in,
+// f32 out). K must be a multiple of 64, x rows 16-byte aligned (ldx % 8 == 0).
+// linear_splits picks the K split for a batch: enough CTAs for 2 per SM, at
+// most max_rows / padded(T) splits (the partial buffer's capacity).
+int linear_splits(int N, int K, int T, int n_sms, int max_rows);
+cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, int N, int K, int splits,
+                          float *out, cudaStream_t stream);
+
+// q/k/v epilogue: bias, RoPE (tables [max_seq, 32] of cos and sin), bf16 q
+// [T, nh * 64] and K/V cache rows [nkv, max_seq, 64] at positions pos0 + t.
+// pos_dev, when not null, replaces pos0 by the position held on the device.
+cudaError_t launch_qkv_post(const float *part, int S, int T, int nh, int nkv, const uint16_t *bias,
+                            const float *rope_cos, const float *rope_sin, int pos0, const int32_t *pos_dev,
+                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream);
+
+struct AttnArgs {
+  const uint16_t *q = nullptr;   // [T, nh * 64] bf16
+  const uint16_t *kc = nullptr, *vc = nullptr;  // [nkv, max_seq, 64] bf16
+  int T = 0, nh = 0, nkv = 0, max_seq = 0, pos0 = 0;
+  int window = 0;                // > 0: keys p - window + 1 .. p
+  float scale = 0.125f;
+  const uint16_t *sinks = nullptr;  // [nh] bf16 or null
+  float *part = nullptr;         // decode split partials (attn_part_floats)
+  const int32_t *pos_dev = nullptr;  // T == 1: the query position read on the device (graph replays)
+  uint16_t *out = nullptr;       // [T, nh * 64] bf16
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream);
+size_t attn_part_floats(int nkv, int G, int max_seq);
+int attn_max_group();
+
+// next[row] = greedy choice (next may be null). With state (one row): the
+// decode-step bookkeeping {position, step, token}: out_seq[step] = token,
+// state token = token, position and step advance by one.
+cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *next, int32_t *state, int32_t *out_seq,
+                          cudaStream_t stream);
+// state = {pos, 0, *tok}
+cudaError_t launch_set_state(int32_t *state, int pos, const int32_t *tok, cudaStream_t stream);
+
+}  // namespace oxg

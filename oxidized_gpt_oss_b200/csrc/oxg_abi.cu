@@ -153,6 +153,8 @@ struct oxg_ctx {
   long long launches = 0;
   bool prefill_pending = false;  // a prefill ran since the error word was last read
   Profiler prof;
+  oxg::ModelState *model = nullptr;  // full-model state (model_abi.cu)
+  unsigned long long epoch = 0;  // bumped when uploaded layers or the scratch move
   // Expert-parallel receive side (oxg_moe_experts): kept apart from ws so
   // that sizing it for the received rows never discards the dispatch's
   // slot positions and weights that oxg_moe_combine reads.
@@ -354,6 +356,7 @@ int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
     OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     cudaFree(ctx->ws.base);
     ctx->ws = Scratch{};
+    ctx->epoch += 1;
   }
   void *p = nullptr;
   OXG_CUDA(ctx, cudaMalloc(&p, need), "cudaMalloc(scratch)");
@@ -795,6 +798,50 @@ bool ctx_layer(oxg_ctx *ctx, int layer, MoeDeviceWeights *w, int *device, cudaSt
 
 int ctx_error(oxg_ctx *ctx, int status, const char *msg) { return fail(ctx, status, "%s", msg); }
 
+int ctx_device(const oxg_ctx *ctx) { return ctx->device; }
+cudaStream_t ctx_stream(const oxg_ctx *ctx) { return ctx->stream; }
+int ctx_n_sms(const oxg_ctx *ctx) { return ctx->n_sms; }
+
+int ctx_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y) {
+  return oxg_moe_forward(ctx, layer, x, T, y, OXG_MODE_AUTO, OXG_PRECISION_PARITY);
+}
+
+int ctx_moe_reserve(oxg_ctx *ctx, int layer, int T) { return oxg_moe_reserve(ctx, layer, T); }
+
+int ctx_moe_hidden(oxg_ctx *ctx, int layer) {
+  Layer *L = get_layer(ctx, layer);
+  return L && !L->sharded() ? L->dims.hidden : 0;
+}
+
+int ctx_moe_topk(oxg_ctx *ctx, int layer) {
+  Layer *L = get_layer(ctx, layer);
+  return L ? L->dims.top_k : 0;
+}
+
+const int32_t *ctx_moe_last_idx(oxg_ctx *ctx) { return ctx->ws.idx; }
+
+void *ctx_prof_begin(oxg_ctx *ctx) {
+  if (!ctx->prof.on) return nullptr;
+  cudaEvent_t a = ctx->prof.get();
+  cudaEventRecord(a, ctx->stream);
+  return (void *)a;
+}
+
+void ctx_prof_end(oxg_ctx *ctx, const char *name, void *begin, cudaError_t st) {
+  if (st == cudaSuccess) ctx->launches += 1;
+  if (ctx->prof.on && begin) {
+    cudaEvent_t b = ctx->prof.get();
+    cudaEventRecord(b, ctx->stream);
+    ctx->prof.recs.push_back(Profiler::Rec{name, (cudaEvent_t)begin, b});
+  }
+}
+
+ModelState *&ctx_model(oxg_ctx *ctx) { return ctx->model; }
+unsigned long long ctx_epoch(const oxg_ctx *ctx) { return ctx->epoch; }
+bool &ctx_profile_flag(oxg_ctx *ctx) { return ctx->prof.on; }
+void ctx_add_launches(oxg_ctx *ctx, long long n) { ctx->launches += n; }
+long long ctx_launch_count(const oxg_ctx *ctx) { return ctx->launches; }
+
 }  // namespace oxg
 
 extern "C" {
@@ -851,6 +898,7 @@ int oxg_ctx_destroy(oxg_ctx *ctx) {
   if (!ctx) return OXG_OK;
   DeviceGuard g(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  oxg::model_free(ctx);
   for (Layer &L : ctx->layers) free_layer(L);
   if (ctx->ws.base) cudaFree(ctx->ws.base);
   if (ctx->ep.base) cudaFree(ctx->ep.base);
@@ -888,7 +936,9 @@ int oxg_sync(oxg_ctx *ctx) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
   DeviceGuard g(ctx->device);
   OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
-  return read_pipeline_error(ctx);
+  const int rc = read_pipeline_error(ctx);
+  if (rc) return rc;
+  return oxg::model_check_error(ctx);
 }
 
 int oxg_dequant_mxfp4(oxg_ctx *ctx, const uint8_t *blocks, size_t n_block_bytes,
@@ -977,6 +1027,7 @@ int upload_impl(oxg_ctx *ctx, int layer, const oxg_moe_dims *dims, const oxg_moe
 
   if ((size_t)layer >= ctx->layers.size()) ctx->layers.resize(layer + 1);
   free_layer(ctx->layers[layer]);
+  ctx->epoch += 1;
   Layer L;
   L.dims = d;
   void *block = nullptr, *stage = nullptr;
@@ -1083,6 +1134,7 @@ int oxg_moe_release(oxg_ctx *ctx, int layer) {
   DeviceGuard g(ctx->device);
   OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
   free_layer(*L);
+  ctx->epoch += 1;
   return OXG_OK;
 }
 

@@ -75,3 +75,95 @@ def moe_bytes_per_expert(hidden: int = 2880, intermediate: int = 2880) -> int:
     """Algorithmic HBM bytes one expert's weights cost a decode step."""
     H, I = hidden, intermediate
     return (2 * I * H // 2 + 2 * I * H // 32 + H * I // 2 + H * I // 32) + (2 * I + H) * 2
+
+
+# ---------------------------------------------------------------------------
+# Full decoder (gpt-oss-20b architecture, random init)
+# ---------------------------------------------------------------------------
+GPT_OSS_20B_MODEL = dict(n_layers=24, hidden=2880, n_heads=64, n_kv_heads=8, head_dim=64, vocab=201088,
+                         sliding_window=128, rope_theta=150000.0, rms_eps=1e-5, intermediate=2880,
+                         n_experts=32, top_k=4, alpha=1.702, limit=7.0)
+
+_ATTN_KEYS = ("attn_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo", "bo", "sinks", "mlp_norm")
+
+
+def model_weights(seed: int = 0, **over) -> dict:
+    """Random-init weights of a gpt-oss-architecture decoder (numpy, host).
+
+    Distributions: embedding bf16 ~N(0, 1); LM head ~N(0, 0.02); RMS-norm
+    weights 1 + N(0, 0.02); q/k/v/o weights ~N(0, 0.02), biases ~N(0, 0.01);
+    sink logits ~N(0, 1); each layer's MoE block as ``moe_layer`` (seed
+    seed * 1000 + 1 + layer). ``over`` overrides fields of
+    ``GPT_OSS_20B_MODEL`` (e.g. fewer layers or a smaller vocab for tests).
+    """
+    d = dict(GPT_OSS_20B_MODEL)
+    d.update(over)
+    rng = np.random.default_rng(seed)
+    H, V, nh, nkv, hd = d["hidden"], d["vocab"], d["n_heads"], d["n_kv_heads"], d["head_dim"]
+    m = dict(dims=d)
+    m["embed"] = _normal_bf16(rng, (V, H), 1.0)
+    m["unembed"] = _normal_bf16(rng, (V, H), 0.02)
+    m["final_norm"] = f32_to_bf16_bits(1.0 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.02))
+    layers = []
+    for layer in range(d["n_layers"]):
+        a = {}
+        a["attn_norm"] = f32_to_bf16_bits(1.0 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.02))
+        a["wq"] = _normal_bf16(rng, (nh * hd, H), 0.02)
+        a["wk"] = _normal_bf16(rng, (nkv * hd, H), 0.02)
+        a["wv"] = _normal_bf16(rng, (nkv * hd, H), 0.02)
+        a["bq"] = _normal_bf16(rng, (nh * hd,), 0.01)
+        a["bk"] = _normal_bf16(rng, (nkv * hd,), 0.01)
+        a["bv"] = _normal_bf16(rng, (nkv * hd,), 0.01)
+        a["wo"] = _normal_bf16(rng, (H, nh * hd), 0.02)
+        a["bo"] = _normal_bf16(rng, (H,), 0.01)
+        a["sinks"] = _normal_bf16(rng, (nh,), 1.0)
+        a["mlp_norm"] = f32_to_bf16_bits(1.0 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.02))
+        a["moe"] = moe_layer(seed * 1000 + 1 + layer, hidden=H, intermediate=d["intermediate"],
+                             n_experts=d["n_experts"], top_k=d["top_k"], alpha=d["alpha"], limit=d["limit"])
+        layers.append(a)
+    m["layers"] = layers
+    return m
+
+
+def model_weights_device(seed: int = 0, device="cuda", **over) -> dict:
+    """The same architecture and distributions as ``model_weights``, drawn on
+    the GPU with torch's generator (a different stream of random numbers) —
+    for full-size benchmarks, where drawing ~13 GB on the host would dominate
+    the set-up time. bf16 tensors are returned as int16 bit patterns."""
+    import torch
+
+    d = dict(GPT_OSS_20B_MODEL)
+    d.update(over)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, V, nh, nkv, hd = d["hidden"], d["vocab"], d["n_heads"], d["n_kv_heads"], d["head_dim"]
+    I, E = d["intermediate"], d["n_experts"]
+
+    def normal(shape, std, mean=0.0):
+        t = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std + mean
+        return t.to(torch.bfloat16).view(torch.int16)
+
+    def codes(shape):
+        return torch.randint(0, 256, shape, generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+
+    def scales(shape, lo=118, hi=126):
+        return torch.randint(lo, hi + 1, shape, generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+
+    m = dict(dims=d)
+    m["embed"] = normal((V, H), 1.0)
+    m["unembed"] = normal((V, H), 0.02)
+    m["final_norm"] = normal((H,), 0.02, 1.0)
+    layers = []
+    for _ in range(d["n_layers"]):
+        a = dict(attn_norm=normal((H,), 0.02, 1.0), wq=normal((nh * hd, H), 0.02), wk=normal((nkv * hd, H), 0.02),
+                 wv=normal((nkv * hd, H), 0.02), bq=normal((nh * hd,), 0.01), bk=normal((nkv * hd,), 0.01),
+                 bv=normal((nkv * hd,), 0.01), wo=normal((H, nh * hd), 0.02), bo=normal((H,), 0.01),
+                 sinks=normal((nh,), 1.0), mlp_norm=normal((H,), 0.02, 1.0))
+        a["moe"] = dict(hidden=H, intermediate=I, n_experts=E, top_k=d["top_k"], alpha=d["alpha"], limit=d["limit"],
+                        router_w=normal((E, H), 0.02), router_b=normal((E,), 0.01),
+                        w1_blocks=codes((E, 2 * I, H // 2)), w1_scales=scales((E, 2 * I, H // 32)),
+                        b1=normal((E, 2 * I), 0.01), w2_blocks=codes((E, H, I // 2)),
+                        w2_scales=scales((E, H, I // 32)), b2=normal((E, H), 0.01))
+        layers.append(a)
+    m["layers"] = layers
+    return m
