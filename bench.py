@@ -725,7 +725,7 @@ def run_model(args, ws, rank, local):
     k_ms = {n: ctx.profile_read(n) for n in MODEL_KERNELS}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     ctx.profile(False)
-    same = int(cur.item()) == int(seq[n_prof])
+    same = int(cur.item()) == int(seq[n_prof]) if n_prof < seq.size else None
 
     # algorithmic HBM bytes of one step (weights streamed once, KV read once)
     H, V, L = d["hidden"], d["vocab"], d["n_layers"]

@@ -68,6 +68,13 @@ constexpr bool kBulk = OXG_DEC_BULK != 0;
 constexpr int kW1 = OXG_DEC_W1, kS1 = OXG_DEC_S1;
 constexpr int kW2 = OXG_DEC_W2, kS2 = OXG_DEC_S2;
 constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
+// At most kDeepTokens tokens (4-8 active experts) a warp streams about one
+// 16-row tile, so the ring depth decides the kernel's time: fewer warps with
+// deeper rings (mlp1: 10 x 16 stages for 1480 warps >= 4 experts x 360
+// tiles; mlp2: 8 x 20, a band being ~5 tiles) fit the same shared memory.
+constexpr int kDeepTokens = 2;
+constexpr int kW1d = 10, kS1d = 16;
+constexpr int kW3d = 8, kS3d = 20;
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
 struct DecodeArgs {
@@ -771,6 +778,10 @@ cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
   a.idx = idx;
   a.err = s.err;
   if (T <= 8 && T * w.k <= kMaxAllTokActive && w.E <= 256) {
+    if (T <= kDeepTokens) {
+      const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1d * kS1d * kStageBytes;
+      return launch_ex(mlp1_alltok_kernel<kW1d, kS1d>, dim3(s.n_sms), kW1d * 32, smem, a.pdl, stream, a);
+    }
     const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1 * kS1 * kStageBytes;
     return launch_ex(mlp1_alltok_kernel<kW1, kS1>, dim3(s.n_sms), kW1 * 32, smem, a.pdl, stream, a);
   }
@@ -798,6 +809,11 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
   if (T <= 8 && s.max_active <= s.n_sms) {
     // persistent grid, bands per expert from the device's active count
     a.dyn_bands = 1;
+    if (T <= kDeepTokens) {
+      const size_t smem = (size_t)decode_stage_bytes(2, 1, true, a.K) + (size_t)kW3d * kS3d * kStageBytes;
+      return launch_ex(moe_decode_kernel<2, 1, kW3d, kS3d, true>, dim3(s.n_sms), kW3d * 32, smem, a.pdl, stream,
+                       a);
+    }
     const size_t smem = (size_t)decode_stage_bytes(2, 1, true, a.K) + (size_t)kW3 * kS3 * kStageBytes;
     return launch_ex(moe_decode_kernel<2, 1, kW3, kS3, true>, dim3(s.n_sms), kW3 * 32, smem, a.pdl, stream, a);
   }
