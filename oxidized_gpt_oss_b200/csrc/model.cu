@@ -184,10 +184,20 @@ struct LinCfg {
 
 __device__ __forceinline__ int swz(int r, int c) { return r * 8 + (c ^ (r & 7)); }
 
+// Orders (value, index) pairs as one 64-bit key: larger value wins, equal
+// values go to the larger index (the reference's Iterator::max_by keeps the
+// last maximum). 0 is below every key; NaN is never a candidate.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  if (v != v) return 0ull;
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)o << 32) | (uint32_t)i;
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kLinThreads)
     linear_kernel(const uint16_t *__restrict__ x, int T, int ldx, const uint16_t *__restrict__ W, int N,
-                  int K, int chunks_per_split, float *__restrict__ out) {
+                  int K, int chunks_per_split, float *__restrict__ out, ArgmaxEpilogue am) {
   constexpr int ST = LinCfg<NT>::kStages;
   extern __shared__ __align__(128) uint8_t lin_smem[];
   uint4 *Ws = reinterpret_cast<uint4 *>(lin_smem);
@@ -276,6 +286,53 @@ __global__ void __launch_bounds__(kLinThreads)
     if (tb < T) {
       if (n_a < N) o[(size_t)tb * N + n_a] = acc[j][1];
       if (n_b < N) o[(size_t)tb * N + n_b] = acc[j][3];
+    }
+  }
+  if constexpr (NT == 8) {
+    if (am.keys) {
+      // greedy choice per token: one 64-bit atomicMax per warp and token,
+      // then the last CTA turns the keys into tokens (and resets them)
+      __shared__ int am_last;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int t = 2 * q + c;
+        unsigned long long best = 0ull;
+        if (n_a < N) best = argmax_key(acc[0][c], n_a);
+        if (n_b < N) {
+          const unsigned long long kb = argmax_key(acc[0][2 + c], n_b);
+          best = kb > best ? kb : best;
+        }
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, off);
+          best = ob > best ? ob : best;
+        }
+        if (g == 0 && t < T && best) atomicMax(am.keys + t, best);
+      }
+      __threadfence();
+      __syncthreads();
+      if (tid == 0)
+        am_last = atomicAdd(am.count, 1u) == gridDim.x * gridDim.y * gridDim.z - 1;
+      __syncthreads();
+      if (am_last) {
+        __threadfence();
+        if (tid < T) {
+          const unsigned long long key = atomicExch(am.keys + tid, 0ull);
+          const int tok = key ? (int)(uint32_t)(key & 0xffffffffull) : 0;
+          if (am.next) am.next[tid] = tok;
+          if (am.state_mode == 1) {  // one-token decode step: feed back and advance
+            am.out_seq[am.state[1]] = tok;
+            am.state[2] = tok;
+            am.state[0] += 1;
+            am.state[1] += 1;
+          } else if (am.state_mode == 2 && tid == T - 1) {
+            am.state[0] = am.set_pos;
+            am.state[1] = 0;
+            am.state[2] = tok;
+          }
+        }
+        if (tid == 0) *am.count = 0u;
+      }
     }
   }
 }
@@ -737,22 +794,26 @@ int linear_splits(int N, int K, int T, int n_sms, int max_rows) {
 }
 
 cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, int N, int K, int splits,
-                          float *out, cudaStream_t stream) {
+                          float *out, cudaStream_t stream, const ArgmaxEpilogue *am) {
   if (T <= 0) return cudaSuccess;
   const int nck = K / kLinK;
   const int per = (nck + splits - 1) / splits;
+  const ArgmaxEpilogue none{};
   if (T <= 8) {
+    if (am && splits != 1) return cudaErrorInvalidValue;
     const dim3 grid((N + kLinRows - 1) / kLinRows, 1, splits);
     cudaError_t st = cudaFuncSetAttribute(linear_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           LinCfg<8>::kSmem);
     if (st != cudaSuccess) return st;
-    linear_kernel<8><<<grid, kLinThreads, LinCfg<8>::kSmem, stream>>>(x, T, ldx, W, N, K, per, out);
+    linear_kernel<8><<<grid, kLinThreads, LinCfg<8>::kSmem, stream>>>(x, T, ldx, W, N, K, per, out,
+                                                                       am ? *am : none);
   } else {
+    if (am) return cudaErrorInvalidValue;
     const dim3 grid((N + kLinRows - 1) / kLinRows, (T + 63) / 64, splits);
     cudaError_t st = cudaFuncSetAttribute(linear_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           LinCfg<64>::kSmem);
     if (st != cudaSuccess) return st;
-    linear_kernel<64><<<grid, kLinThreads, LinCfg<64>::kSmem, stream>>>(x, T, ldx, W, N, K, per, out);
+    linear_kernel<64><<<grid, kLinThreads, LinCfg<64>::kSmem, stream>>>(x, T, ldx, W, N, K, per, out, none);
   }
   return cudaGetLastError();
 }

@@ -31,8 +31,21 @@ cudaError_t launch_residual_norm(const NormArgs &a, cudaStream_t stream);
 // linear_splits picks the K split for a batch: enough CTAs for 2 per SM, at
 // most max_rows / padded(T) splits (the partial buffer's capacity).
 int linear_splits(int N, int K, int T, int n_sms, int max_rows);
+
+// Greedy choice fused into a linear layer's epilogue (T <= 8, one split):
+// per token the largest output and its row (ties to the larger row), through
+// 64-bit atomicMax keys; the last CTA writes next[t] (if not null) and, with
+// state_mode 1, advances the decode state {pos, step, token} (out_seq[step] =
+// token) or, with state_mode 2, sets it to {set_pos, 0, token of row T-1}.
+// keys [T] and count must start at zero; the last CTA leaves them so.
+struct ArgmaxEpilogue {
+  unsigned long long *keys = nullptr;
+  unsigned int *count = nullptr;
+  int32_t *next = nullptr, *state = nullptr, *out_seq = nullptr;
+  int state_mode = 0, set_pos = 0;
+};
 cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, int N, int K, int splits,
-                          float *out, cudaStream_t stream);
+                          float *out, cudaStream_t stream, const ArgmaxEpilogue *am = nullptr);
 
 // q/k/v epilogue: bias, RoPE (tables [max_seq, 32] of cos and sin), bf16 q
 // [T, nh * 64] and K/V cache rows [nkv, max_seq, 64] at positions pos0 + t.

@@ -49,6 +49,8 @@ struct ModelState {
   int32_t *tok = nullptr, *gen = nullptr;
   int32_t *dstate = nullptr;  // decode state {position, step, token} read by the captured step
   int32_t *first = nullptr;   // generate: the prompt's greedy token
+  unsigned long long *am_keys = nullptr;  // fused LM-head argmax keys [8] (zero between uses)
+  unsigned int *am_count = nullptr;       // its finished-CTA counter
   int *err = nullptr;
   int part_rows = 0, max_logits = 0, gen_cap = 0;
   int pos = 0;
@@ -315,7 +317,23 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
             "residual norm launch");
     }
   }
-  if (n_logits > 0) {
+  if (n_logits > 0 && n_logits <= 8) {
+    // LM head with the greedy choice and the decode-state update in its epilogue
+    float *lg = logits_out ? logits_out : M.logits;
+    ArgmaxEpilogue am;
+    am.keys = M.am_keys;
+    am.count = M.am_count;
+    am.next = dstate ? nullptr : (next_out ? next_out : M.tok);
+    am.state = dstate ? dstate : M.dstate;
+    am.out_seq = M.gen;
+    am.state_mode = dstate ? 1 : 2;
+    am.set_pos = pos0 + T;
+    MCUDA(ctx, ctx_launch(ctx, "lm_head", [&] {
+            return launch_linear(M.xn, n_logits, H, M.unembed, d.vocab, H, 1, lg, s, &am);
+          }),
+          "lm head launch");
+    if (dstate) return OXG_OK;  // the caller advances the host position
+  } else if (n_logits > 0) {
     float *lg = logits_out ? logits_out : M.logits;
     MCUDA(ctx, ctx_launch(ctx, "lm_head", [&] {
             return launch_linear(M.xn, n_logits, H, M.unembed, d.vocab, H, 1, lg, s);
@@ -486,6 +504,7 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   const size_t o_lg = take((size_t)M->max_logits * d.vocab * 4);
   const size_t o_tok = take(Tm * 4), o_gen = take((size_t)M->gen_cap * 4), o_err = take(4);
   const size_t o_ds = take(4 * 4), o_first = take(4);
+  const size_t o_amk = take(8 * 8), o_amc = take(4);
   cudaError_t e = cudaMalloc(&M->state, off);
   if (e) {
     delete M;
@@ -508,6 +527,8 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->err = (int *)(b + o_err);
   M->dstate = (int32_t *)(b + o_ds);
   M->first = (int32_t *)(b + o_first);
+  M->am_keys = (unsigned long long *)(b + o_amk);
+  M->am_count = (unsigned int *)(b + o_amc);
   // RoPE tables: angle(pos, i) = pos * theta^(-2i / head_dim), i < head_dim / 2,
   // evaluated in double and rounded once to f32.
   std::vector<float> cs((size_t)d.max_seq * 32), sn((size_t)d.max_seq * 32);
@@ -522,6 +543,8 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   if (!e) e = cudaMemcpy(M->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
   if (!e) e = cudaMemset(M->err, 0, 4);
   if (!e) e = cudaMemset(M->dstate, 0, 16);
+  if (!e) e = cudaMemset(M->am_keys, 0, 8 * 8);
+  if (!e) e = cudaMemset(M->am_count, 0, 4);
   if (e) {
     oxg::free_model(M);
     return oxg::mcuda(ctx, e, "model state initialisation");

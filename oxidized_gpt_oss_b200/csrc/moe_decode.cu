@@ -323,6 +323,7 @@ __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int 
                                         RowOf row_of, const int32_t *sigma) {
   const int K = a.K;
   const int units = NT * 8 * (K / 8);
+#pragma unroll 4
   for (int u = threadIdx.x; u < units; u += blockDim.x) {
     const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
     const int blk = k0 >> 5, qq = (k0 & 31) >> 3, nt = tok >> 3, gg = tok & 7;
@@ -450,6 +451,7 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
       }
     } else {
       const int units = kTokPerPass * (K / 8);
+#pragma unroll 4
       for (int u = tid; u < units; u += kThreads) {
         const int tok = u / (K / 8), k0 = (u % (K / 8)) * 8;
         const int blk = k0 >> 5, qq = (k0 & 31) >> 3;
