@@ -2,7 +2,7 @@
 """Benchmark of the MXFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_prefill|moe_decode|dequant] [--tokens T] [--layers L]
+                    [--workload moe_prefill|moe_decode|dequant|model_decode] [--tokens T] [--layers L]
 
 Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
   moe_prefill (default) 8192 tokens per GPU through one MoE block on the
@@ -12,12 +12,19 @@ Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
               peak. On N GPUs the experts are split 32/N per GPU (expert
               parallel) with NCCL all-to-all dispatch and return; on one GPU
               the line also carries a "decode" object (the moe_decode
-              workload measured in the same process).
+              workload measured in the same process) and a "model_decode"
+              object (the model_decode workload, 64 timed steps).
   moe_decode  one MoE block forward over T tokens (default 8: the 8-token
               gpt-oss-20b block — hidden 2880, 32 experts top-4, MXFP4
               weights with E8M0 scales in [118, 126], bf16 activations).
               Metric: tokens/s; roofline: HBM GB/s of the gate/up kernel.
               N > 1: independent replicas.
+  model_decode greedy decode of the full 24-layer gpt-oss-20b architecture
+              (random init), batch 1: a 2048-token prompt, then --steps
+              one-token steps replayed from a captured CUDA graph. Metric:
+              tokens/s; roofline: HBM GB/s of the slowest weight-streaming
+              kernel; e2e through oxg_model_generate (host prompt in, host
+              tokens out).
   dequant     standalone MXFP4 -> bf16 dequant of one layer's expert tensors
               (32x5760x2880 + 32x2880x2880, E8M0 in [110, 135]). Metric: GB/s
               of algorithmic traffic (423,014,400 B read + 1,592,524,800 B written).
@@ -815,6 +822,8 @@ def main():
     ap.add_argument("--model-layers", type=int, default=None, help="model_decode: layers (default 24)")
     ap.add_argument("--no-decode", action="store_true",
                     help="moe_prefill on one GPU: skip the decode measurement added to the line")
+    ap.add_argument("--no-model", action="store_true",
+                    help="moe_prefill on one GPU: skip the 24-layer decoder measurement added to the line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8 for moe_decode, 8192 for moe_prefill)")
     ap.add_argument("--layers", type=int, default=4)
@@ -850,6 +859,13 @@ def main():
             dec = run_moe(dargs, ws, rank, local)
             out["decode"] = {k: dec[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline", "e2e",
                                                   "config", "cpu_baseline") if k in dec}
+        if args.workload == "moe_prefill" and ws == 1 and not args.no_model:
+            # configuration 2: the full 24-layer decoder, batch 1, greedy decode
+            margs = argparse.Namespace(**vars(args))
+            margs.steps, margs.warmup = 64, 4
+            md = run_model(margs, ws, rank, local)
+            out["model_decode"] = {k: md[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline", "step",
+                                                      "e2e", "config", "cpu_baseline", "gpu_launches") if k in md}
         if rank == 0:
             emit(out)
     finally:
