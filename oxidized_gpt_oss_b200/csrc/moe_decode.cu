@@ -68,12 +68,11 @@ constexpr bool kBulk = OXG_DEC_BULK != 0;
 constexpr int kW1 = OXG_DEC_W1, kS1 = OXG_DEC_S1;
 constexpr int kW2 = OXG_DEC_W2, kS2 = OXG_DEC_S2;
 constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
-// At most kDeepTokens tokens (4-8 active experts) a warp streams about one
-// 16-row tile, so the ring depth decides the kernel's time: fewer warps with
-// deeper rings (mlp1: 10 x 16 stages for 1480 warps >= 4 experts x 360
-// tiles; mlp2: 8 x 20, a band being ~5 tiles) fit the same shared memory.
+// At most kDeepTokens tokens (4-8 active experts): mlp1 splits each tile's K
+// over 4 warps (28 warps x 5 stages, 7 tiles in flight per SM); mlp2, whose
+// CTA covers a band of ~5 tiles, uses fewer warps with deeper rings (8 x 20).
 constexpr int kDeepTokens = 2;
-constexpr int kW1d = 10, kS1d = 16;
+constexpr int kW1d = 28, kS1d = 5, kK1d = 4;  // mlp1: 7 groups of 4 warps splitting K
 constexpr int kW3d = 8, kS3d = 20;
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
@@ -143,10 +142,17 @@ constexpr int kErrDecodeWait = 21;  // error word: a decode weight copy did not 
 // budget; the copies still in flight have then been waited for (bounded).
 template <int STAGES, bool BULK, class ItemPtr, class GroupFn, class DoneFn>
 __device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, int *err, ItemPtr item_ptr,
-                                             GroupFn group_fn, DoneFn done_fn) {
+                                             GroupFn group_fn, DoneFn done_fn, int g_begin = 0,
+                                             int g_count = -1) {
   if (n_items <= 0) return true;
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int nb = K / 32, full = nb / 4, tail = nb % 4, ngroups = full + (tail ? 1 : 0);
+  // groups [g_begin, g_begin + ng) of every item (all of them by default)
+  const int ng = g_count < 0 ? ngroups - g_begin : g_count;
+  if (ng <= 0) {  // an empty share of K: nothing to stream, partial sums stay zero
+    for (int i = 0; i < n_items; ++i) done_fn(i);
+    return true;
+  }
   const uint32_t tail_bytes = 256u * tail + 64u;
   // Issue side: runs STAGES groups ahead of the consumer.
   int i_item = 0, i_grp = 0, i_slot = 0, pending = 0;
@@ -154,15 +160,15 @@ __device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, i
   auto issue_next = [&]() {
     if (i_item < n_items) {
       uint8_t *st = wr.ring + i_slot * kStageBytes;
-      const uint8_t *ch = ip + (size_t)i_grp * 1088;
+      const uint8_t *ch = ip + (size_t)(g_begin + i_grp) * 1088;
       if (BULK) {
         if (lane == 0) {
-          const uint32_t bytes = i_grp < full ? 1088u : tail_bytes;
+          const uint32_t bytes = g_begin + i_grp < full ? 1088u : tail_bytes;
           sm100::mbar_arrive_expect_tx(&wr.bars[i_slot], bytes);
           sm100::bulk_copy(st, ch, bytes, &wr.bars[i_slot]);
         }
         ++pending;
-      } else if (i_grp < full) {
+      } else if (g_begin + i_grp < full) {
         cp_async_16(st + lane * 16, ch + lane * 16);
         cp_async_16(st + 512 + lane * 16, ch + 512 + lane * 16);
         if (lane < 4) cp_async_16(st + 1024 + lane * 16, ch + 1024 + lane * 16);
@@ -173,7 +179,7 @@ __device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, i
         }
         if (lane < 4) cp_async_16(st + 1024 + lane * 16, ch + 256 * tail + lane * 16);
       }
-      if (++i_grp == ngroups) {
+      if (++i_grp == ng) {
         i_grp = 0;
         if (++i_item < n_items) ip = item_ptr(i_item);
       }
@@ -199,7 +205,7 @@ __device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, i
       --pending;
       // a bulk copy lands the chunk as stored: narrow groups keep their
       // packed layout (4 * tail bytes per lane and row half)
-      if (c_grp < full) {
+      if (g_begin + c_grp < full) {
         const uint4 va = *reinterpret_cast<const uint4 *>(st + lane * 16);
         const uint4 vb = *reinterpret_cast<const uint4 *>(st + 512 + lane * 16);
         wa[0] = va.x; wa[1] = va.y; wa[2] = va.z; wa[3] = va.w;
@@ -229,11 +235,11 @@ __device__ __forceinline__ bool stream_items(int n_items, int K, WarpRing &wr, i
       sxb = *reinterpret_cast<const uint32_t *>(st + 1056 + g * 4);
     }
     issue_next();
-    if (c_grp < full)
-      group_fn(c_grp * 4, 4, wa, wb, sxa, sxb);
+    if (g_begin + c_grp < full)
+      group_fn((g_begin + c_grp) * 4, 4, wa, wb, sxa, sxb);
     else
-      group_fn(c_grp * 4, tail, wa, wb, sxa, sxb);
-    if (++c_grp == ngroups) {
+      group_fn((g_begin + c_grp) * 4, tail, wa, wb, sxa, sxb);
+    if (++c_grp == ng) {
       done_fn(c_item);
       c_grp = 0;
       ++c_item;
@@ -345,10 +351,19 @@ __device__ __forceinline__ void stage_x(const DecodeArgs &a, uint8_t *smem, int 
 // ---------------------------------------------------------------------------
 // mlp1 over all tokens (T <= 8): persistent grid over (active expert, tile).
 // ---------------------------------------------------------------------------
-template <int WARPS, int STAGES>
+// KS > 1: KS consecutive warps share each tile, warp kq of a group streams
+// the kq-th share of K's 128-wide groups; at the end of a tile the partial
+// sums meet in shared memory and the group's first warp adds them in warp
+// order (the same order every run) and runs the epilogue. At one or two
+// tokens there are only ~4 experts x 360 tiles, so this keeps every warp of
+// the SM busy instead of one warp per tile.
+template <int WARPS, int STAGES, int KS = 1>
 __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const DecodeArgs a) {
+  static_assert(WARPS % KS == 0, "warps come in groups of KS");
   constexpr int kThreads = WARPS * 32;
+  constexpr int kGroups = WARPS / KS;
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ __align__(16) float red_s[KS > 1 ? WARPS * 32 * 4 : 4];
   __shared__ float tok_scale[8];
   __shared__ int act_s[kMaxAllTokActive];
   __shared__ int act_of[256];
@@ -378,9 +393,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const Decode
   __syncthreads();
   if (a.pdl) pdl_launch();
 
-  const int W = gridDim.x * WARPS, wg = blockIdx.x * WARPS + warp;
+  const int gw = warp / KS, kq = warp % KS;
+  const int W = gridDim.x * kGroups, wg = blockIdx.x * kGroups + gw;
   const int total = n_act * n_tiles;
   const int n_items = wg < total ? (total - wg + W - 1) / W : 0;
+  const int n_grp = nb / 4 + (nb % 4 ? 1 : 0);
+  const int g_begin = kq * n_grp / KS, g_end = (kq + 1) * n_grp / KS;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   auto item_ptr = [&](int i) {
     const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
@@ -389,6 +407,32 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const Decode
   auto group_fn = [&](int blk0, int nblk, const uint32_t(&wa)[4], const uint32_t(&wb)[4], uint32_t sxa,
                       uint32_t sxb) { mma_group<8>(smem, nb, 0, blk0, nblk, wa, wb, sxa, sxb, g, q, acc); };
   auto done_fn = [&](int i) {
+    if constexpr (KS > 1) {
+      float4 *slot = reinterpret_cast<float4 *>(red_s) + (gw * KS + kq) * 32 + lane;
+      *slot = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + gw), "r"(KS * 32) : "memory");
+      if (kq == 0) {
+        const float4 *g0 = reinterpret_cast<const float4 *>(red_s) + gw * KS * 32 + lane;
+        float4 t = g0[0];
+#pragma unroll
+        for (int r = 1; r < KS; ++r) {
+          const float4 v = g0[r * 32];
+          t.x += v.x;
+          t.y += v.y;
+          t.z += v.z;
+          t.w += v.w;
+        }
+        acc[0] = t.x;
+        acc[1] = t.y;
+        acc[2] = t.z;
+        acc[3] = t.w;
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + gw), "r"(KS * 32) : "memory");
+      if (kq != 0) {
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        return;
+      }
+    }
     const int w = wg + i * W, ai = w / n_tiles, tile = w - ai * n_tiles;
     const int e = act_s[ai];
     const int pr = tile * 8 + g;  // intermediate unit (gate row 2pr, up row 2pr + 1)
@@ -408,7 +452,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const Decode
   };
   WarpRing wr = make_ring<STAGES>(smem + nb * 2 * 32 * 8 + warp * (STAGES * kStageBytes),
                                   ring_bars + warp * STAGES);
-  stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn);
+  stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn, g_begin, g_end - g_begin);
 }
 
 // ---------------------------------------------------------------------------
@@ -782,7 +826,7 @@ cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
   if (T <= 8 && T * w.k <= kMaxAllTokActive && w.E <= 256) {
     if (T <= kDeepTokens) {
       const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1d * kS1d * kStageBytes;
-      return launch_ex(mlp1_alltok_kernel<kW1d, kS1d>, dim3(s.n_sms), kW1d * 32, smem, a.pdl, stream, a);
+      return launch_ex(mlp1_alltok_kernel<kW1d, kS1d, kK1d>, dim3(s.n_sms), kW1d * 32, smem, a.pdl, stream, a);
     }
     const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1 * kS1 * kStageBytes;
     return launch_ex(mlp1_alltok_kernel<kW1, kS1>, dim3(s.n_sms), kW1 * 32, smem, a.pdl, stream, a);
