@@ -775,7 +775,7 @@ def run_model(args, ws, rank, local):
            "dtype": "bf16 activations and attention weights, mxfp4 experts, f32 accumulate",
            "data": "synthetic", "config": model_config(args, d, P),
            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "peak_kind": hbm_kind,
-                        "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                        "unit": "GB/s", "frac": achieved / hbm, "traffic": ncu_traffic(dom, "T1"),
                         "algorithmic_bytes_per_launch": per_kernel_bytes[dom] / max(dom_n / n_prof, 1),
                         "avg_launch_us": dom_ms / max(dom_n, 1) * 1e3},
            "step": {"hbm_gbs": step_bytes / (ms / args.steps * 1e-3) / 1e9,

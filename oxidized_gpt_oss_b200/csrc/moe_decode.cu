@@ -68,12 +68,12 @@ constexpr bool kBulk = OXG_DEC_BULK != 0;
 constexpr int kW1 = OXG_DEC_W1, kS1 = OXG_DEC_S1;
 constexpr int kW2 = OXG_DEC_W2, kS2 = OXG_DEC_S2;
 constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
-// At most kDeepTokens tokens (4-8 active experts): mlp1 splits each tile's K
-// over 4 warps (28 warps x 5 stages, 7 tiles in flight per SM); mlp2, whose
-// CTA covers a band of ~5 tiles, uses fewer warps with deeper rings (8 x 20).
+// At most kDeepTokens tokens (4-8 active experts): each tile's K is split
+// over 4 warps — mlp1 28 warps x 5 stages (7 tiles in flight per SM), mlp2
+// 20 x 7 (5 tiles, a band being ~5 tiles of one expert).
 constexpr int kDeepTokens = 2;
 constexpr int kW1d = 28, kS1d = 5, kK1d = 4;  // mlp1: 7 groups of 4 warps splitting K
-constexpr int kW3d = 8, kS3d = 20;
+constexpr int kW3d = 20, kS3d = 7, kK3d = 4;  // mlp2: 5 groups of 4 warps splitting K
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 
 struct DecodeArgs {
@@ -466,10 +466,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const Decode
 // The activation stage occupies the first stage_bytes of smem (the kernel's
 // layout: NT n-tiles of 8-byte fragments for mlp1 and packed mlp2, 16-byte
 // ones otherwise); the warps' rings follow it.
-template <int MODE, int NT, bool PACKED, int WARPS, int STAGES>
+// KS > 1: groups of KS warps share each tile, warp kq streaming the kq-th
+// share of K; the group's first warp adds the partial sums in warp order and
+// writes the tile (see mlp1_alltok_kernel).
+template <int MODE, int NT, bool PACKED, int WARPS, int STAGES, int KS = 1>
 __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, int stage_bytes, float *tok_scale,
                                             uint64_t *ring_bars, int e, int n_e, int pos0, int t_begin,
                                             int t_end) {
+  static_assert(WARPS % KS == 0, "warps come in groups of KS");
+  constexpr int kGroups = WARPS / KS;
   constexpr int kTokPerPass = PACKED ? 4 : NT * 8;
   constexpr int kFrag = (MODE == 1 || PACKED) ? 8 : 16;  // bytes per staged fragment
   constexpr int kNT = PACKED ? 1 : NT;
@@ -480,8 +485,12 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
   constexpr int kThreads = WARPS * 32;
   WarpRing wr = make_ring<STAGES>(smem + stage_bytes + warp * (STAGES * kStageBytes), ring_bars + warp * STAGES);
   bool ok = true;
-  // tiles of this warp: t_begin + warp, t_begin + warp + WARPS, ...
-  const int n_items = t_begin + warp < t_end ? (t_end - t_begin - warp + WARPS - 1) / WARPS : 0;
+  // tiles of this warp's group: t_begin + gw, t_begin + gw + kGroups, ...
+  const int gw = warp / KS, kq = warp % KS;
+  const int n_items = t_begin + gw < t_end ? (t_end - t_begin - gw + kGroups - 1) / kGroups : 0;
+  const int n_grp = nb / 4 + (nb % 4 ? 1 : 0);
+  const int g_begin = kq * n_grp / KS, g_end = (kq + 1) * n_grp / KS;
+  __shared__ __align__(16) float red_s[KS > 1 ? WARPS * 32 * 4 * kNT : 4];
 
   for (int tok0 = 0; tok0 < n_e; tok0 += kTokPerPass) {
     // ---- stage this pass's activations in fragment order ----
@@ -532,7 +541,7 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
     float acc[kNT][4];
 #pragma unroll
     for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    auto tile_of = [&](int i) { return t_begin + warp + i * WARPS; };
+    auto tile_of = [&](int i) { return t_begin + gw + i * kGroups; };
     auto item_ptr = [&](int i) { return a.codes + ((size_t)e * (a.rows / 16) + tile_of(i)) * a.item_bytes; };
     auto group_fn = [&](int blk0, int nblk, const uint32_t(&wa)[4], const uint32_t(&wb)[4], uint32_t sxa,
                         uint32_t sxb) {
@@ -541,6 +550,37 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
         mma_group<kFrag>(smem, nb, nt, blk0, nblk, wa, wb, sxa, sxb, g, q, acc[nt]);
     };
     auto done_fn = [&](int i) {
+      if constexpr (KS > 1) {
+        float4 *slot = reinterpret_cast<float4 *>(red_s) + ((gw * KS + kq) * kNT) * 32 + lane;
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt) slot[nt * 32] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + gw), "r"(KS * 32) : "memory");
+        if (kq == 0) {
+#pragma unroll
+          for (int nt = 0; nt < kNT; ++nt) {
+            const float4 *g0 = reinterpret_cast<const float4 *>(red_s) + (gw * KS * kNT + nt) * 32 + lane;
+            float4 t = g0[0];
+#pragma unroll
+            for (int r = 1; r < KS; ++r) {
+              const float4 v = g0[r * kNT * 32];
+              t.x += v.x;
+              t.y += v.y;
+              t.z += v.z;
+              t.w += v.w;
+            }
+            acc[nt][0] = t.x;
+            acc[nt][1] = t.y;
+            acc[nt][2] = t.z;
+            acc[nt][3] = t.w;
+          }
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + gw), "r"(KS * 32) : "memory");
+        if (kq != 0) {
+#pragma unroll
+          for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+          return;
+        }
+      }
       const int tile = tile_of(i);
       const int row_a = MODE == 1 ? 2 * (tile * 8 + g) : tile * 16 + g;
       const int row_b = MODE == 1 ? row_a + 1 : row_a + 8;
@@ -575,7 +615,8 @@ __device__ __forceinline__ void expert_band(const DecodeArgs &a, uint8_t *smem, 
 #pragma unroll
       for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     };
-    if (ok) ok = stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn);
+    if (ok) ok = stream_items<STAGES, kBulk>(n_items, K, wr, a.err, item_ptr, group_fn, done_fn, g_begin,
+                                             g_end - g_begin);
     __syncthreads();
   }
 }
@@ -590,7 +631,7 @@ __host__ __device__ constexpr int decode_stage_bytes(int mode, int nt, bool pack
 // PACKED_ONLY (mlp2): h is always staged as f16 hi/lo column pairs, four
 // tokens per pass, so the stage needs half the shared memory and the ring
 // gets the rest.
-template <int MODE, int NT, int WARPS, int STAGES, bool PACKED_ONLY>
+template <int MODE, int NT, int WARPS, int STAGES, bool PACKED_ONLY, int KS = 1>
 __global__ void __launch_bounds__(WARPS * 32, 1) moe_decode_kernel(const DecodeArgs a) {
   constexpr int kThreads = WARPS * 32;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -623,7 +664,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) moe_decode_kernel(const DecodeA
   // shared memory: the activation stage, then the rings (launch size
   // stage_bytes + WARPS * STAGES * kStageBytes)
   const int stage_bytes = decode_stage_bytes(MODE, NT, PACKED_ONLY, a.K);
-  if (MODE == 2 && (PACKED_ONLY || n_e <= 4))
+  if constexpr (MODE == 2 && PACKED_ONLY)
+    expert_band<MODE, NT, true, WARPS, STAGES, KS>(a, smem, stage_bytes, tok_scale, ring_bars, e, n_e, pos0,
+                                                   t_begin, t_end);
+  else if (MODE == 2 && n_e <= 4)
     expert_band<MODE, NT, true, WARPS, STAGES>(a, smem, stage_bytes, tok_scale, ring_bars, e, n_e, pos0, t_begin,
                                                t_end);
   else
@@ -857,8 +901,8 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
     a.dyn_bands = 1;
     if (T <= kDeepTokens) {
       const size_t smem = (size_t)decode_stage_bytes(2, 1, true, a.K) + (size_t)kW3d * kS3d * kStageBytes;
-      return launch_ex(moe_decode_kernel<2, 1, kW3d, kS3d, true>, dim3(s.n_sms), kW3d * 32, smem, a.pdl, stream,
-                       a);
+      return launch_ex(moe_decode_kernel<2, 1, kW3d, kS3d, true, kK3d>, dim3(s.n_sms), kW3d * 32, smem, a.pdl,
+                       stream, a);
     }
     const size_t smem = (size_t)decode_stage_bytes(2, 1, true, a.K) + (size_t)kW3 * kS3 * kStageBytes;
     return launch_ex(moe_decode_kernel<2, 1, kW3, kS3, true>, dim3(s.n_sms), kW3 * 32, smem, a.pdl, stream, a);
