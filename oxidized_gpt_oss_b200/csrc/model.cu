@@ -21,6 +21,8 @@
 
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "model.h"
 
@@ -70,6 +72,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // ---------------------------------------------------------------------------
 constexpr int kNormThreads = 512;
 constexpr int kMaxSplits = 16;  // partial arrays a consumer sums (linear_splits caps at this)
+constexpr int kNormClusterRows = 8;  // up to this many rows the norm runs as 8-CTA clusters
 
 // 4 consecutive floats of row t: the residual (or embedding) plus the split
 // partials and the bias; every load of an element is issued before the sums.
@@ -161,6 +164,76 @@ __global__ void __launch_bounds__(kNormThreads)
     const uint32_t b3 = f32_to_bf16_bits(v.w * inv * bf16_to_f32(gm.y >> 16));
     o[i4] = make_uint2(b0 | (b1 << 16), b2 | (b3 << 16));
   }
+}
+
+// The same for a few rows (decode): a cluster of kNormCl CTAs per row, each
+// holding 1/kNormCl of the row, so every element's loads (residual, split
+// partials, bias) are in flight at once across 8 SMs; the CTAs' partial sums
+// of squares meet through distributed shared memory, added in rank order.
+constexpr int kNormCl = 8;
+constexpr int kNormClThreads = 128;
+
+__global__ void __cluster_dims__(kNormCl, 1, 1) __launch_bounds__(kNormClThreads)
+    residual_norm_cluster_kernel(float *__restrict__ res, int H, const int32_t *__restrict__ tokens,
+                                 const uint16_t *__restrict__ embed, int V, const float *__restrict__ add, int S,
+                                 size_t add_stride, const uint16_t *__restrict__ add_bias,
+                                 const uint16_t *__restrict__ gamma, float eps, uint16_t *__restrict__ out,
+                                 int *__restrict__ err) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  extern __shared__ float4 vc4[];
+  __shared__ float red[kNormClThreads / 32];
+  __shared__ float part_ss;
+  const int rank = (int)cl.block_rank();
+  const int t = blockIdx.y;
+  float *r = res + (size_t)t * H;
+  const uint16_t *erow = nullptr;
+  if (tokens) {
+    int tok = tokens[t];
+    if (tok < 0 || tok >= V) {
+      if (threadIdx.x == 0 && rank == 0) atomicExch(err, 60);
+      tok = 0;
+    }
+    erow = embed + (size_t)tok * H;
+  }
+  const bool write_res = erow || add;
+  const int H4 = H >> 2, chunk = (H4 + kNormCl - 1) / kNormCl;
+  const int i0 = rank * chunk, i1 = min(H4, i0 + chunk);
+  float ss = 0.f;
+  for (int i4 = i0 + threadIdx.x; i4 < i1; i4 += kNormClThreads) {
+    const float4 v = norm_value4(r, erow, add, S, add_stride, (size_t)t * H, add_bias, i4);
+    if (write_res) reinterpret_cast<float4 *>(r)[i4] = v;
+    vc4[i4 - i0] = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float p = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormClThreads / 32; ++w) p += red[w];
+    part_ss = p;
+  }
+  cl.sync();
+  float tot = 0.f;
+#pragma unroll
+  for (int q = 0; q < kNormCl; ++q) tot += *cl.map_shared_rank(&part_ss, q);
+  const float inv = 1.0f / sqrtf(tot / (float)H + eps);
+  uint2 *o = reinterpret_cast<uint2 *>(out + (size_t)t * H);
+  for (int i4 = i0 + threadIdx.x; i4 < i1; i4 += kNormClThreads) {
+    const float4 v = vc4[i4 - i0];
+    const uint2 gm = *reinterpret_cast<const uint2 *>(gamma + 4 * i4);
+    const uint32_t b0 = f32_to_bf16_bits(v.x * inv * bf16_to_f32(gm.x & 0xFFFFu));
+    const uint32_t b1 = f32_to_bf16_bits(v.y * inv * bf16_to_f32(gm.x >> 16));
+    const uint32_t b2 = f32_to_bf16_bits(v.z * inv * bf16_to_f32(gm.y & 0xFFFFu));
+    const uint32_t b3 = f32_to_bf16_bits(v.w * inv * bf16_to_f32(gm.y >> 16));
+    o[i4] = make_uint2(b0 | (b1 << 16), b2 | (b3 << 16));
+  }
+  cl.sync();  // no CTA leaves while another may still read its part_ss
 }
 
 // ---------------------------------------------------------------------------
@@ -771,6 +844,12 @@ __global__ void set_state_kernel(int32_t *__restrict__ state, int pos, const int
 cudaError_t launch_residual_norm(const NormArgs &a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.S > kMaxSplits || a.H % 4) return cudaErrorInvalidValue;
+  if (a.rows <= kNormClusterRows) {
+    const int chunk = (a.H / 4 + kNormCl - 1) / kNormCl;
+    residual_norm_cluster_kernel<<<dim3(kNormCl, a.rows), kNormClThreads, (size_t)chunk * sizeof(float4), stream>>>(
+        a.res, a.H, a.tokens, a.embed, a.V, a.add, a.S, a.add_stride, a.add_bias, a.gamma, a.eps, a.out, a.err);
+    return cudaGetLastError();
+  }
   residual_norm_kernel<<<a.rows, kNormThreads, (size_t)a.H * sizeof(float), stream>>>(
       a.res, a.H, a.tokens, a.embed, a.V, a.add, a.S, a.add_stride, a.add_bias, a.gamma, a.eps, a.out,
       a.err);
