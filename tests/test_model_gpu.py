@@ -203,3 +203,21 @@ def test_graph_decode_matches_eager_steps(small_model):
     assert [eager[0]] + a + b == eager[:1] + eager[1:24]
     assert g.position() == N_PROMPT + 23
     g.release()
+
+
+def test_checkpoint_loader_uploads_the_same_model(tmp_path):
+    """A checkpoint in the reference's naming (scales stored as bf16 bits, as
+    src/loader.rs:62 reads them), loaded packed, gives the same logits bit for
+    bit as the weights uploaded directly."""
+    from oxidized_gpt_oss_b200 import loader
+    m = synth.model_weights(seed=4, n_layers=2, vocab=4096, n_experts=4)
+    loader.save_model_weights(str(tmp_path), m, scales_as_bf16=True)
+    m2 = loader.load_model_weights(str(tmp_path), m["dims"])
+    prompt = np.random.default_rng(5).integers(0, 4096, 40)
+    g = _gpu_model(m)
+    a = g.forward(prompt, n_logits=4).cpu().numpy()
+    g.release()
+    g2 = _gpu_model(m2)
+    b = g2.forward(prompt, n_logits=4).cpu().numpy()
+    g2.release()
+    assert np.array_equal(a, b)
