@@ -283,6 +283,8 @@ typedef struct {
   int max_tokens;      /* largest n_tokens of one oxg_model_forward (prompts are chunked) */
   float rope_theta;    /* 150000 (src/config.rs:122) */
   float rms_eps;       /* 1e-5 (src/model.rs:433) */
+  int max_batch;       /* sequences with a KV cache of their own (0 or 1: one), at most min(128, max_tokens);
+                          the cache holds max_batch * max_seq positions per layer and kv head */
 } oxg_model_dims;
 
 /* One layer's attention weights (host or device pointers, bf16 unless noted;
@@ -338,6 +340,21 @@ OXG_API int oxg_model_generate(oxg_ctx *ctx, const int32_t *prompt_host, int n_p
  * idx_dev + layer * max_tokens * k. NULL switches it off. Graph-replayed
  * decode steps do not record. */
 OXG_API int oxg_model_route_tap(oxg_ctx *ctx, int32_t *idx_dev, int max_tokens);
+/* Several sequences at once (the reference runs one sequence per GPTModel;
+ * this is GPTModel::forward, src/model.rs:713-741, applied to max_batch
+ * independent KV caches). Sequence 0 is the one oxg_model_forward, _decode
+ * and _generate use; oxg_model_reset empties every sequence.
+ * oxg_model_prefill_seq appends n_tokens tokens (device) to sequence seq's
+ * cache and writes its greedy next token to next_dev [1] (may be NULL).
+ * oxg_model_step_batch appends one token to each of sequences 0 .. n_seqs-1
+ * (tokens_dev [n_seqs]; n_seqs <= max_batch) as one batch of n_seqs tokens
+ * through every layer — each attends to its own cache only — and writes the
+ * greedy next tokens to next_dev [n_seqs] and, if not NULL, the logits
+ * [n_seqs, V] f32 to logits_dev. Both asynchronous on the context's stream. */
+OXG_API int oxg_model_prefill_seq(oxg_ctx *ctx, int seq, const int32_t *tokens_dev, int n_tokens,
+                                  int32_t *next_dev);
+OXG_API int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens_dev, int32_t *next_dev,
+                                 float *logits_dev);
 OXG_API int oxg_model_release(oxg_ctx *ctx);
 
 /* ---- measurement (no reference counterpart: the reference's only timing is

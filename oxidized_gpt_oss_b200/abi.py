@@ -54,7 +54,7 @@ class ModelDims(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("n_heads", ctypes.c_int),
                 ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int),
                 ("sliding_window", ctypes.c_int), ("max_seq", ctypes.c_int), ("max_tokens", ctypes.c_int),
-                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_batch", ctypes.c_int)]
 
 
 class AttnWeights(ctypes.Structure):
@@ -106,6 +106,8 @@ SIGNATURES = {
     "oxg_model_generate": (_I, [_CTX, _P, _I, _I, _P]),
     "oxg_model_decode": (_I, [_CTX, _I, _P]),
     "oxg_model_route_tap": (_I, [_CTX, _P, _I]),
+    "oxg_model_prefill_seq": (_I, [_CTX, _I, _P, _I, _P]),
+    "oxg_model_step_batch": (_I, [_CTX, _I, _P, _P, _P]),
     "oxg_model_release": (_I, [_CTX]),
     "oxg_profile_enable": (_I, [_CTX, _I]),
     "oxg_profile_read": (_I, [_CTX, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),

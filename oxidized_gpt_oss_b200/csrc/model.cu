@@ -412,7 +412,9 @@ __global__ void __launch_bounds__(kLinThreads)
 
 // ---------------------------------------------------------------------------
 // q/k/v epilogue: sum of the split partials + bias, RoPE on q and k, bf16
-// q rows and the K/V cache rows of positions pos0 .. pos0 + T - 1.
+// q rows and the K/V cache rows of positions pos0 .. pos0 + T - 1 (one
+// sequence), or, with tok_pos, token t at position tok_pos[t] and cache row
+// tok_row0[t] + tok_pos[t] (one token of each of T sequences).
 // One CTA per token.
 // ---------------------------------------------------------------------------
 constexpr int kQkvThreads = 256;
@@ -421,14 +423,15 @@ __global__ void __launch_bounds__(kQkvThreads)
     qkv_post_kernel(const float *__restrict__ part, int S, int T, int nh, int nkv,
                     const uint16_t *__restrict__ bias, const float *__restrict__ rope_cos,
                     const float *__restrict__ rope_sin, int pos0, const int32_t *__restrict__ pos_dev,
-                    int max_seq, uint16_t *__restrict__ q_out, uint16_t *__restrict__ kc,
-                    uint16_t *__restrict__ vc) {
+                    const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_row0, int max_seq,
+                    uint16_t *__restrict__ q_out, uint16_t *__restrict__ kc, uint16_t *__restrict__ vc) {
   const int t = blockIdx.x;
   const int Nq = nh * 64, Nkv = nkv * 64, N = Nq + 2 * Nkv;
   const int n_pairs = (nh + nkv) * 32;
   const int it = blockIdx.y * kQkvThreads + threadIdx.x;  // one RoPE pair or one v element
   if (it >= n_pairs + Nkv) return;
-  const int pos = (pos_dev ? *pos_dev : pos0) + t;
+  const int pos = tok_pos ? tok_pos[t] : (pos_dev ? *pos_dev : pos0) + t;
+  const int row = tok_pos ? tok_row0[t] + pos : pos;  // cache row within a kv head's run
   const float *pt = part + (size_t)t * N;
   const size_t ps = (size_t)T * N;
   if (it < n_pairs) {
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(kQkvThreads)
     const float o1 = x1 * c - x2 * sn;
     const float o2 = x2 * c + x1 * sn;
     uint16_t *dst = head < nh ? q_out + (size_t)t * Nq + head * 64
-                              : kc + ((size_t)(head - nh) * max_seq + pos) * 64;
+                              : kc + ((size_t)(head - nh) * max_seq + row) * 64;
     dst[d] = (uint16_t)f32_to_bf16_bits(o1);
     dst[d + 32] = (uint16_t)f32_to_bf16_bits(o2);
   } else {
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kQkvThreads)
     for (int s = 0; s < kMaxSplits; ++s)
       if (s < S) x += a[s];
     if (bias) x += bf16_to_f32(bias[n]);
-    vc[((size_t)(e >> 6) * max_seq + pos) * 64 + (e & 63)] = (uint16_t)f32_to_bf16_bits(x);
+    vc[((size_t)(e >> 6) * max_seq + row) * 64 + (e & 63)] = (uint16_t)f32_to_bf16_bits(x);
   }
 }
 
@@ -479,7 +482,9 @@ __global__ void __launch_bounds__(kQkvThreads)
 // Decode attention (one query token at position key_hi): CTA (kv head, split)
 // handles up to 64 keys of [key_lo, key_hi] for the G query heads sharing the
 // kv head and writes (max, sum, unnormalised output) per head; the combine
-// kernel merges the splits with the sink.
+// kernel merges the splits with the sink. With tok_pos, grid z runs over T
+// tokens of T sequences: token t's keys are cache rows tok_row0[t] + (lo ..
+// tok_pos[t]), its q row t * Nq and its partials part_tok floats apart.
 // ---------------------------------------------------------------------------
 constexpr int kDecKeys = 64;
 constexpr int kMaxGroup = 16;
@@ -490,7 +495,8 @@ __global__ void __launch_bounds__(kDecThreads)
     attn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ kc,
                        const uint16_t *__restrict__ vc, int max_seq, int G, int key_lo, int key_hi,
                        float scale, int n_split, const int32_t *__restrict__ pos_dev, int window,
-                       float *__restrict__ part) {
+                       float *__restrict__ part, const int32_t *__restrict__ tok_pos,
+                       const int32_t *__restrict__ tok_row0, int Nq, size_t part_tok) {
   __shared__ float qs[kMaxGroup][64];
   __shared__ __align__(16) uint16_t Kt[64][kKtPad];     // K transposed: [dim][key]
   __shared__ __align__(16) uint16_t Vs[kDecKeys][64];   // V as stored: [key][dim]
@@ -502,6 +508,15 @@ __global__ void __launch_bounds__(kDecThreads)
     key_lo = window > 0 ? max(0, key_hi - window + 1) : 0;
     n_split = (key_hi - key_lo + kDecKeys) / kDecKeys;
     if (sp >= n_split) return;
+  } else if (tok_pos) {  // one token per sequence: the grid covers the longest sequence
+    const int t = blockIdx.z, p = tok_pos[t], r0 = tok_row0[t];
+    const int lo = window > 0 ? max(0, p - window + 1) : 0;
+    n_split = (p - lo + kDecKeys) / kDecKeys;
+    if (sp >= n_split) return;
+    key_lo = r0 + lo;
+    key_hi = r0 + p;
+    q += (size_t)t * Nq;
+    part += (size_t)t * part_tok;
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int k0 = key_lo + sp * kDecKeys;
@@ -584,14 +599,21 @@ __global__ void __launch_bounds__(kDecThreads)
   }
 }
 
-// One CTA of 64 threads per query head: merges the decode splits and the sink.
+// One CTA of 64 threads per (query head, token): merges the decode splits and
+// the sink.
 __global__ void __launch_bounds__(64)
     attn_combine_kernel(const float *__restrict__ part, int G, int n_split, const int32_t *__restrict__ pos_dev,
-                        int window, const uint16_t *__restrict__ sinks, uint16_t *__restrict__ out) {
+                        int window, const uint16_t *__restrict__ sinks, uint16_t *__restrict__ out,
+                        const int32_t *__restrict__ tok_pos, int Nq, size_t part_tok) {
   const int h = blockIdx.x, kvh = h / G, hl = h % G, d = threadIdx.x;
-  if (pos_dev) {
-    const int hi = *pos_dev, lo = window > 0 ? max(0, hi - window + 1) : 0;
+  if (pos_dev || tok_pos) {
+    const int t = blockIdx.y;
+    const int hi = tok_pos ? tok_pos[t] : *pos_dev, lo = window > 0 ? max(0, hi - window + 1) : 0;
     n_split = (hi - lo + kDecKeys) / kDecKeys;
+    if (tok_pos) {
+      part += (size_t)t * part_tok;
+      out += (size_t)t * Nq;
+    }
   }
   const float sink = sinks ? bf16_to_f32(sinks[h]) : -INFINITY;
   const float *p0 = part + ((size_t)kvh * n_split * G + hl) * 66;
@@ -899,12 +921,13 @@ cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, 
 
 cudaError_t launch_qkv_post(const float *part, int S, int T, int nh, int nkv, const uint16_t *bias,
                             const float *rope_cos, const float *rope_sin, int pos0, const int32_t *pos_dev,
-                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream) {
+                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream,
+                            const int32_t *tok_pos, const int32_t *tok_row0) {
   if (T <= 0) return cudaSuccess;
   if (S > kMaxSplits) return cudaErrorInvalidValue;
   const int items = (nh + nkv) * 32 + nkv * 64;
   qkv_post_kernel<<<dim3(T, (items + kQkvThreads - 1) / kQkvThreads), kQkvThreads, 0, stream>>>(
-      part, S, T, nh, nkv, bias, rope_cos, rope_sin, pos0, pos_dev, max_seq, q_out, kc, vc);
+      part, S, T, nh, nkv, bias, rope_cos, rope_sin, pos0, pos_dev, tok_pos, tok_row0, max_seq, q_out, kc, vc);
   return cudaGetLastError();
 }
 
@@ -913,17 +936,35 @@ int attn_decode_splits(int n_keys) { return (n_keys + kDecKeys - 1) / kDecKeys; 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
   const int G = a.nh / a.nkv;
+  const int Nq = a.nh * 64;
+  const int rows = a.split_rows > 0 ? a.split_rows : a.max_seq;  // positions of one sequence
+  if (a.tok_pos) {  // one query of each of T sequences
+    const size_t part_tok = attn_part_floats(a.nkv, G, rows);
+    const int window_splits = attn_decode_splits(a.window > 0 && a.window < rows ? a.window : rows);
+    const int grid_split = a.window > 0 && window_splits < a.max_splits ? window_splits : a.max_splits;
+    if (grid_split <= 0 || grid_split > attn_decode_splits(rows)) return cudaErrorInvalidValue;
+    attn_decode_kernel<<<dim3(a.nkv, grid_split, a.T), kDecThreads, 0, stream>>>(
+        a.q, a.kc, a.vc, a.max_seq, G, 0, 0, a.scale, grid_split, nullptr, a.window, a.part, a.tok_pos,
+        a.tok_row0, Nq, part_tok);
+    cudaError_t st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, grid_split, nullptr, a.window, a.sinks,
+                                                           a.out, a.tok_pos, Nq, part_tok);
+    return cudaGetLastError();
+  }
   if (a.T == 1) {
     const int pos = a.pos0;
     const int lo = a.window > 0 ? (pos - a.window + 1 > 0 ? pos - a.window + 1 : 0) : 0;
     // with the position on the device the grid covers the largest split count
-    const int grid_split = a.pos_dev ? attn_decode_splits(a.window > 0 && a.window < a.max_seq ? a.window : a.max_seq)
+    const int grid_split = a.pos_dev ? attn_decode_splits(a.window > 0 && a.window < rows ? a.window : rows)
                                      : attn_decode_splits(pos - lo + 1);
-    attn_decode_kernel<<<dim3(a.nkv, grid_split), kDecThreads, 0, stream>>>(a.q, a.kc, a.vc, a.max_seq, G, lo, pos, a.scale,
-                                                                     grid_split, a.pos_dev, a.window, a.part);
+    attn_decode_kernel<<<dim3(a.nkv, grid_split), kDecThreads, 0, stream>>>(
+        a.q, a.kc, a.vc, a.max_seq, G, lo, pos, a.scale, grid_split, a.pos_dev, a.window, a.part, nullptr, nullptr,
+        Nq, 0);
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    attn_combine_kernel<<<a.nh, 64, 0, stream>>>(a.part, G, grid_split, a.pos_dev, a.window, a.sinks, a.out);
+    attn_combine_kernel<<<a.nh, 64, 0, stream>>>(a.part, G, grid_split, a.pos_dev, a.window, a.sinks, a.out,
+                                                 nullptr, Nq, 0);
     return cudaGetLastError();
   }
   attn_prefill_kernel<<<dim3((a.T + kAttQ - 1) / kAttQ, a.nh), 128, 0, stream>>>(

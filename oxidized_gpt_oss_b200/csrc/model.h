@@ -47,21 +47,28 @@ struct ArgmaxEpilogue {
 cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, int N, int K, int splits,
                           float *out, cudaStream_t stream, const ArgmaxEpilogue *am = nullptr);
 
-// q/k/v epilogue: bias, RoPE (tables [max_seq, 32] of cos and sin), bf16 q
-// [T, nh * 64] and K/V cache rows [nkv, max_seq, 64] at positions pos0 + t.
-// pos_dev, when not null, replaces pos0 by the position held on the device.
+// q/k/v epilogue: bias, RoPE (tables [positions, 32] of cos and sin), bf16 q
+// [T, nh * 64] and K/V cache rows (a kv head's rows max_seq apart) at
+// positions pos0 + t. pos_dev, when not null, replaces pos0 by the position
+// held on the device. tok_pos / tok_row0 (device, [T]), when not null, make
+// token t one of its own sequence: position tok_pos[t], cache row
+// tok_row0[t] + tok_pos[t].
 cudaError_t launch_qkv_post(const float *part, int S, int T, int nh, int nkv, const uint16_t *bias,
                             const float *rope_cos, const float *rope_sin, int pos0, const int32_t *pos_dev,
-                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream);
+                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream,
+                            const int32_t *tok_pos = nullptr, const int32_t *tok_row0 = nullptr);
 
 struct AttnArgs {
   const uint16_t *q = nullptr;   // [T, nh * 64] bf16
-  const uint16_t *kc = nullptr, *vc = nullptr;  // [nkv, max_seq, 64] bf16
+  const uint16_t *kc = nullptr, *vc = nullptr;  // [nkv, max_seq, 64] bf16 (max_seq: rows per kv head)
   int T = 0, nh = 0, nkv = 0, max_seq = 0, pos0 = 0;
+  int split_rows = 0;            // positions of one sequence (0: max_seq); sizes the decode grid
+  const int32_t *tok_pos = nullptr, *tok_row0 = nullptr;  // [T] device: one query of each of T sequences
+  int max_splits = 0;            // with tok_pos: splits of the longest sequence's full-attention span
   int window = 0;                // > 0: keys p - window + 1 .. p
   float scale = 0.125f;
   const uint16_t *sinks = nullptr;  // [nh] bf16 or null
-  float *part = nullptr;         // decode split partials (attn_part_floats)
+  float *part = nullptr;         // decode split partials (attn_part_floats per query token)
   const int32_t *pos_dev = nullptr;  // T == 1: the query position read on the device (graph replays)
   uint16_t *out = nullptr;       // [T, nh * 64] bf16
 };

@@ -7,9 +7,10 @@
 //     (q rows, then k, then v, so one linear launch covers all three), their
 //     bias, o projection [H, nh 64] + bias, sinks [nh], MoE norm [H];
 //   * embeddings [V, H], LM head [V, H], final norm [H];
-//   * KV cache [layer][K|V][nkv][max_seq][64] bf16 (a kv head's keys are one
-//     contiguous run, which both attention kernels stream), RoPE cos/sin
-//     tables [max_seq][32] f32 (built on the host in double precision);
+//   * KV cache [layer][K|V][nkv][max_batch * max_seq][64] bf16: a kv head's
+//     keys of sequence s are the contiguous rows s * max_seq .. (both
+//     attention kernels stream one run), RoPE cos/sin tables [max_seq][32]
+//     f32 (built on the host in double precision);
 //   * activations for max_tokens tokens: residual f32, normed bf16, linear
 //     partials f32, q and attention output bf16, MoE output f32, logits.
 // Reference interfaces replaced: GPTModel::forward (src/model.rs:713-741),
@@ -53,7 +54,11 @@ struct ModelState {
   unsigned int *am_count = nullptr;       // its finished-CTA counter
   int *err = nullptr;
   int part_rows = 0, max_logits = 0, gen_cap = 0;
-  int pos = 0;
+  int pos = 0;                 // sequence 0's position (the single-sequence API's)
+  int B = 1;                   // sequences with a KV cache of their own
+  size_t kv_stride = 0;        // cache rows per kv head: B * max_seq
+  std::vector<int> seq_pos;    // positions of sequences 1 .. B-1 (index 0 unused)
+  int32_t *tok_pos = nullptr, *tok_row0 = nullptr;  // batched step: [B] position, cache row base
   bool moe_reserved = false;
   bool state_ok = false;  // the device state holds the last forward's greedy token
   int32_t *route_tap = nullptr;  // oxg_model_route_tap: [n_layers][tap_tokens][k] expert ids
@@ -138,6 +143,9 @@ int check_model_dims(oxg_ctx *ctx, const oxg_model_dims *d) {
     return mfail(ctx, OXG_ERR_SHAPE, "max_seq must be in [1, 2^22], got %d", d->max_seq);
   if (d->max_tokens <= 0 || d->max_tokens > d->max_seq)
     return mfail(ctx, OXG_ERR_SHAPE, "max_tokens must be in [1, max_seq], got %d", d->max_tokens);
+  if (d->max_batch < 0 || d->max_batch > kMaxLogits || d->max_batch > d->max_tokens)
+    return mfail(ctx, OXG_ERR_SHAPE, "max_batch must be in [0, min(%d, max_tokens)], got %d", kMaxLogits,
+                 d->max_batch);
   if (!(d->rope_theta > 0.f)) return mfail(ctx, OXG_ERR_INVALID_ARG, "rope_theta must be positive");
   if (!(d->rms_eps >= 0.f)) return mfail(ctx, OXG_ERR_INVALID_ARG, "rms_eps must be >= 0");
   return OXG_OK;
@@ -198,13 +206,18 @@ int upload_attn(oxg_ctx *ctx, ModelState &M, int layer, const oxg_attn_weights *
   return OXG_OK;
 }
 
-// One forward of T tokens at positions pos .. pos + T - 1. With dstate (the
-// decode step a graph captures: T = 1, n_logits = 1) the token, position and
-// output slot come from the device state instead, and the argmax advances it;
-// otherwise a forward that computes logits leaves the state at its end
-// position and greedy token, ready for one-token steps.
+int &seq_pos_ref(ModelState &M, int seq) { return seq == 0 ? M.pos : M.seq_pos[seq]; }
+
+// One forward of T tokens of sequence seq at positions pos .. pos + T - 1.
+// With dstate (the decode step a graph captures: sequence 0, T = 1,
+// n_logits = 1) the token, position and output slot come from the device
+// state instead, and the argmax advances it; otherwise a forward of sequence
+// 0 that computes logits leaves the state at its end position and greedy
+// token, ready for one-token steps. With batch, token t is the next token of
+// sequence t (positions and cache rows in M.tok_pos / M.tok_row0, max_splits
+// the longest one's attention splits) and the caller advances the positions.
 int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits, float *logits_out,
-            int32_t *next_out, int32_t *dstate = nullptr) {
+            int32_t *next_out, int32_t *dstate = nullptr, int seq = 0, bool batch = false, int max_splits = 0) {
   const oxg_model_dims &d = M.d;
   const int H = d.hidden, L = d.n_layers;
   cudaStream_t s = ctx_stream(ctx);
@@ -223,7 +236,8 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     }
     M.moe_reserved = true;
   }
-  const int pos0 = M.pos;
+  const bool own_state = !batch && seq == 0;  // the decode state follows sequence 0
+  const int pos0 = batch ? 0 : seq_pos_ref(M, seq);
   // embedding + layer 0's attention norm
   {
     NormArgs a;
@@ -240,10 +254,12 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     MCUDA(ctx, ctx_launch(ctx, "embed_norm", [&] { return launch_residual_norm(a, s); }), "embed launch");
   }
   const float scale = 1.0f / std::sqrt((float)d.head_dim);
-  const size_t kv_layer = (size_t)2 * d.n_kv_heads * d.max_seq * 64;
+  const size_t kv_layer = (size_t)2 * d.n_kv_heads * M.kv_stride * 64;
+  const size_t seq_row0 = batch ? 0 : (size_t)seq * d.max_seq * 64;
+  const int32_t *tpos = batch ? M.tok_pos : nullptr, *trow = batch ? M.tok_row0 : nullptr;
   for (int l = 0; l < L; ++l) {
     const ModelState::Attn &A = M.layers[l];
-    uint16_t *kc = M.kv + (size_t)l * kv_layer;
+    uint16_t *kc = M.kv + (size_t)l * kv_layer + seq_row0;
     uint16_t *vc = kc + kv_layer / 2;
     const int s_qkv = linear_splits(M.Nqkv, H, T, n_sms, M.part_rows);
     MCUDA(ctx, ctx_launch(ctx, "linear_qkv", [&] {
@@ -252,7 +268,7 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
           "qkv launch");
     MCUDA(ctx, ctx_launch(ctx, "qkv_rope", [&] {
             return launch_qkv_post(M.part, s_qkv, T, d.n_heads, d.n_kv_heads, A.bqkv, M.rope_cos, M.rope_sin,
-                                   pos0, dstate, d.max_seq, M.qb, kc, vc, s);
+                                   pos0, dstate, (int)M.kv_stride, M.qb, kc, vc, s, tpos, trow);
           }),
           "qkv epilogue launch");
     AttnArgs at;
@@ -262,7 +278,11 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     at.T = T;
     at.nh = d.n_heads;
     at.nkv = d.n_kv_heads;
-    at.max_seq = d.max_seq;
+    at.max_seq = (int)M.kv_stride;
+    at.split_rows = d.max_seq;
+    at.tok_pos = tpos;
+    at.tok_row0 = trow;
+    at.max_splits = max_splits;
     at.pos0 = pos0;
     at.window = (l % 2 == 0) ? d.sliding_window : 0;
     at.scale = scale;
@@ -326,7 +346,7 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     am.next = dstate ? nullptr : (next_out ? next_out : M.tok);
     am.state = dstate ? dstate : M.dstate;
     am.out_seq = M.gen;
-    am.state_mode = dstate ? 1 : 2;
+    am.state_mode = dstate ? 1 : (own_state ? 2 : 0);
     am.set_pos = pos0 + T;
     MCUDA(ctx, ctx_launch(ctx, "lm_head", [&] {
             return launch_linear(M.xn, n_logits, H, M.unembed, d.vocab, H, 1, lg, s, &am);
@@ -351,13 +371,14 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
             return launch_argmax(lg, n_logits, d.vocab, nx, nullptr, nullptr, s);
           }),
           "argmax launch");
-    MCUDA(ctx, ctx_launch(ctx, "decode_state", [&] {
+    if (own_state) MCUDA(ctx, ctx_launch(ctx, "decode_state", [&] {
             return launch_set_state(M.dstate, pos0 + T, nx + n_logits - 1, s);
           }),
           "state launch");
   }
-  M.state_ok = n_logits > 0;
-  M.pos = pos0 + T;
+  if (batch) return OXG_OK;  // the caller advances every sequence's position
+  if (own_state) M.state_ok = n_logits > 0;
+  seq_pos_ref(M, seq) = pos0 + T;
   return OXG_OK;
 }
 
@@ -487,6 +508,9 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->max_logits = d.max_tokens < oxg::kMaxLogits ? d.max_tokens : oxg::kMaxLogits;
   M->part_rows = d.max_tokens > 1024 ? d.max_tokens : 1024;
   M->gen_cap = d.max_seq;
+  M->B = d.max_batch > 1 ? d.max_batch : 1;
+  M->kv_stride = (size_t)M->B * d.max_seq;
+  M->seq_pos.assign(M->B, 0);
   const size_t H = d.hidden, Tm = d.max_tokens;
   const size_t nmax = (size_t)(M->Nqkv > d.hidden ? M->Nqkv : d.hidden);
   size_t off = 0;
@@ -495,16 +519,17 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
     off = oxg::al(off + bytes);
     return o;
   };
-  const size_t o_kv = take((size_t)d.n_layers * 2 * d.n_kv_heads * d.max_seq * 64 * 2);
+  const size_t o_kv = take((size_t)d.n_layers * 2 * d.n_kv_heads * M->kv_stride * 64 * 2);
   const size_t o_cos = take((size_t)d.max_seq * 32 * 4), o_sin = take((size_t)d.max_seq * 32 * 4);
   const size_t o_res = take(Tm * H * 4), o_xn = take(Tm * H * 2), o_y = take(Tm * H * 4);
   const size_t o_part = take((size_t)M->part_rows * nmax * 4);
   const size_t o_qb = take(Tm * M->Nq * 2), o_cb = take(Tm * M->Nq * 2);
-  const size_t o_ap = take(oxg::attn_part_floats(d.n_kv_heads, M->G, d.max_seq) * 4);
+  const size_t o_ap = take(oxg::attn_part_floats(d.n_kv_heads, M->G, d.max_seq) * M->B * 4);
   const size_t o_lg = take((size_t)M->max_logits * d.vocab * 4);
   const size_t o_tok = take(Tm * 4), o_gen = take((size_t)M->gen_cap * 4), o_err = take(4);
   const size_t o_ds = take(4 * 4), o_first = take(4);
   const size_t o_amk = take(8 * 8), o_amc = take(4);
+  const size_t o_tp = take((size_t)M->B * 4), o_tr = take((size_t)M->B * 4);
   cudaError_t e = cudaMalloc(&M->state, off);
   if (e) {
     delete M;
@@ -529,6 +554,8 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->first = (int32_t *)(b + o_first);
   M->am_keys = (unsigned long long *)(b + o_amk);
   M->am_count = (unsigned int *)(b + o_amc);
+  M->tok_pos = (int32_t *)(b + o_tp);
+  M->tok_row0 = (int32_t *)(b + o_tr);
   // RoPE tables: angle(pos, i) = pos * theta^(-2i / head_dim), i < head_dim / 2,
   // evaluated in double and rounded once to f32.
   std::vector<float> cs((size_t)d.max_seq * 32), sn((size_t)d.max_seq * 32);
@@ -597,6 +624,7 @@ int oxg_model_reset(oxg_ctx *ctx) {
   ModelState *M = oxg::get_model(ctx);
   if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
   M->pos = 0;  // positions at or beyond pos are never read before they are written again
+  for (int &p : M->seq_pos) p = 0;
   M->state_ok = false;
   return OXG_OK;
 }
@@ -678,6 +706,56 @@ int oxg_model_route_tap(oxg_ctx *ctx, int32_t *idx_dev, int max_tokens) {
     return oxg::mfail(ctx, OXG_ERR_SHAPE, "max_tokens must be positive, got %d", max_tokens);
   M->route_tap = idx_dev;
   M->tap_tokens = idx_dev ? max_tokens : 0;
+  return OXG_OK;
+}
+
+int oxg_model_prefill_seq(oxg_ctx *ctx, int seq, const int32_t *tokens, int n_tokens, int32_t *next) {
+  if (!ctx) return oxg::ctx_error(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ModelState *M = oxg::get_model(ctx);
+  if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
+  if (seq < 0 || seq >= M->B)
+    return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "seq %d out of range [0, max_batch = %d)", seq, M->B);
+  if (n_tokens <= 0 || n_tokens > M->d.max_tokens)
+    return oxg::mfail(ctx, OXG_ERR_SHAPE, "n_tokens must be in [1, max_tokens = %d], got %d", M->d.max_tokens,
+                      n_tokens);
+  if (!tokens) return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "tokens_dev is NULL");
+  const int p = oxg::seq_pos_ref(*M, seq);
+  if (p + n_tokens > M->d.max_seq)
+    return oxg::mfail(ctx, OXG_ERR_SHAPE, "KV cache of sequence %d full: position %d + %d tokens exceeds max_seq %d",
+                      seq, p, n_tokens, M->d.max_seq);
+  oxg::DevGuard g(oxg::ctx_device(ctx));
+  return oxg::forward(ctx, *M, tokens, n_tokens, 1, nullptr, next, nullptr, seq);
+}
+
+int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens, int32_t *next, float *logits) {
+  if (!ctx) return oxg::ctx_error(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ModelState *M = oxg::get_model(ctx);
+  if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
+  if (n_seqs <= 0 || n_seqs > M->B)
+    return oxg::mfail(ctx, OXG_ERR_SHAPE, "n_seqs must be in [1, max_batch = %d], got %d", M->B, n_seqs);
+  if (!tokens || !next) return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "tokens_dev and next_dev must be non-NULL");
+  std::vector<int32_t> hp(n_seqs), hr(n_seqs);
+  int max_splits = 1;
+  for (int i = 0; i < n_seqs; ++i) {
+    const int p = oxg::seq_pos_ref(*M, i);
+    if (p + 1 > M->d.max_seq)
+      return oxg::mfail(ctx, OXG_ERR_SHAPE, "KV cache of sequence %d full: position %d + 1 exceeds max_seq %d", i, p,
+                        M->d.max_seq);
+    hp[i] = p;
+    hr[i] = i * M->d.max_seq;
+    const int sp = (p + 64) / 64;  // decode splits of 64 keys over positions 0 .. p
+    if (sp > max_splits) max_splits = sp;
+  }
+  oxg::DevGuard g(oxg::ctx_device(ctx));
+  cudaStream_t s = oxg::ctx_stream(ctx);
+  // pageable sources: each copy is staged before the call returns
+  MCUDA(ctx, cudaMemcpyAsync(M->tok_pos, hp.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s), "position copy");
+  MCUDA(ctx, cudaMemcpyAsync(M->tok_row0, hr.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s),
+        "cache row copy");
+  int rc = oxg::forward(ctx, *M, tokens, n_seqs, n_seqs, logits, next, nullptr, 0, true, max_splits);
+  if (rc) return rc;
+  for (int i = 0; i < n_seqs; ++i) oxg::seq_pos_ref(*M, i) += 1;
+  M->state_ok = false;  // sequence 0 moved without the one-token decode state
   return OXG_OK;
 }
 

@@ -51,7 +51,7 @@ class GPTModel:
     layer the attention arrays of ``_ATTN_KEYS`` and ``moe``, an MoE-block dict).
     """
 
-    def __init__(self, weights: dict, *, max_seq: int = 4096, max_tokens: int = 2048,
+    def __init__(self, weights: dict, *, max_seq: int = 4096, max_tokens: int = 2048, max_batch: int = 1,
                  ctx: abi.Context | None = None):
         # a context of its own (its layer ids 0..n_layers-1 must not collide
         # with other MoE layers), bound to torch's current stream
@@ -65,7 +65,8 @@ class GPTModel:
         self.max_tokens = int(min(max_tokens, max_seq))
         md = abi.ModelDims(self.n_layers, int(d["hidden"]), int(d["n_heads"]), int(d["n_kv_heads"]),
                            int(d["head_dim"]), self.vocab, int(d["sliding_window"]), self.max_seq,
-                           self.max_tokens, float(d["rope_theta"]), float(d["rms_eps"]))
+                           self.max_tokens, float(d["rope_theta"]), float(d["rms_eps"]), int(max_batch))
+        self.max_batch = max(int(max_batch), 1)
         lib, h = self.ctx.lib, self.ctx.handle
         abi.check(lib.oxg_model_init(h, ctypes.byref(md)), h)
         e, u, n = (_contig(weights[k]) for k in ("embed", "unembed", "final_norm"))
@@ -113,6 +114,25 @@ class GPTModel:
         """Device-side forward (no host synchronisation): ids int32 CUDA tensor."""
         abi.check(self.ctx.lib.oxg_model_forward(self.ctx.handle, ids.data_ptr(), int(ids.numel()), int(n_logits),
                                                  _ptr(logits), _ptr(nxt)), self.ctx.handle)
+
+    def prefill_seq(self, seq: int, input_ids) -> torch.Tensor:
+        """Appends a prompt (at most max_tokens ids) to sequence ``seq``'s own
+        KV cache; returns its greedy next token (int32 CUDA tensor [1])."""
+        ids = torch.as_tensor(np.asarray(input_ids, dtype=np.int32)).to(self._dev)
+        nxt = torch.empty(1, dtype=torch.int32, device=self._dev)
+        abi.check(self.ctx.lib.oxg_model_prefill_seq(self.ctx.handle, int(seq), ids.data_ptr(), int(ids.numel()),
+                                                     nxt.data_ptr()), self.ctx.handle)
+        return nxt
+
+    def step_batch(self, tokens: torch.Tensor, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """One token for each of sequences 0 .. len(tokens)-1 as one batch
+        (each attends to its own cache); returns their greedy next tokens
+        (int32 CUDA tensor) and fills ``logits`` [len(tokens), V] f32 if given."""
+        tok = tokens.to(device=self._dev, dtype=torch.int32).contiguous()
+        nxt = torch.empty(tok.numel(), dtype=torch.int32, device=self._dev)
+        abi.check(self.ctx.lib.oxg_model_step_batch(self.ctx.handle, int(tok.numel()), tok.data_ptr(),
+                                                    nxt.data_ptr(), _ptr(logits)), self.ctx.handle)
+        return nxt
 
     def decode(self, n_steps: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """n_steps greedy one-token steps on the device (a captured CUDA graph

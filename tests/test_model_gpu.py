@@ -221,3 +221,70 @@ def test_checkpoint_loader_uploads_the_same_model(tmp_path):
     b = g2.forward(prompt, n_logits=4).cpu().numpy()
     g2.release()
     assert np.array_equal(a, b)
+
+
+def test_batched_steps_match_single_sequences(small_model):
+    """Three sequences of different lengths (40; 150, past the 128-key
+    window; 90), each in its own KV cache, stepped together with
+    oxg_model_step_batch: one token per sequence per step, teacher-forced with
+    the tokens that sequence chose when run alone. Every step's logits match
+    the same sequence run alone within LOGIT_TOL. The exception is a row whose
+    routing took another expert at a near-tie; this can happen because the
+    MoE batch differs (3 tokens against 1). The routing taps find those rows,
+    and at most 3 of the 18 may be exempt."""
+    import torch
+    m, _ = small_model
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 4096, n) for n in (40, 150, 90)]
+    steps = 6
+    g = _gpu_model(m)
+    tap = g.route_tap(256)
+    ref_tok, ref_lg, ref_rt = [], [], []
+    for p in prompts:
+        g.reset_kv_cache()
+        lg = [g.forward(p)[0].cpu().numpy()]
+        toks, rts = [int(mo.greedy(lg[-1][None])[0])], []
+        for _ in range(steps):
+            lg.append(g.forward([toks[-1]])[0].cpu().numpy())
+            rts.append(np.sort(tap[:, 0].cpu().numpy(), axis=-1))
+            toks.append(int(mo.greedy(lg[-1][None])[0]))
+        ref_tok.append(toks)
+        ref_lg.append(np.stack(lg))
+        ref_rt.append(rts)
+    g.release()
+    gb = _gpu_model(m, max_batch=3)
+    first = [int(gb.prefill_seq(i, p).item()) for i, p in enumerate(prompts)]
+    assert first == [t[0] for t in ref_tok]
+    tapb = gb.route_tap(8)
+    worst, exempt = 0.0, 0
+    for k in range(steps):
+        toks = torch.tensor([ref_tok[i][k] for i in range(3)], dtype=torch.int32, device="cuda")
+        logits = torch.empty((3, 4096), dtype=torch.float32, device="cuda")
+        nxt = gb.step_batch(toks, logits).cpu().numpy()
+        lgk = logits.cpu().numpy()
+        rt = np.sort(tapb[:, :3].cpu().numpy(), axis=-1)
+        for i in range(3):
+            assert int(nxt[i]) == int(mo.greedy(lgk[i][None])[0])
+            if not np.array_equal(rt[:, i], ref_rt[i][k]):
+                exempt += 1
+                continue
+            err = float(np.abs(lgk[i] - ref_lg[i][k + 1]).max())
+            worst = max(worst, err)
+            assert err <= LOGIT_TOL, (i, k, err)
+            assert float(np.abs(lgk[i] - ref_lg[i][k + 1]).mean()) <= MEAN_TOL, (i, k)
+    print(f"batched vs single sequences: max |logit diff| {worst:.3e}, routing-exempt rows {exempt}/{3 * steps}")
+    assert exempt <= 3
+    assert gb.position() == 40 + steps  # sequence 0's position
+    gb.release()
+
+
+def test_batched_step_errors(small_model):
+    from oxidized_gpt_oss_b200 import abi
+    import torch
+    m, _ = small_model
+    gb = _gpu_model(m, max_batch=2)
+    with pytest.raises(abi.OxgError, match="max_batch"):
+        gb.step_batch(torch.zeros(3, dtype=torch.int32))
+    with pytest.raises(abi.OxgError, match="seq 2 out of range"):
+        gb.prefill_seq(2, [1, 2, 3])
+    gb.release()
