@@ -194,7 +194,7 @@ def run_reference(args):
         unit = "GB/s"
         sample = f"{rows} rows x {c1} cols of mlp1 per step ({per_step_bytes} B algorithmic)"
         config = {"workload": "dequant_layer", "rows": 32 * 5760 + 32 * 2880, "cols": 2880}
-    elif args.workload == "model_decode":
+    elif args.workload in ("model_decode", "model_batch"):
         # bounded sample: one decode token through one MoE block per step
         # (the reference's algorithm), scaled to the model's 24 layers
         d = synth.moe_layer(seed=0)
@@ -212,6 +212,9 @@ def run_reference(args):
         sample = (f"{n} decode tokens through one MoE block (reference algorithm, single thread) x "
                   f"{synth.GPT_OSS_20B_MODEL['n_layers']} layers; attention and LM head not counted")
         config = model_config(args, synth.GPT_OSS_20B_MODEL, args.prompt)
+        if args.workload == "model_batch":
+            # the reference decodes one sequence at a time: its rate is the batch-1 rate
+            config.update(workload="gpt_oss_20b_batched_decode", batch=args.batch, kv_length=args.prompt)
     else:
         # bounded sample of the workload's tokens: one per host thread
         T = min(args.tokens, max(threads, 1))
@@ -795,6 +798,169 @@ def run_model(args, ws, rank, local):
     return out
 
 
+ZIPF_S = 1.1
+BATCH_KERNELS = MODEL_KERNELS + ("router_topk", "permute", "combine")
+
+
+def zipf_router(m, s, seed):
+    """Skews each layer's expert loads: adds -s ln(rank) to the router bias,
+    ranks 1..E a seeded permutation per layer, so with router logits of about
+    unit spread the experts are picked with Zipf-like frequencies (rank^-s)."""
+    import torch
+    rng = np.random.default_rng(seed)
+    for lw in m["layers"]:
+        mw = lw["moe"]
+        rb = mw["router_b"]
+        E = rb.numel()
+        rank = np.empty(E)
+        rank[rng.permutation(E)] = np.arange(1, E + 1)
+        zb = torch.tensor(-s * np.log(rank), dtype=torch.float32, device=rb.device)
+        mw["router_b"] = (rb.view(torch.bfloat16).float() + zb).to(torch.bfloat16).view(torch.int16)
+
+
+def run_model_batch(args, ws, rank, local):
+    """Batched greedy decode over the full 24-layer gpt-oss-20b architecture:
+    ``--batch`` sequences, each with its own KV cache filled by a random
+    ``--prompt``-token prompt, then ``--steps`` timed steps that each advance
+    every sequence by one token (oxg_model_step_batch: one batch through the
+    projections, MoE blocks and LM head; attention per sequence). Router
+    biases skewed Zipf-like (s = 1.1) so the expert loads are imbalanced."""
+    import torch
+    from oxidized_gpt_oss_b200 import synth
+    from oxidized_gpt_oss_b200.model import GPTModel
+
+    device = torch.device("cuda", local)
+    over = {} if args.model_layers is None else {"n_layers": args.model_layers}
+    m = synth.model_weights_device(seed=rank, device=device, **over)
+    zipf_router(m, ZIPF_S, 77 + rank)
+    d = m["dims"]
+    B, P = args.batch, args.prompt
+    chunk = 2048
+    n_prof, n_e2e = 4, max(4, min(args.steps, 16))
+    max_seq = P + args.warmup + args.steps + n_prof + n_e2e + 8
+    g = GPTModel(m, max_seq=max_seq, max_tokens=min(chunk, max_seq), max_batch=B)
+    del m
+    torch.cuda.empty_cache()
+    ctx = g.ctx
+    rng = np.random.default_rng(4321 + rank)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    cur = torch.zeros(B, dtype=torch.int32, device=device)
+    ev[0].record(stream)
+    for sq in range(B):
+        prompt = torch.from_numpy(rng.integers(0, d["vocab"], P).astype(np.int32)).to(device)
+        for c0 in range(0, P, chunk):
+            nx = g.prefill_seq(sq, prompt[c0:c0 + chunk])
+        cur[sq:sq + 1].copy_(nx)
+    ev[1].record(stream)
+    for _ in range(args.warmup):
+        cur = g.step_batch(cur)
+    torch.cuda.synchronize()
+    g.sync()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    launches0 = ctx.launches()
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        torch.cuda.synchronize()
+        ev[2].record(stream)
+        for _ in range(args.steps):
+            cur = g.step_batch(cur)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+    g.sync()
+    ms = ev[2].elapsed_time(ev[3])
+    launches = ctx.launches() - launches0
+    ms_max = max_over_ranks(ms, ws)
+
+    # per-kernel device time: steps queued behind a GPU sleep, library CUDA
+    # events per launch; the routing of the last one gives the experts hit
+    tap = g.route_tap(B)
+    ctx.profile(True)
+    ctx.profile_reset()
+    for _ in range(n_prof):
+        torch.cuda._sleep(40_000_000)
+        cur = g.step_batch(cur)
+        torch.cuda.synchronize()
+    k_ms = {n: ctx.profile_read(n) for n in BATCH_KERNELS}
+    k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
+    ctx.profile(False)
+    routes = tap.cpu().numpy()  # [L, B, k]
+    g.route_tap(None)
+    L, E = d["n_layers"], d["n_experts"]
+    loads = np.stack([np.bincount(routes[li].ravel(), minlength=E) for li in range(L)])
+    hit = (loads > 0).sum(axis=1)
+
+    H, V = d["hidden"], d["vocab"]
+    nh, nkv, hd, W = d["n_heads"], d["n_kv_heads"], d["head_dim"], d["sliding_window"]
+    Nq, Nkv = nh * hd, nkv * hd
+    qkv_b = (Nq + 2 * Nkv) * H * 2
+    o_b = H * Nq * 2
+    mlp1_w = 2 * d["intermediate"] * H // 2 + 2 * d["intermediate"] * H // 32 + 2 * d["intermediate"] * 2
+    mlp2_w = H * d["intermediate"] // 2 + H * d["intermediate"] // 32 + H * 2
+    head_b = V * H * 2 + B * V * 4
+    pos_mid = P + args.warmup + args.steps / 2
+    kv_b = B * sum(2 * nkv * hd * 2 * (min(W, pos_mid) if (li % 2 == 0 and W) else pos_mid) for li in range(L))
+    per_kernel_bytes = {"linear_qkv": L * qkv_b, "linear_o": L * o_b, "moe_mlp1_decode": int(hit.sum()) * mlp1_w,
+                        "moe_mlp2_decode": int(hit.sum()) * mlp2_w, "lm_head": head_b, "attention": kv_b}
+    step_bytes = sum(per_kernel_bytes.values()) + L * E * H * 2
+    hbm, hbm_kind = peaks()
+    kern = {}
+    for n, (t, cnt) in k_ms.items():
+        per_step_ms = t / n_prof
+        e = {"us_per_step": per_step_ms * 1e3, "launches_per_step": cnt / n_prof}
+        if n in per_kernel_bytes:
+            e["gbs"] = per_kernel_bytes[n] / (per_step_ms * 1e-3) / 1e9
+        kern[n] = e
+    dom = max((n for n in kern if n in per_kernel_bytes), key=lambda n: kern[n]["us_per_step"])
+    dom_ms, dom_n = k_ms[dom]
+    achieved = per_kernel_bytes[dom] * n_prof / (dom_ms * 1e-3) / 1e9
+
+    # end to end through the public API: each step's tokens from pinned host
+    # memory, the greedy tokens back to pinned host memory
+    host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    host_tok.copy_(cur)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        nx = g.step_batch(host_tok.to(device, non_blocking=True))
+        host_tok.copy_(nx)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+
+    cfg = model_config(args, d, P)
+    cfg.update(workload="gpt_oss_20b_batched_decode", batch=B, kv_length=P,
+               router=f"bias -{ZIPF_S} ln(rank) per layer (seeded rank permutation): Zipf-like expert loads",
+               l2="inputs larger than L2: every step streams the weights of all hit experts and every KV run")
+    out = {"metric": METRIC, "value": ws * B * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 activations and attention weights, mxfp4 experts, f32 accumulate",
+           "data": "synthetic", "config": cfg,
+           "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "peak_kind": hbm_kind,
+                        "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                        "algorithmic_bytes_per_launch": per_kernel_bytes[dom] / max(dom_n / n_prof, 1),
+                        "avg_launch_us": dom_ms / max(dom_n, 1) * 1e3},
+           "step": {"hbm_gbs": step_bytes / (ms / args.steps * 1e-3) / 1e9,
+                    "frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / hbm, "bytes": step_bytes,
+                    "kernels": kern, "prefill_ms": prefill_ms, "prefill_tokens": B * P,
+                    "experts_hit_per_layer": float(hit.mean()),
+                    "max_expert_load_over_mean": float((loads.max(axis=1) / loads.mean(axis=1)).mean()),
+                    "kernel_times": "steps queued behind a GPU sleep, library CUDA events per launch"},
+           "e2e": {"value": B * n_e2e / e2e_s, "unit": "tokens/s",
+                   "what": f"oxg_model_step_batch x {n_e2e}: {B} tokens from pinned host memory in, "
+                           f"{B} greedy tokens to pinned host memory out per step",
+                   "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
+           "gpu_launches": launches,
+           "clocks": clk.summary()}
+    if rank == 0 and ws == 1:
+        cb = cpu_baseline_model(d)
+        cb["sample"] += "; the reference decodes one sequence at a time, so its rate does not grow with the batch"
+        out["cpu_baseline"] = cb
+    g.release()
+    return out
+
+
 def cpu_baseline_model(d):
     """The reference's algorithm for one decode token through one MoE block
     (REF-FAITHFUL oracle, single thread), scaled to the model's layers;
@@ -816,9 +982,11 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant", "model_decode"],
+    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant", "model_decode", "model_batch"],
                     default="moe_prefill")
-    ap.add_argument("--prompt", type=int, default=2048, help="model_decode: prompt tokens")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="model_decode: prompt tokens (default 2048); model_batch: KV length per sequence (8192)")
+    ap.add_argument("--batch", type=int, default=64, help="model_batch: concurrent sequences")
     ap.add_argument("--model-layers", type=int, default=None, help="model_decode: layers (default 24)")
     ap.add_argument("--no-decode", action="store_true",
                     help="moe_prefill on one GPU: skip the decode measurement added to the line")
@@ -837,6 +1005,8 @@ def main():
     args = ap.parse_args()
     if args.tokens is None:
         args.tokens = 8192 if args.workload == "moe_prefill" else 8
+    if args.prompt is None:
+        args.prompt = 8192 if args.workload == "model_batch" else 2048
     if args.impl == "reference":
         run_reference(args)
         return
@@ -850,7 +1020,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe,
-               "model_decode": run_model}[args.workload]
+               "model_decode": run_model, "model_batch": run_model_batch}[args.workload]
         out = run(args, ws, rank, local)
         if args.workload == "moe_prefill" and ws == 1 and not args.no_decode:
             # the metric's decode half (tokens/s and HBM GB/s at 8 tokens), same process

@@ -118,7 +118,10 @@ class GPTModel:
     def prefill_seq(self, seq: int, input_ids) -> torch.Tensor:
         """Appends a prompt (at most max_tokens ids) to sequence ``seq``'s own
         KV cache; returns its greedy next token (int32 CUDA tensor [1])."""
-        ids = torch.as_tensor(np.asarray(input_ids, dtype=np.int32)).to(self._dev)
+        if isinstance(input_ids, torch.Tensor):
+            ids = input_ids.to(device=self._dev, dtype=torch.int32).contiguous()
+        else:
+            ids = torch.as_tensor(np.asarray(input_ids, dtype=np.int32)).to(self._dev)
         nxt = torch.empty(1, dtype=torch.int32, device=self._dev)
         abi.check(self.ctx.lib.oxg_model_prefill_seq(self.ctx.handle, int(seq), ids.data_ptr(), int(ids.numel()),
                                                      nxt.data_ptr()), self.ctx.handle)
