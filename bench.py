@@ -171,13 +171,58 @@ def emit(d: dict):
 
 
 # --------------------------------------------------------------------------- reference arm
+def host_cpu():
+    """(cores this process may run on, CPU model name) of the host."""
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        cores = os.cpu_count() or 1
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return cores, model
+
+
+def ref_moe_rates(d, x_np, steps: int = 1):
+    """The reference's MoE algorithm (the oracle's REF-FAITHFUL restatement of
+    src/moe.rs:16-100 and src/model.rs:1088-1184: f16 buffers, per-call weight
+    conversion, sequential loops) on this host, measured two ways with explicit
+    thread counts (never inherited from OMP_NUM_THREADS, which torchrun sets
+    to 1): one token on one thread (the reference is single-threaded), and one
+    token per core on every core of the host. Returns tokens/s for both, the
+    core count and the CPU model; the same at every GPU count."""
+    from oracle import oracle
+    cores, model = host_cpu()
+    T = min(cores, x_np.shape[0])
+    W = oracle.Weights(d)
+    L = oracle.RefLayer(W, x_np[:T])
+    L.forward(x_np[:1], nthreads=1)  # warm: page in the weights
+    t0 = time.perf_counter()
+    L.forward(x_np[:1], nthreads=1)
+    one_s = time.perf_counter() - t0
+    L.forward(x_np[:T], nthreads=T)
+    t0 = time.perf_counter()
+    for _ in range(max(steps, 1)):
+        L.forward(x_np[:T], nthreads=T)
+    all_s = (time.perf_counter() - t0) / max(steps, 1)
+    L.close()
+    return {"single_thread": 1.0 / one_s, "all_cores": T / all_s, "cores": T, "cpu_model": model,
+            "single_thread_s_per_token": one_s, "all_cores_s_per_step": all_s}
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
         return
     from oracle import oracle
     from oxidized_gpt_oss_b200 import synth
-    threads = oracle.max_threads()
+    threads, cpu_model = host_cpu()
     if args.workload == "dequant":
         (w1, s1, r1, c1), _ = synth.dequant_tensors(seed=0)
         rows = 5760 * 4  # bounded sample: 4 experts' mlp1 rows per step
@@ -193,58 +238,53 @@ def run_reference(args):
         value = per_step_bytes * args.steps / dt / 1e9
         unit = "GB/s"
         sample = f"{rows} rows x {c1} cols of mlp1 per step ({per_step_bytes} B algorithmic)"
-        config = {"workload": "dequant_layer", "rows": 32 * 5760 + 32 * 2880, "cols": 2880}
-    elif args.workload in ("model_decode", "model_batch"):
-        # bounded sample: one decode token through one MoE block per step
-        # (the reference's algorithm), scaled to the model's 24 layers
-        d = synth.moe_layer(seed=0)
-        x = synth.activations(0, 1, d["hidden"])
-        L = oracle.RefLayer(oracle.Weights(d), x)
-        L.forward(x, nthreads=1)
-        n = max(1, min(args.steps, 8))
-        t0 = time.perf_counter()
-        for _ in range(n):
-            L.forward(x, nthreads=1)
-        per_token = (time.perf_counter() - t0) / n * synth.GPT_OSS_20B_MODEL["n_layers"]
-        value, unit = 1.0 / per_token, "tokens/s"
-        dt = per_token * args.steps
+        config = dequant_config()
         threads = 1
-        sample = (f"{n} decode tokens through one MoE block (reference algorithm, single thread) x "
-                  f"{synth.GPT_OSS_20B_MODEL['n_layers']} layers; attention and LM head not counted")
-        config = model_config(args, synth.GPT_OSS_20B_MODEL, args.prompt)
-        if args.workload == "model_batch":
-            # the reference decodes one sequence at a time: its rate is the batch-1 rate
-            config.update(workload="gpt_oss_20b_batched_decode", batch=args.batch, kv_length=args.prompt)
     else:
-        # bounded sample of the workload's tokens: one per host thread
-        T = min(args.tokens, max(threads, 1))
+        # bounded sample: one MoE block through the reference's algorithm,
+        # timed on one thread and on every core of the host (explicit thread
+        # counts: the same measurement at every GPU count)
         d = synth.moe_layer(seed=0)
-        x = synth.activations(0, T, d["hidden"])
-        W = oracle.Weights(d)
-        L = oracle.RefLayer(W, x)
-        for _ in range(min(args.warmup, 1)):
-            L.forward(x, nthreads=threads)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            L.forward(x, nthreads=threads)
-        dt = time.perf_counter() - t0
-        value = T * args.steps / dt
+        x = synth.activations(0, max(threads, 1), d["hidden"])
+        n_rep = 2 if args.workload in ("moe_prefill", "moe_decode") else 1
+        r = ref_moe_rates(d, x, steps=n_rep)
+        threads = r["cores"]
+        n_layers = synth.GPT_OSS_20B_MODEL["n_layers"]
         unit = "tokens/s"
-        sample = (f"{T} of the workload's {args.tokens} tokens per step through one MoE block "
-                  f"(reference algorithm, OpenMP over tokens)")
-        config = moe_config(args, d)
-        if args.workload == "moe_prefill":
-            config["workload"] = "moe_prefill"
+        if args.workload == "model_decode":
+            # one sequence decodes one token at a time, single-threaded, as the reference does
+            value = r["single_thread"] / n_layers
+            threads = 1
+            sample = (f"one token through one MoE block on one thread ({r['single_thread_s_per_token']:.2f} s) "
+                      f"x {n_layers} layers; attention and LM head not counted (an upper bound on its rate)")
+            config = model_config(args, synth.GPT_OSS_20B_MODEL, args.prompt)
+        elif args.workload == "model_batch":
+            # independent sequences: one per host core, each decoding as the reference does
+            value = r["all_cores"] / n_layers
+            sample = (f"{r['cores']} sequences' tokens through one MoE block, one per core "
+                      f"({r['all_cores_s_per_step']:.2f} s) x {n_layers} layers; attention and LM head "
+                      f"not counted (an upper bound on its rate)")
+            config = model_batch_config(args, synth.GPT_OSS_20B_MODEL)
+        else:
+            value = r["all_cores"]
+            sample = (f"{r['cores']} of the workload's {args.tokens} tokens per step (one per core) through one "
+                      f"MoE block, {n_rep} steps of {r['all_cores_s_per_step']:.2f} s")
+            config = prefill_config(args, d, ws) if args.workload == "moe_prefill" else moe_config(args, d)
+        dt = args.steps * (x.shape[0] / value if value > 0 else 0.0)
+    cb = {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample,
+          "cpu_model": cpu_model, "scope": "this host's cores, the same measurement at every GPU count"}
+    if args.workload != "dequant":
+        cb["single_thread_tokens_s"] = r["single_thread"]
+        cb["all_cores_tokens_s"] = r["all_cores"]
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": ws,
-          "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / max(args.steps, 1) * 1e3,
           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-          "data": "synthetic", "config": config,
-          "cpu_baseline": {"value": value, "unit": unit, "cores": min(threads, args.tokens)
-                           if args.workload != "dequant" else threads, "kind": "port", "sample": sample},
+          "data": "synthetic", "config": config, "cpu_baseline": cb,
           "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
 def moe_config(args, d):
+    """Workload description shared by both arms (so their configs compare equal)."""
     return {"workload": "moe_block_decode", "tokens_per_gpu": args.tokens, "hidden": d["hidden"],
             "intermediate": d["intermediate"], "experts": d["n_experts"], "top_k": d["top_k"],
             "weights": "mxfp4 e2m1 + e8m0[118,126]", "layers_cycled": args.layers,
@@ -252,18 +292,59 @@ def moe_config(args, d):
             "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "single"}
 
 
+def prefill_config(args, d, ws):
+    """The moe_prefill workload, shared by both arms."""
+    return {"workload": "moe_prefill", "tokens_per_gpu": args.tokens, "hidden": d["hidden"],
+            "intermediate": d["intermediate"], "experts": d["n_experts"], "top_k": d["top_k"],
+            "weights": "mxfp4 e2m1 + e8m0[118,126]", "layers_cycled": args.layers,
+            "l2": "inputs larger than L2 (424 MB of packed weights and 189 MB of slot activations per step)",
+            "parallelism": (f"ep{ws} (experts 32/{ws} per GPU; " +
+                            ("rows and output rows stored over NVLink peer memory by the library's kernels)"
+                             if args.ep == "p2p" else "NCCL all-to-all)")) if ws > 1 else "single"}
+
+
+def dequant_config():
+    return {"workload": "dequant_layer", "elements": 32 * 5760 * 2880 + 32 * 2880 * 2880,
+            "l2": "inputs larger than L2 (423 MB in, 1.59 GB out per step)"}
+
+
 # --------------------------------------------------------------------------- our arm
-def cpu_baseline_moe(d, x, T):
+def cpu_baseline_moe(d, x):
+    """The reference's algorithm on this host (rank 0, one GPU): the headline
+    value is one thread (the reference is single-threaded); the all-cores rate
+    (what the reference arm reports) rides along."""
+    r = ref_moe_rates(d, x, steps=1)
+    return {"value": r["single_thread"], "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"one token through one MoE block on one thread (the reference's algorithm as written), "
+                      f"{r['single_thread_s_per_token']:.2f} s",
+            "all_cores": {"value": r["all_cores"], "cores": r["cores"],
+                          "sample": f"{r['cores']} tokens, one per core, {r['all_cores_s_per_step']:.2f} s"},
+            "cpu_model": r["cpu_model"]}
+
+
+def oracle_parity(d, x_np, y, idx, w, logits, n_sample: int, seed: int):
+    """Checks sampled rows of a GPU forward against the fp64 SPEC oracle (the
+    checker; it runs beside the CPU baseline, outside every timed region):
+    routing identical to the oracle's own top-k except at near-ties, and the
+    layer bar max |err| <= 2e-2, sum|err| / sum|ref| <= 1e-3."""
     from oracle import oracle
+    cores, _ = host_cpu()
+    T, K = x_np.shape[0], d["top_k"]
+    sample = np.sort(np.random.default_rng(seed).choice(T, min(n_sample, T), replace=False))
     W = oracle.Weights(d)
-    L = oracle.RefLayer(W, x)
-    t0 = time.perf_counter()
-    L.forward(x, nthreads=1)
-    dt = time.perf_counter() - t0
-    L.close()
-    return {"value": T / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
-            "sample": f"one forward of {T} tokens through one MoE block, single thread (the reference's "
-                      f"algorithm as written), {dt:.2f} s"}
+    ref_logits = oracle.router_logits(W, x_np[sample])
+    ref_idx, _ = oracle.topk_softmax(ref_logits, K)
+    srt = -np.sort(-ref_logits, axis=1)
+    near_tie = (srt[:, K - 1] - srt[:, K]) < 1e-4
+    same = np.all(idx[sample] == ref_idx, axis=1)
+    y_ref = oracle.moe_forward_spec(W, x_np[sample], idx=idx[sample], wts=w[sample], acc64=True, nthreads=cores)
+    err = np.abs(y[sample] - y_ref)
+    max_abs = float(err.max())
+    mean_rel = float(err.sum() / max(np.abs(y_ref).sum(), 1e-30))
+    return {"oracle_sample_tokens": int(sample.size), "oracle_max_abs": max_abs, "oracle_mean_rel": mean_rel,
+            "routing_matches_oracle": bool(np.all(same | near_tie)),
+            "logits_max_abs_diff": float(np.abs(logits[sample] - ref_logits).max()),
+            "within_bar": bool(max_abs <= 2e-2 and mean_rel <= 1e-3 and np.all(same | near_tie))}
 
 
 def gpu_layers(args, d0, device):
@@ -404,7 +485,13 @@ def run_moe(args, ws, rank, local):
            "gpu_launches": launches,
            "clocks": clk.summary()}
     if rank == 0 and ws == 1:
-        out["cpu_baseline"] = cpu_baseline_moe(d0, xs_np[0], T)
+        out["cpu_baseline"] = cpu_baseline_moe(d0, xs_np[0])
+        # parity of the measured configuration: layer 0 on batch 0 against the oracle
+        y0 = layers[0].forward(xs[0], mode=mode)
+        idx0, w0, lg0 = layers[0].route(xs[0])
+        ctx.sync()
+        out["parity"] = oracle_parity(d0, xs_np[0], y0.cpu().numpy(), idx0.cpu().numpy(), w0.cpu().numpy(),
+                                      lg0.cpu().numpy(), n_sample=T, seed=T)
     return out
 
 
@@ -532,46 +619,52 @@ def run_prefill(args, ws, rank, local):
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": ("mxfp4 weights (E2M1 + E8M0 into tcgen05 block-scaled MMA) x bf16 activations as E4M3 "
-                     "terms (2 for x, 3 for h), f32 accumulate") if mxf else
+                     "terms (2 for x, 4 for h), f32 accumulate") if mxf else
                     "mxfp4 weights x bf16 activations (exact f16 tcgen05 operands), f32 accumulate",
            "data": "synthetic",
-           "config": {"workload": "moe_prefill", "tokens_per_gpu": T, "hidden": H, "intermediate": I,
-                      "experts": E, "top_k": K, "weights": "mxfp4 e2m1 + e8m0[118,126]",
-                      "layers_cycled": args.layers,
-                      "l2": "inputs larger than L2 (424 MB of packed weights and 189 MB of slot "
-                            "activations per step)",
-                      "parallelism": (f"ep{ws} (experts 32/{ws} per GPU; " +
-                                      ("rows and output rows stored over NVLink peer memory by the "
-                                       "library's kernels)" if p2p is not None else "NCCL all-to-all)"))
-                                     if ws > 1 else "single",
-                      "expert_rows_per_step_rank0": rows_per_step},
+           "config": prefill_config(args, d0, ws),
            "roofline": {"bound": "tensor", "kernel": k1, "achieved": achieved, "peak": peak,
                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": achieved / peak,
                         "traffic": ncu_traffic(k1, f"T{T}") if ws == 1 else None,
                         "algorithmic_flop_per_launch": flop1,
                         "flop_per_unit": f1_row, "unit_of_work": "expert row (token, slot)",
                         "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3},
-           "layer": {"tflops": layer_tflops, "frac": layer_tflops / peak,
-                     "kernel_us_per_step": {n: v[0] / max(v[1], 1) * 1e3 for n, v in k_ms.items()},
-                     "mlp2_tflops": flop2 * m2_n / (m2_ms * 1e-3) / 1e12},
            "e2e": {"value": T * ws * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
            "gpu_launches": launches,
-           "clocks": clk.summary()}
+           "clocks": clk.summary(),
+           "layer": {"tflops": layer_tflops, "frac": layer_tflops / peak,
+                     "kernel_us_per_step": {n: round(v[0] / max(v[1], 1) * 1e3, 1) for n, v in k_ms.items()},
+                     "mlp2_tflops": flop2 * m2_n / (m2_ms * 1e-3) / 1e12,
+                     "expert_rows_per_step_rank0": rows_per_step}}
+
+    # parity of the measured configuration, outside the timed regions
+    if ws > 1:
+        # every rank: the expert-parallel output of its 8192 tokens against a
+        # forward of the same tokens with every expert of the layer on this GPU
+        full = MoELayer(d0, ctx=ctx, layer=args.layers)
+        full.reserve(T)
+        y_ep = step(0, xs[0]).clone()
+        y_one = full.forward(xs[0], mode=mode)
+        ctx.sync()
+        eq = bool(torch.equal(y_ep, y_one))
+        diff = float((y_ep - y_one).abs().max().item())
+        import torch.distributed as dist
+        t = torch.tensor([0.0 if eq else 1.0, diff], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out["parity"] = {"ep_bit_exact": bool(t[0].item() == 0.0), "ep_max_abs_diff": float(t[1].item()),
+                         "ranks_checked": ws, "tokens_per_rank": T,
+                         "against": "the same tokens through oxg_moe_forward with all 32 experts on one GPU"}
+        full.release()
     if p2p is not None:
         p2p.close()
     if rank == 0 and ws == 1:
-        from oracle import oracle
-        n_cpu = 2
-        W = oracle.Weights(d0)
-        L = oracle.RefLayer(W, xs_np[0][:n_cpu])
-        t0 = time.perf_counter()
-        L.forward(xs_np[0][:n_cpu], nthreads=1)
-        dt = time.perf_counter() - t0
-        L.close()
-        out["cpu_baseline"] = {"value": n_cpu / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
-                               "sample": f"{n_cpu} of the {T} tokens through the reference's algorithm, "
-                                         f"single thread, {dt:.2f} s"}
+        out["cpu_baseline"] = cpu_baseline_moe(d0, xs_np[0])
+        y0 = layers[0].forward(xs[0], out=y, mode=mode)
+        idx0, w0, lg0 = layers[0].route(xs[0])
+        ctx.sync()
+        out["parity"] = oracle_parity(d0, xs_np[0], y0.cpu().numpy(), idx0.cpu().numpy(), w0.cpu().numpy(),
+                                      lg0.cpu().numpy(), n_sample=32, seed=T)
     return out
 
 
@@ -633,8 +726,7 @@ def run_dequant(args, ws, rank, local):
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8->bf16",
            "data": "synthetic",
-           "config": {"workload": "dequant_layer", "elements": (r1 * c1 + r2 * c2),
-                      "l2": "inputs larger than L2 (423 MB in, 1.59 GB out per step)"},
+           "config": dequant_config(),
            "roofline": {"bound": "hbm", "kernel": "dequant_mxfp4", "achieved": achieved, "peak": hbm,
                         "peak_kind": hbm_kind, "unit": "GB/s", "frac": achieved / hbm,
                         "traffic": ncu_traffic("dequant_mxfp4", "layer"),
@@ -666,6 +758,15 @@ def model_config(args, d, prompt):
             "weights": "random init: attention/embeddings bf16, experts mxfp4 e2m1 + e8m0[118,126]",
             "l2": "inputs larger than L2: every step streams ~3.7 GB of weights",
             "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "single"}
+
+
+def model_batch_config(args, d):
+    """The model_batch workload (configuration 4), shared by both arms."""
+    cfg = model_config(args, d, args.prompt)
+    cfg.update(workload="gpt_oss_20b_batched_decode", batch=args.batch, kv_length=args.prompt,
+               router=f"bias -{ZIPF_S} ln(rank) per layer (seeded rank permutation): Zipf-like expert loads",
+               l2="inputs larger than L2: every step streams the weights of all hit experts and every KV run")
+    return cfg
 
 
 def run_model(args, ws, rank, local):
@@ -928,10 +1029,7 @@ def run_model_batch(args, ws, rank, local):
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
 
-    cfg = model_config(args, d, P)
-    cfg.update(workload="gpt_oss_20b_batched_decode", batch=B, kv_length=P,
-               router=f"bias -{ZIPF_S} ln(rank) per layer (seeded rank permutation): Zipf-like expert loads",
-               l2="inputs larger than L2: every step streams the weights of all hit experts and every KV run")
+    cfg = model_batch_config(args, d)
     out = {"metric": METRIC, "value": ws * B * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -969,11 +1067,15 @@ def cpu_baseline_model(d):
     from oxidized_gpt_oss_b200 import synth
     d0 = synth.moe_layer(seed=0)
     x = synth.activations(0, 1, d0["hidden"])
-    b = cpu_baseline_moe(d0, x, 1)
-    per_token_s = d["n_layers"] / b["value"]
-    return {"value": 1.0 / per_token_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+    cores, _ = host_cpu()
+    b = cpu_baseline_moe(d0, synth.activations(0, cores, d0["hidden"]))
+    n = d["n_layers"]
+    return {"value": b["value"] / n, "unit": "tokens/s", "cores": 1, "kind": "port",
             "sample": f"one token through one MoE block (the reference's algorithm, single thread, "
-                      f"{1.0 / b['value']:.2f} s) x {d['n_layers']} layers; attention and LM head not counted"}
+                      f"{1.0 / b['value']:.2f} s) x {n} layers; attention and LM head not counted",
+            "all_cores": {"value": b["all_cores"]["value"] / n, "cores": b["all_cores"]["cores"],
+                          "sample": "one sequence per core, each as above"},
+            "cpu_model": b["cpu_model"]}
 
 
 def main():
@@ -1022,20 +1124,38 @@ def main():
         run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe,
                "model_decode": run_model, "model_batch": run_model_batch}[args.workload]
         out = run(args, ws, rank, local)
-        if args.workload == "moe_prefill" and ws == 1 and not args.no_decode:
-            # the metric's decode half (tokens/s and HBM GB/s at 8 tokens), same process
-            dargs = argparse.Namespace(**vars(args))
-            dargs.tokens, dargs.steps, dargs.warmup = 8, max(args.steps, 20), max(args.warmup, 5)
-            dec = run_moe(dargs, ws, rank, local)
-            out["decode"] = {k: dec[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline", "e2e",
-                                                  "config", "cpu_baseline") if k in dec}
+        def brief(r):
+            # the figures a reader of the line needs, kept short so that the
+            # end of the line (decode last) survives a truncated log tail
+            rf = r.get("roofline", {})
+            b = {"value": r["value"], "unit": r["unit"], "ms_per_step": r["ms_per_step"], "steps": r["steps"],
+                 "roofline": {k: rf.get(k) for k in ("kernel", "achieved", "peak", "unit", "frac", "traffic",
+                                                      "avg_launch_us", "algorithmic_bytes_per_launch")},
+                 "e2e": r.get("e2e"), "gpu_launches": r.get("gpu_launches")}
+            for k in ("parity", "cpu_baseline"):
+                if k in r:
+                    b[k] = r[k]
+            return b
+
         if args.workload == "moe_prefill" and ws == 1 and not args.no_model:
             # configuration 2: the full 24-layer decoder, batch 1, greedy decode
             margs = argparse.Namespace(**vars(args))
             margs.steps, margs.warmup = 64, 4
             md = run_model(margs, ws, rank, local)
-            out["model_decode"] = {k: md[k] for k in ("value", "unit", "ms_per_step", "steps", "roofline", "step",
-                                                      "e2e", "config", "cpu_baseline", "gpu_launches") if k in md}
+            out["model_decode"] = brief(md)
+            st = md.get("step", {})
+            out["model_decode"]["step"] = {k: st.get(k) for k in ("hbm_gbs", "frac", "eager_steps_match_graph_steps",
+                                                                  "generate_matches_device_loop")}
+            out["model_decode"]["kernel_us_per_step"] = {n: round(v["us_per_step"], 1)
+                                                         for n, v in st.get("kernels", {}).items()}
+        if args.workload == "moe_prefill" and ws == 1 and not args.no_decode:
+            # the metric's decode half (tokens/s and HBM GB/s at 8 tokens), same process; last in the line
+            dargs = argparse.Namespace(**vars(args))
+            dargs.tokens, dargs.steps, dargs.warmup = 8, max(args.steps, 20), max(args.warmup, 5)
+            dec = run_moe(dargs, ws, rank, local)
+            out["decode"] = brief(dec)
+            out["decode"]["layer_frac"] = dec["layer"]["frac"]
+            out["decode"]["kernel_us_per_step"] = {n: round(v, 1) for n, v in dec["layer"]["kernel_us_per_step"].items()}
         if rank == 0:
             emit(out)
     finally:

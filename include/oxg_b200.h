@@ -238,9 +238,11 @@ OXG_API int oxg_ep_close(oxg_ctx *ctx);
 /* Rows this process received in its last oxg_moe_forward_ep (waits for it). */
 OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
 
-/* Has no counterpart in the reference. The same layer forward as
- * oxg_moe_forward (same kernels, same results), for callers that must not
- * have the library allocate device memory during a forward: serving runtimes
+/* Has no counterpart in the reference. The same layer math as
+ * oxg_moe_forward (router, top-k, expert MLPs, weighted combine; outputs
+ * within the layer tolerance of oxg_moe_forward's, not bit-identical: the
+ * small-batch path of oxg_moe_forward sums in another order), for callers
+ * that must not have the library allocate device memory during a forward: serving runtimes
  * that reserve the whole GPU for their own memory pool, decode loops that
  * cannot absorb the synchronisation a cudaMalloc/cudaFree may cause, and
  * embedders that forbid foreign code from allocating. This call allocates
@@ -252,7 +254,10 @@ OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
  * OXG_ERR_SHAPE and a message giving the largest token count that fits (45
  * tokens of a gpt-oss-20b layer). The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress, done once per device), so make
- * that first call before any stream capture. All calls share the one array and
+ * that first call before any stream capture; the address is cached for the
+ * life of the process, so do not use this call after a cudaDeviceReset. A
+ * layer uploaded as an expert-parallel shard is refused (OXG_ERR_STATE). All
+ * calls share the one array and
  * it keeps the last call's contents (every part is rewritten before it is read,
  * so nothing is cleared); calls that overlap on the GPU — concurrent streams,
  * contexts or threads on the same device — race on it and must be serialised

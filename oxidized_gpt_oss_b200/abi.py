@@ -1,8 +1,8 @@
 """ctypes binding of liboxg_b200.so (the C ABI in include/oxg_b200.h).
 
-This is the binding a host runner writes against the library; the Rust form a
-maintainer of the reference would add is in INTEGRATION.md. Loading fails
-loudly if the library has not been built: there is no fallback path.
+This is the binding a host runner writes against the library (a Rust runner
+declares the same functions in an ``extern "C"`` block). Loading fails loudly
+if the library has not been built: there is no fallback path.
 """
 from __future__ import annotations
 

@@ -14,6 +14,10 @@ namespace oxg {
 // stream. Returns false, with the context's last error set, when the layer
 // has not been uploaded.
 bool ctx_layer(oxg_ctx *ctx, int layer, MoeDeviceWeights *w, int *device, cudaStream_t *stream);
+// Resident expert range [*begin, *begin + *count) of uploaded layer `layer`
+// (all experts unless it was uploaded with oxg_moe_upload_shard); false when
+// the layer has not been uploaded.
+bool ctx_layer_experts(oxg_ctx *ctx, int layer, int *begin, int *count, int *n_experts);
 
 // Records `msg` as the context's last error and returns `status`.
 int ctx_error(oxg_ctx *ctx, int status, const char *msg);

@@ -8,14 +8,25 @@
 // fail or fragment the pool), a real-time decode loop that cannot afford the
 // device-wide synchronisation cudaMalloc/cudaFree may imply, or an embedding
 // runtime whose policy is that foreign code never allocates device memory.
-// oxg_moe_forward_noalloc serves them: the same kernels, with the scratch
-// carved out of one fixed array compiled into this library.
+// oxg_moe_forward_noalloc serves them: the same layer math (router, top-k,
+// expert MLPs, weighted combine) on the library's per-expert decode kernels,
+// with the scratch carved out of one fixed array compiled into this library.
+// Its outputs agree with oxg_moe_forward's within the layer tolerance; they
+// are not bit-identical, because oxg_moe_forward's small-batch path uses the
+// fused router and the scheduled expert kernels, which sum in another order.
 //
 // The array is a file-scope __device__ variable, so every GPU that loads the
 // library holds kNoAllocScratchBytes of it until the process exits. Its host
 // name is only a stand-in for the device symbol, so the device address is
 // looked up once per device with cudaGetSymbolAddress (with that device
-// current) on the first call made there, and cached.
+// current) on the first call made there, and cached for the life of the
+// process: a cudaDeviceReset (or anything else that tears down and recreates
+// the device's primary context) invalidates it, so this entry point must not
+// be used after one.
+//
+// The decode kernels used here stream their weights with cp.async, which has
+// no bounded wait that could give up, so no error word is carved out: a call
+// that returns OXG_OK has launched work that cannot report a timeout.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -98,6 +109,20 @@ extern "C" int oxg_moe_forward_noalloc(oxg_ctx *ctx, int layer, const uint16_t *
   int device = 0;
   cudaStream_t stream = nullptr;
   if (!oxg::ctx_layer(ctx, layer, &w, &device, &stream)) return OXG_ERR_STATE;
+  {
+    // an expert-parallel shard holds only some experts' weights; the kernels
+    // below index every expert of the layer, so refuse it before any launch
+    // (oxg_moe_forward refuses it with the same message)
+    int eb = 0, ec = 0, ne = 0;
+    if (oxg::ctx_layer_experts(ctx, layer, &eb, &ec, &ne) && ec != ne) {
+      char msg[256];
+      snprintf(msg, sizeof(msg),
+               "layer %d holds experts [%d, %d) only: use oxg_moe_dispatch / oxg_moe_experts / "
+               "oxg_moe_combine",
+               layer, eb, eb + ec);
+      return oxg::ctx_error(ctx, OXG_ERR_STATE, msg);
+    }
+  }
   const int T = n_tokens;
   if (T < 0) return oxg::ctx_error(ctx, OXG_ERR_SHAPE, "n_tokens must be >= 0");
   if (T == 0) return OXG_OK;

@@ -796,6 +796,15 @@ bool ctx_layer(oxg_ctx *ctx, int layer, MoeDeviceWeights *w, int *device, cudaSt
   return true;
 }
 
+bool ctx_layer_experts(oxg_ctx *ctx, int layer, int *begin, int *count, int *n_experts) {
+  Layer *L = get_layer(ctx, layer);
+  if (!L) return false;
+  *begin = L->expert_begin;
+  *count = L->expert_count;
+  *n_experts = L->dims.n_experts;
+  return true;
+}
+
 int ctx_error(oxg_ctx *ctx, int status, const char *msg) { return fail(ctx, status, "%s", msg); }
 
 int ctx_device(const oxg_ctx *ctx) { return ctx->device; }

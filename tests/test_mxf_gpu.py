@@ -2,7 +2,7 @@
 
 The E2M1 weights and their E8M0 scales go straight into
 tcgen05.mma.kind::mxf8f6f4; x enters as two E4M3 terms per element and the
-SwiGLU output as three (one UE8M0 exponent per 32-element block). Same bar as
+SwiGLU output as four (one UE8M0 exponent per 32-element block). Same bar as
 every MoE parity test: max |err| <= 2e-2 and sum|err| / sum|ref| <= 1e-3
 against the fp64-accumulating oracle, plus agreement with the in-register-
 dequant decode path (OXG_MODE_DECODE) on the same inputs.

@@ -73,6 +73,41 @@ def test_prefill_gpt_oss_widths(cuda_ctx):
     print(f"prefill gpt-oss widths: max_abs={max_abs:.3e} mean_rel={mean_rel:.3e}")
 
 
+def test_prefill_benchmark_shape_8192_tokens(cuda_ctx):
+    """The benchmarked configuration itself: 8192 tokens through one
+    gpt-oss-20b MoE block (the bench's layer, seed 0) on the default path
+    (AUTO, which takes the tcgen05 grouped GEMMs here). Every expert gets
+    ~1024 slots, i.e. 4-5 token tiles of 256, so tiles beyond the first of
+    each expert are exercised. A seeded sample of 96 tokens (all k slots of
+    each, spread over the whole batch and so over every token tile) is
+    checked against the fp64 oracle; routing must equal the oracle's own
+    top-k except at near-ties (k-th and (k+1)-th logits closer than 1e-4)."""
+    import torch
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    d = synth.moe_layer(seed=0)
+    T, K = 8192, d["top_k"]
+    x = synth.activations(4242, T, d["hidden"])
+    layer = MoELayer(d)
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    y = layer.forward(xt).cpu().numpy()
+    idx, w, logits = (a.cpu().numpy() for a in layer.route(xt))
+    layer.ctx.sync()
+    counts = np.bincount(idx.ravel(), minlength=d["n_experts"])
+    assert counts.max() > 768, "some expert must span more than three 256-slot tiles"
+    sample = np.sort(np.random.default_rng(8192).choice(T, 96, replace=False))
+    W = oracle.Weights(d)
+    ref_logits = oracle.router_logits(W, x[sample])
+    assert np.max(np.abs(logits[sample] - ref_logits)) < 1e-4 * max(1.0, np.abs(ref_logits).max())
+    ref_idx, _ = oracle.topk_softmax(ref_logits, K)
+    srt = -np.sort(-ref_logits, axis=1)
+    near_tie = (srt[:, K - 1] - srt[:, K]) < 1e-4
+    same = np.all(idx[sample] == ref_idx, axis=1)
+    assert np.all(same | near_tie), f"routing differs on tokens {sample[~(same | near_tie)]}"
+    max_abs, mean_rel = _check(d, x[sample], y[sample], idx[sample], w[sample])
+    layer.release()
+    print(f"prefill 8192 tokens, 96 sampled: max_abs={max_abs:.3e} mean_rel={mean_rel:.3e}")
+
+
 def test_prefill_matches_decode_path(cuda_ctx):
     """The two GPU paths (tcgen05 prefill, mma decode) on the same inputs."""
     import torch

@@ -2,7 +2,8 @@
 library allocate device memory (runtimes that pre-reserve the whole GPU,
 latency-critical loops that cannot absorb an allocation's synchronisation,
 embedders that forbid foreign allocations). Its scratch is a fixed 4 MiB
-array inside the library; its results must equal oxg_moe_forward's.
+array inside the library; its results must agree with oxg_moe_forward's within
+the layer tolerance.
 
 This file is collected last so that, if it fails, a run stopping at the first
 failure has already run every other test. It creates its own context, so it
@@ -40,6 +41,22 @@ def test_noalloc_matches_forward_on_two_calls_in_a_row():
         assert torch.isfinite(out).all()
         assert err.max().item() <= MAX_ABS
         assert (err.sum() / ref.abs().sum()).item() <= MEAN_REL
+
+
+def test_noalloc_refuses_an_expert_parallel_shard():
+    """A layer uploaded as a shard (experts [8, 16) of 32) holds only those
+    experts' weights; the call must refuse it before launching anything."""
+    import torch
+    from oxidized_gpt_oss_b200.moe import MoELayer
+    d = synth.moe_layer(seed=23, hidden=256, intermediate=256, n_experts=32, top_k=4)
+    layer = MoELayer(d, experts=(8, 8))
+    x = torch.zeros((4, layer.hidden), dtype=torch.int16, device="cuda")
+    out = torch.empty((4, layer.hidden), dtype=torch.float32, device="cuda")
+    st = _noalloc(layer, x, out)
+    assert st == abi.OXG_ERR_STATE
+    msg = abi.load().oxg_last_error(layer.ctx.handle).decode()
+    assert "holds experts [8, 16) only" in msg
+    layer.release()
 
 
 def test_noalloc_refuses_batches_beyond_its_array():
