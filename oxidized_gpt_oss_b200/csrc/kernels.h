@@ -101,7 +101,17 @@ struct RouteSmallArgs {
   // per expert the bit mask of the tokens routed to it (T <= 32)
   uint8_t *xq, *xsf;
   uint32_t *tok_mask;
+  // optional: the active experts cut into groups of at most kVirtualTokens
+  // consecutive slots ("virtual experts", expert order then slot order):
+  // expert id, first position and slot count of each, and their number
+  int32_t *v_expert, *v_pos0, *v_count, *n_virtual;
 };
+constexpr int kVirtualTokens = 8;
+// Upper bound on the virtual experts of T tokens routed top-k over E experts.
+inline int max_virtual(int E, int T, int k) {
+  const int S = T * k, a = E < S ? E : S;
+  return a + S / kVirtualTokens;
+}
 // pdl: launch with programmatic stream serialisation (overlaps the previous
 // kernel's tail; the kernel waits for it before touching memory).
 cudaError_t launch_route_small(const RouteSmallArgs &a, cudaStream_t stream, bool pdl);
@@ -193,12 +203,24 @@ cudaError_t launch_moe_mlp2_decode(const MoeDeviceWeights &w, const float *h,
 struct DecodeSched {
   const int32_t *active, *n_active;
   int max_active;  // grid.y: upper bound on the number of active experts
+  int exp_active;  // expected number of active experts (uniform routing)
   int bands1;      // per-expert bands of the mlp1 kernel (when not all-token)
   int bands2;      // per-expert bands of the mlp2 kernel
   int n_sms;       // persistent grid of the all-token mlp1 kernel
   bool pdl;
   int *err;        // error word (bounded waits of the weight streams)
+  // flat-split kernels: partial sums, flat_parts_bytes(n_sms) bytes, and
+  // kFlatMaxWarps arrival counters, zero between launches
+  float4 *parts;
+  uint32_t *flat_cnt;
+  // virtual experts from the routing kernel (8 < T <= 64): expert, first
+  // position, slot count, number; max_virtual bounds the number
+  const int32_t *v_expert, *v_pos0, *v_count, *n_virtual;
+  int max_virtual;
 };
+constexpr int kFlatMaxWarps = 8192;  // grid warps a flat-split launch may use (n_sms x warps per CTA)
+// Partial-sum scratch of the flat-split decode kernels on a GPU with n_sms SMs.
+inline size_t flat_parts_bytes(int n_sms) { return (size_t)n_sms * 32 * 2 * 2 * 32 * 16; }
 // Bands (CTAs per expert) so that expected_active experts fill n_sms SMs.
 int decode_bands(int rows, int expected_active, int n_sms);
 // mlp2's fused combine counts finished experts per row band in band_done,

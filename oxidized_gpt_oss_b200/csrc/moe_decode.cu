@@ -36,6 +36,8 @@
 //    ~2^-22 relative), so the intermediate is not rounded to 16 bits. For an
 //    expert with at most 4 tokens, hi and lo of token j sit in MMA columns 2j
 //    and 2j+1 (one MMA per k-step); otherwise each half takes its own MMA.
+#include <cmath>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -75,6 +77,24 @@ constexpr int kDeepTokens = 2;
 constexpr int kW1d = 28, kS1d = 5, kK1d = 4;  // mlp1: 7 groups of 4 warps splitting K
 constexpr int kW3d = 20, kS3d = 7, kK3d = 4;  // mlp2: 5 groups of 4 warps splitting K
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
+// Flat-split kernels: warps x ring stages per CTA, one CTA per SM. mlp1
+// stages 8 activation rows, mlp2 16 (two column groups of four slots' hi / lo
+// halves); the rest of shared memory is the warps' rings.
+#ifndef OXG_FLAT_W1
+#define OXG_FLAT_W1 24
+#define OXG_FLAT_S1 6
+#endif
+#ifndef OXG_FLAT_W2B
+#define OXG_FLAT_W2B 20
+#define OXG_FLAT_S2B 6
+#endif
+constexpr int kWf1 = OXG_FLAT_W1, kSf1 = OXG_FLAT_S1;
+constexpr int kWf2b = OXG_FLAT_W2B, kSf2b = OXG_FLAT_S2B;
+#ifndef OXG_DEC_FLAT
+#define OXG_DEC_FLAT 1
+#endif
+constexpr bool kUseFlat = OXG_DEC_FLAT != 0;
+constexpr size_t kMaxFlatSmem = 220 * 1024;  // dynamic shared memory (static arrays take the rest of 227 KB)
 
 struct DecodeArgs {
   const uint8_t *codes;   // tile chunks of [E, rows, K] (codes + scales)
@@ -111,6 +131,13 @@ struct DecodeArgs {
   const float *wts;
   float *y;
   int *err;  // error word: bounded waits that ran out record their code here
+  // flat split (flat kernels): per grid warp two float4 x 32 partial-sum
+  // slots, and per grid warp one arrival counter (zero between launches)
+  float4 *parts;
+  uint32_t *flat_cnt;
+  // grouped kernels: virtual experts (expert id, first position, slot count
+  // of each group of at most kVirtualTokens slots, and their number)
+  const int32_t *v_expert, *v_pos0, *v_count, *n_virtual;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -456,8 +483,782 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_alltok_kernel(const Decode
 }
 
 // ---------------------------------------------------------------------------
-// Per-expert kernel: CTA = (expert, band of tiles); tokens staged per expert.
+// Flat split (T <= 8 tokens). The launch's work is one sequence of weight
+// chunks — (item, group) with item an (active expert, 16-row tile) and group
+// one 128-element step of K — cut into equal contiguous ranges, one per warp
+// of the grid, so every warp streams the same number of bytes whatever the
+// number of active experts and tiles (a per-tile split leaves the warps of a
+// last, partial round idle: at one token 1440 mlp1 tiles over 1036 warp
+// groups). An item split between warps is summed by the warp that finishes
+// its part last: each part lands in its warp's slot, and the last arrival adds
+// the parts in range order — the same order every run, whichever warp is last.
 // ---------------------------------------------------------------------------
+// Balanced partition in 32-bit arithmetic (64-bit divisions are long
+// instruction sequences on the GPU): the first r warps take q + 1 chunks, the
+// other W - r take q, with q = C / W and r = C % W.
+struct FlatRange {
+  int C;  // chunks of the launch (or of one expert)
+  int W;  // warps sharing them (<= C)
+  int q, r;
+  // warp w (< W) streams chunks [first(w), first(w + 1))
+  __device__ __forceinline__ int first(int w) const { return w * q + min(w, r); }
+  // the warp whose range holds chunk x
+  __device__ __forceinline__ int owner(int x) const {
+    const int b = r * (q + 1);
+    return x < b ? x / (q + 1) : r + (x - b) / q;
+  }
+  // first(w) for any warp of the grid: warps w >= W (when the grid has more
+  // warps than there are chunks) get the empty range [C, C)
+  __device__ __forceinline__ int lo(int w) const { return w >= W ? C : first(w); }
+};
+// At most one warp per chunk, so that every warp of the range has a non-empty
+// share and the owners of an item's chunks are consecutive warps.
+__device__ __forceinline__ FlatRange flat_range(int chunks, int grid_warps) {
+  FlatRange R;
+  R.C = chunks;
+  R.W = chunks < grid_warps ? (chunks > 0 ? chunks : 1) : grid_warps;
+  R.q = chunks / R.W;
+  R.r = chunks - R.q * R.W;
+  return R;
+}
+
+// Arrival on a counter that publishes this warp's earlier stores and, for the
+// last arrival, acquires every other arrival's (one atom.acq_rel by lane 0
+// after a warp barrier, instead of two full fences).
+__device__ __forceinline__ bool arrive_last(uint32_t *cnt, uint32_t n) {
+  __syncwarp();
+  uint32_t old = 0u;
+  if ((threadIdx.x & 31) == 0)
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+  const bool last = __shfl_sync(0xFFFFFFFFu, old, 0) == n - 1;
+  __syncwarp();
+  return last;
+}
+
+// Row pitch (bytes) of an activation stage of K f16 values per row: a
+// multiple of 64 that is 64 mod 128, so the eight lanes of one 16-byte
+// shared-memory wavefront (two rows x four quarters) hit distinct banks.
+__host__ __device__ constexpr int flat_row_pitch(int K) { return (2 * K) % 128 == 0 ? 2 * K + 64 : 2 * K; }
+
+// The E2M1 codes of one word (byte i: codes 2i, 2i + 1, low nibble first)
+// as four exact f16x2 values. OXG_E2M1_SHR 1: each byte reaches the
+// conversion by a shift of the word; 0: by unpacking the word into bytes.
+#ifndef OXG_E2M1_SHR
+#define OXG_E2M1_SHR 0
+#endif
+__device__ __forceinline__ void e2m1_word(uint32_t w, uint32_t (&o)[4]) {
+#if OXG_E2M1_SHR
+  o[0] = e2m1x2_to_f16x2(w);
+  o[1] = e2m1x2_to_f16x2(w >> 8);
+  o[2] = e2m1x2_to_f16x2(w >> 16);
+  o[3] = e2m1x2_to_f16x2(w >> 24);
+#else
+  e2m1x8_to_f16x8(w, o);
+#endif
+}
+
+// The four E8M0 scales of a word (byte b: block b) as f32 powers of two,
+// byte << 23 exactly as e8m0_to_f32 (0 -> 0.0, 255 -> +inf).
+__device__ __forceinline__ void e8m0x4(uint32_t sx, float (&s)[4]) {
+  s[0] = __uint_as_float((sx << 23) & 0x7F800000u);
+  s[1] = __uint_as_float((sx << 15) & 0x7F800000u);
+  s[2] = __uint_as_float((sx << 7) & 0x7F800000u);
+  s[3] = __uint_as_float((sx >> 1) & 0x7F800000u);
+}
+
+// The m16n8k16 A operands of one block's two k-steps from the lane's code
+// words of rows a and b (see a_operands).
+__device__ __forceinline__ void a_ops(uint32_t wa, uint32_t wb, uint32_t (&A0)[4], uint32_t (&A1)[4]) {
+  uint32_t fa[4], fb[4];
+  e2m1_word(wa, fa);
+  e2m1_word(wb, fb);
+  A0[0] = fa[0]; A0[1] = fb[0]; A0[2] = fa[1]; A0[3] = fb[1];
+  A1[0] = fa[2]; A1[1] = fb[2]; A1[2] = fa[3]; A1[3] = fb[3];
+}
+
+// One block's two k-steps against a row-major f16 activation stage: bv holds
+// the lane's row's 8 values of the block (elements 8q .. 8q + 7, the K order
+// the code words use, one 16-byte load); acc += scale * (A . B).
+__device__ __forceinline__ void mma_blk(const uint32_t (&A0)[4], const uint32_t (&A1)[4], const uint4 &bv, float s_a,
+                                        float s_b, float (&acc)[4]) {
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  float d[4];
+  mma_f16_16816(d, A0, bv.x, bv.y, zero4);
+  mma_f16_16816(d, A1, bv.z, bv.w, d);
+  acc[0] = fmaf(s_a, d[0], acc[0]);
+  acc[1] = fmaf(s_a, d[1], acc[1]);
+  acc[2] = fmaf(s_b, d[2], acc[2]);
+  acc[3] = fmaf(s_b, d[3], acc[3]);
+}
+
+// One slot of a warp's ring as the consumer reads it: the lane's 16 code
+// bytes of rows a and b (word b = block b) and the four scale bytes of each.
+struct SlotData {
+  uint4 va, vb;
+  uint32_t sxa, sxb;
+};
+
+// Shared-window helpers of the flat stream: 32-bit shared addresses with
+// immediate offsets keep the per-chunk address arithmetic to a few adds.
+__device__ __forceinline__ void cp16_s(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp4_s(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+
+// A warp's stream of chunks [c0, c1) (n_grp groups per item: `full` groups of
+// four blocks, then one narrow group of `tail` blocks when K % 128 != 0)
+// through its cp.async ring of STAGES slots, continuing across item
+// boundaries, in two phases: prefill() puts the first STAGES chunks in flight
+// (it needs only the weights), consume() runs the rest. item_ptr(i): first
+// byte of item i's tile (consecutive chunks of an item are contiguous).
+// consume(start_fn, full_fn, tail_fn, end_fn): start_fn(i) runs before the
+// warp's first group of item i (to prefetch what the item's epilogue needs),
+// full_fn(grp, slot) takes a group of four blocks, tail_fn(grp, slot) the
+// item's narrow group, end_fn(i) runs after the warp's last group of item i. Per chunk the issue side does three 16-byte
+// copies per lane, the consumer four shared loads; everything else is a few
+// counters (no division, no 64-bit index arithmetic).
+template <int STAGES, class ItemPtr>
+struct FlatStream {
+  static constexpr uint32_t kLast = (STAGES - 1) * kStageBytes;
+  int full, tail, lane;
+  // issue side: this lane's 16 bytes of the next chunk, chunks left to issue,
+  // full groups left in the issuing item, its index, the next slot's offset
+  const uint8_t *src;
+  int i_left, i_full, i_item;
+  uint32_t i_off;
+  // consume side
+  int c_left, c_full, c_grp, c_item;
+  uint32_t ring_lane, ring_g;  // shared addresses of the lane's code bytes and scale word in slot 0
+  ItemPtr item_ptr;
+
+  __device__ __forceinline__ FlatStream(int c0, int c1, int K, uint8_t *ring, ItemPtr ptr)
+      : item_ptr(ptr) {
+    lane = threadIdx.x & 31;
+    const int nb = K / 32;
+    full = nb / 4;
+    tail = nb % 4;
+    const int n_grp = full + (tail ? 1 : 0);
+    const int n = c1 > c0 ? (int)(c1 - c0) : 0;
+    const int item = n > 0 ? (int)(c0 / n_grp) : 0;
+    const int grp = n > 0 ? c0 - item * n_grp : 0;
+    i_left = c_left = n;
+    i_item = c_item = item;
+    i_full = c_full = full - grp;  // 0 when the range starts at the narrow group
+    c_grp = grp;
+    i_off = 0u;
+    src = n > 0 ? item_ptr(item) + (size_t)grp * 1088 + lane * 16 : nullptr;
+    ring_lane = smem_u32(ring) + lane * 16;
+    ring_g = smem_u32(ring) + 1024 + (lane >> 2) * 4;
+  }
+
+  __device__ __forceinline__ void next_item_issue() {
+    ++i_item;
+    src = item_ptr(i_item) + lane * 16;
+    i_full = full;
+  }
+
+  __device__ __forceinline__ void issue() {
+    if (i_left > 0) {
+      const uint32_t d = ring_lane + i_off;
+      if (i_full > 0) {
+        cp16_s(d, src);
+        cp16_s(d + 512, src + 512);
+        if (lane < 4) cp16_s(d + 1024, src + 1024);
+        src += 1088;
+        if (--i_full == 0 && tail == 0 && i_left > 1) next_item_issue();
+      } else {
+        // the narrow group is stored packed (4 * tail bytes per lane and row
+        // half, then 64 scale bytes): spread it into the full layout
+        const uint8_t *ch = src - lane * 16;
+        for (int b = 0; b < tail; ++b) {
+          cp4_s(d + b * 4, ch + lane * 4 * tail + b * 4);
+          cp4_s(d + 512 + b * 4, ch + 128 * tail + lane * 4 * tail + b * 4);
+        }
+        if (lane < 4) cp16_s(d + 1024, ch + 256 * tail + lane * 16);
+        if (i_left > 1) next_item_issue();
+      }
+      --i_left;
+    }
+    cp_async_commit();
+    i_off = i_off == kLast ? 0u : i_off + kStageBytes;
+  }
+
+  __device__ __forceinline__ void prefill() {
+#pragma unroll
+    for (int u = 0; u < STAGES; ++u) issue();
+  }
+
+  template <class StartFn, class FullFn, class TailFn, class EndFn>
+  __device__ __forceinline__ void consume(StartFn start_fn, FullFn full_fn, TailFn tail_fn, EndFn end_fn) {
+    uint32_t off = 0u;
+    if (c_left > 0) start_fn(c_item);
+#pragma unroll 1
+    for (int n = c_left; n > 0; --n) {
+      cp_async_wait<STAGES - 1>();
+      __syncwarp();  // the scale bytes were copied by lanes 0-3
+      SlotData d;
+      d.va = lds128(ring_lane + off);
+      d.vb = lds128(ring_lane + off + 512);
+      d.sxa = lds32(ring_g + off);
+      d.sxb = lds32(ring_g + off + 32);
+      issue();  // the warp read the slot above (converged) before any lane refills it
+      bool ends;
+      if (c_full > 0) {
+        full_fn(c_grp, d);
+        ends = (--c_full == 0 && tail == 0) || n == 1;
+        ++c_grp;
+      } else {
+        tail_fn(c_grp, d);
+        ends = true;
+      }
+      if (ends) {
+        end_fn(c_item);
+        ++c_item;
+        c_grp = 0;
+        c_full = full;
+        if (n > 1) start_fn(c_item);
+      }
+      off = off == kLast ? 0u : off + kStageBytes;
+    }
+    cp_async_wait<0>();
+  }
+};
+
+// A warp's parts of the (at most two) items its range shares with other
+// warps: slot 0 the item that began before the range, slot 1 the one that
+// ends after it. They stay in registers while the weights stream and are
+// settled once the warp's ring is empty (settle()): a memory fence inside the
+// streaming loop would stall the warp until its copies in flight landed.
+template <int NCG>
+struct SplitParts {
+  float4 v[2][NCG];  // indexed with compile-time slots only (registers)
+  float2 bias[2];    // the item's epilogue values the warp prefetched
+  int item[2];
+  bool has[2];
+  __device__ __forceinline__ SplitParts() { has[0] = has[1] = false; }
+
+  // True when item [ia, ib) lies wholly in the warp's range [c0, c1) (write
+  // it now); otherwise keeps the warp's part (and the item's prefetched
+  // epilogue values) and returns false.
+  __device__ __forceinline__ bool take(int c0, int c1, int ia, int ib, int it,
+                                       const float4 (&p)[NCG], float2 b) {
+    if (ia >= c0 && ib <= c1) return true;
+    if (ia < c0) {
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg) v[0][cg] = p[cg];
+      bias[0] = b;
+      item[0] = it;
+      has[0] = true;
+    } else {
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg) v[1][cg] = p[cg];
+      bias[1] = b;
+      item[1] = it;
+      has[1] = true;
+    }
+    return false;
+  }
+
+  // Publishes the parts, then for each: the last warp to arrive adds every
+  // part of the item in range order (the same order every run, whichever warp
+  // is last) and calls finish(item, sum, epilogue values). Parts live in the warp's two slots
+  // of `parts`, arrival counters in cnt[slot_base + first owner] (left at zero).
+  template <class Finish>
+  __device__ __forceinline__ void settle(const FlatRange &R, int w, int n_grp, float4 *parts, uint32_t *cnt,
+                                         int slot_base, Finish finish) {
+    const int lane = threadIdx.x & 31;
+    if (!has[0] && !has[1]) return;
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+      if (has[s])
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) parts[((slot_base + w) * 2 + s) * NCG * 32 + cg * 32 + lane] = v[s][cg];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (!has[s]) continue;
+      const int ia = item[s] * n_grp, ib = ia + n_grp;
+      const int wf = R.owner(ia), wl = R.owner(ib - 1);
+      if (!arrive_last(&cnt[slot_base + wf], (uint32_t)(wl - wf + 1))) continue;
+      if (lane == 0) cnt[slot_base + wf] = 0u;  // zero again for the next launch
+      float4 t[NCG];
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg) t[cg] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int wp = wf; wp <= wl; ++wp) {
+        const int sp = ia < R.first(wp) ? 0 : 1;
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) {
+          const float4 u = wp == w ? v[s][cg] : __ldcg(&parts[((slot_base + wp) * 2 + sp) * NCG * 32 + cg * 32 + lane]);
+          t[cg].x += u.x;
+          t[cg].y += u.y;
+          t[cg].z += u.z;
+          t[cg].w += u.w;
+        }
+      }
+      finish(item[s], t, bias[s]);
+    }
+  }
+};
+
+// mlp1 + bias + clamped SwiGLU over all tokens (T <= 8), flat split over the
+// whole grid: x is staged once per CTA (row-major f16 x * 2^-sigma, 8 rows,
+// rows >= T zero) and every tile computes all 8 token columns; the epilogue
+// keeps the columns of the tokens routed to the tile's expert. The weight
+// ring is filled before the activations are staged, so the first weight
+// bytes are in flight while x is converted.
+template <int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1) mlp1_flat_kernel(const DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float tok_scale[8];
+  __shared__ int act_s[kMaxAllTokActive];
+  __shared__ int act_of[256];
+  __shared__ int col_pos[kMaxAllTokActive * 8];  // position of (active expert, token), or -1
+
+  if (a.pdl) pdl_wait();
+  const int K = a.K, XS = flat_row_pitch(K);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int T = a.T, k = a.topk;
+  const int n_act = *a.n_active;
+  const int n_tiles = a.rows / 16;
+  const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0), fs_tail = nb % 4;
+
+  for (int i = tid; i < n_act; i += kThreads) {
+    act_s[i] = a.active[i];
+    act_of[a.active[i]] = i;
+  }
+  for (int i = tid; i < n_act * 8; i += kThreads) col_pos[i] = -1;
+  __syncthreads();
+
+  const FlatRange R = flat_range(n_act * n_tiles * n_grp, (int)gridDim.x * WARPS);
+  const int w = (int)blockIdx.x * WARPS + warp;
+  const int c0 = R.lo(w), c1 = R.lo(w + 1);
+  uint8_t *ring = smem + 8 * XS + warp * (STAGES * kStageBytes);
+  auto item_ptr = [&](int i) {
+    const int ai = i / n_tiles, tile = i - ai * n_tiles;
+    return a.codes + ((size_t)act_s[ai] * n_tiles + tile) * a.item_bytes;
+  };
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint8_t *brow = smem + g * XS + q * 16;
+  // one block of the group: its A operands, the activation load, the MMAs
+  auto block = [&](const uint8_t *bp, uint32_t wa, uint32_t wb, float s_a, float s_b) {
+    uint32_t A0[4], A1[4];
+    a_ops(wa, wb, A0, A1);
+    mma_blk(A0, A1, *reinterpret_cast<const uint4 *>(bp), s_a, s_b, acc);
+  };
+  auto full_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    block(bp, d.va.x, d.vb.x, sa[0], sb[0]);
+    block(bp + 64, d.va.y, d.vb.y, sa[1], sb[1]);
+    block(bp + 128, d.va.z, d.vb.z, sa[2], sb[2]);
+    block(bp + 192, d.va.w, d.vb.w, sa[3], sb[3]);
+  };
+  auto tail_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    const uint32_t wa[4] = {d.va.x, d.va.y, d.va.z, d.va.w}, wb[4] = {d.vb.x, d.vb.y, d.vb.z, d.vb.w};
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      if (b < fs_tail) block(bp + 64 * b, wa[b], wb[b], sa[b], sb[b]);
+  };
+  // bias + clamped SwiGLU of one finished tile, for the tokens routed to its expert
+  auto write_tile = [&](int item, const float4 (&v)[1], float2 bias) {
+    const int ai = item / n_tiles, tile = item - ai * n_tiles;
+    const int pr = tile * 8 + g;  // intermediate unit (gate row 2pr, up row 2pr + 1)
+    const float gate[2] = {v[0].x, v[0].y}, up[2] = {v[0].z, v[0].w};
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int t = 2 * q + c;
+      const int p = col_pos[ai * 8 + t];
+      if (p >= 0)
+        a.out[(size_t)p * a.out_ld + pr] = swiglu_clamped(fmaf(gate[c], tok_scale[t], bias.x),
+                                                          fmaf(up[c], tok_scale[t], bias.y), a.alpha, a.limit);
+    }
+  };
+  // the gate / up biases of the lane's unit, loaded when the warp starts an
+  // item so their latency hides behind the item's weight stream
+  float2 cur_bias = make_float2(0.f, 0.f);
+  auto start_fn = [&](int item) {
+    const int ai = item / n_tiles, tile = item - ai * n_tiles;
+    const uint16_t *bp = a.bias + (size_t)act_s[ai] * a.rows + 2 * (tile * 8 + g);
+    cur_bias = make_float2(bf16_to_f32(bp[0]), bf16_to_f32(bp[1]));
+  };
+  SplitParts<1> split;
+  auto end_fn = [&](int item) {
+    const float4 v[1] = {make_float4(acc[0], acc[1], acc[2], acc[3])};
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    const int ia = item * n_grp;
+    if (split.take(c0, c1, ia, ia + n_grp, item, v, cur_bias)) write_tile(item, v, cur_bias);
+  };
+
+  // the weight stream does not depend on x: put it in flight first
+  FlatStream<STAGES, decltype(item_ptr)> fs(c0, c1, K, ring, item_ptr);
+  fs.prefill();
+
+  // the per-(active expert, token) output positions (two dependent loads:
+  // started first so that their latency overlaps the staging)
+  for (int p = tid; p < T * k; p += kThreads) {
+    const int s = a.perm[p];
+    col_pos[act_of[a.idx[s]] * 8 + s / k] = p;
+  }
+  if (tid < 8) tok_scale[tid] = tid < T ? __uint_as_float((uint32_t)(127 + a.sigma[tid]) << 23) : 1.f;
+  // stage x (row-major f16 x * 2^-sigma; conflict-free 16-byte stores), the
+  // loads of kU units per thread issued together
+  constexpr int kU = 4;
+  const int units = 8 * (K / 8);
+  for (int u0 = tid; u0 < units; u0 += kU * kThreads) {
+    uint4 v[kU];
+    float inv[kU];
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, tok = u / (K / 8), c8 = u - tok * (K / 8);
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      inv[j] = 0.f;
+      if (u < units && tok < T) {
+        v[j] = *reinterpret_cast<const uint4 *>(a.x + (size_t)tok * K + c8 * 8);
+        inv[j] = __uint_as_float((uint32_t)(127 - a.sigma[tok]) << 23);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, tok = u / (K / 8), c8 = u - tok * (K / 8);
+      if (u < units) {
+        uint4 o;
+        o.x = pack_f16x2(bf16_to_f32(v[j].x & 0xFFFFu) * inv[j], bf16_to_f32(v[j].x >> 16) * inv[j]);
+        o.y = pack_f16x2(bf16_to_f32(v[j].y & 0xFFFFu) * inv[j], bf16_to_f32(v[j].y >> 16) * inv[j]);
+        o.z = pack_f16x2(bf16_to_f32(v[j].z & 0xFFFFu) * inv[j], bf16_to_f32(v[j].z >> 16) * inv[j]);
+        o.w = pack_f16x2(bf16_to_f32(v[j].w & 0xFFFFu) * inv[j], bf16_to_f32(v[j].w >> 16) * inv[j]);
+        *reinterpret_cast<uint4 *>(smem + tok * XS + c8 * 16) = o;
+      }
+    }
+  }
+  __syncthreads();
+  if (a.pdl) pdl_launch();
+  fs.consume(start_fn, full_fn, tail_fn, end_fn);
+  split.settle(R, w, n_grp, a.parts, a.flat_cnt, 0, write_tile);
+}
+
+// mlp1 + bias + clamped SwiGLU over the virtual experts (groups of at most 8
+// consecutive slots of one expert): the grid's CTAs are dealt to the groups in
+// equal numbers, each CTA stages its group's x rows (gathered through perm,
+// f16 x * 2^-sigma, row j = slot pos0 + j, rows beyond n_e zero) and the
+// group's warps split the expert's weight chunks flat; the epilogue writes
+// h[pos] for the group's slots. Used above 8 tokens, where one expert can hold
+// many of the batch's tokens.
+template <int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1) mlp1_group_kernel(const DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float tok_scale[8];
+
+  if (a.pdl) pdl_wait();
+  const int K = a.K, XS = flat_row_pitch(K);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int n_v = *a.n_virtual;
+  const int per = (int)gridDim.x / max(n_v, 1);
+  const int ai = per > 0 ? (int)blockIdx.x / per : n_v;
+  if (ai >= n_v) return;
+  const int band = (int)blockIdx.x - ai * per;
+  const int e = a.v_expert[ai];
+  const int n_e = a.v_count[ai], pos0 = a.v_pos0[ai];
+  const int n_tiles = a.rows / 16;
+  const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0), fs_tail = nb % 4;
+
+  const FlatRange R = flat_range(n_tiles * n_grp, per * WARPS);
+  const int w = band * WARPS + warp;
+  const int c0 = R.lo(w), c1 = R.lo(w + 1);
+  const int slot_base = ai * per * WARPS;  // the group's first warp in the grid
+  uint8_t *ring = smem + 8 * XS + warp * (STAGES * kStageBytes);
+  auto item_ptr = [&](int tile) { return a.codes + ((size_t)e * n_tiles + tile) * a.item_bytes; };
+  FlatStream<STAGES, decltype(item_ptr)> fs(c0, c1, K, ring, item_ptr);
+  fs.prefill();
+
+  // stage the group's x rows (the loads of kU units per thread issued together)
+  if (tid < 8)
+    tok_scale[tid] =
+        tid < n_e ? __uint_as_float((uint32_t)(127 + a.sigma[a.perm[pos0 + tid] / a.topk]) << 23) : 1.f;
+  constexpr int kU = 4;
+  const int units = 8 * (K / 8);
+  for (int u0 = tid; u0 < units; u0 += kU * kThreads) {
+    uint4 v[kU];
+    float inv[kU];
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, row = u / (K / 8), c8 = u - row * (K / 8);
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      inv[j] = 0.f;
+      if (u < units && row < n_e) {
+        const int t = a.perm[pos0 + row] / a.topk;
+        v[j] = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + c8 * 8);
+        inv[j] = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, row = u / (K / 8), c8 = u - row * (K / 8);
+      if (u < units) {
+        uint4 o;
+        o.x = pack_f16x2(bf16_to_f32(v[j].x & 0xFFFFu) * inv[j], bf16_to_f32(v[j].x >> 16) * inv[j]);
+        o.y = pack_f16x2(bf16_to_f32(v[j].y & 0xFFFFu) * inv[j], bf16_to_f32(v[j].y >> 16) * inv[j]);
+        o.z = pack_f16x2(bf16_to_f32(v[j].z & 0xFFFFu) * inv[j], bf16_to_f32(v[j].z >> 16) * inv[j]);
+        o.w = pack_f16x2(bf16_to_f32(v[j].w & 0xFFFFu) * inv[j], bf16_to_f32(v[j].w >> 16) * inv[j]);
+        *reinterpret_cast<uint4 *>(smem + row * XS + c8 * 16) = o;
+      }
+    }
+  }
+  __syncthreads();
+  if (a.pdl) pdl_launch();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint8_t *brow = smem + g * XS + q * 16;
+  auto block = [&](const uint8_t *bp, uint32_t wa, uint32_t wb, float s_a, float s_b) {
+    uint32_t A0[4], A1[4];
+    a_ops(wa, wb, A0, A1);
+    mma_blk(A0, A1, *reinterpret_cast<const uint4 *>(bp), s_a, s_b, acc);
+  };
+  auto full_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    block(bp, d.va.x, d.vb.x, sa[0], sb[0]);
+    block(bp + 64, d.va.y, d.vb.y, sa[1], sb[1]);
+    block(bp + 128, d.va.z, d.vb.z, sa[2], sb[2]);
+    block(bp + 192, d.va.w, d.vb.w, sa[3], sb[3]);
+  };
+  auto tail_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    const uint32_t wa[4] = {d.va.x, d.va.y, d.va.z, d.va.w}, wb[4] = {d.vb.x, d.vb.y, d.vb.z, d.vb.w};
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      if (b < fs_tail) block(bp + 64 * b, wa[b], wb[b], sa[b], sb[b]);
+  };
+  // bias + clamped SwiGLU of a finished tile for the group's slots (columns 2q, 2q + 1)
+  auto write_tile = [&](int tile, const float4 (&v)[1], float2 bias) {
+    const int pr = tile * 8 + g;  // intermediate unit (gate row 2pr, up row 2pr + 1)
+    const float gate[2] = {v[0].x, v[0].y}, up[2] = {v[0].z, v[0].w};
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int j = 2 * q + c;
+      if (j < n_e)
+        a.out[(size_t)(pos0 + j) * a.out_ld + pr] = swiglu_clamped(fmaf(gate[c], tok_scale[j], bias.x),
+                                                                   fmaf(up[c], tok_scale[j], bias.y), a.alpha,
+                                                                   a.limit);
+    }
+  };
+  float2 cur_bias = make_float2(0.f, 0.f);
+  auto start_fn = [&](int tile) {
+    const uint16_t *bp = a.bias + (size_t)e * a.rows + 2 * (tile * 8 + g);
+    cur_bias = make_float2(bf16_to_f32(bp[0]), bf16_to_f32(bp[1]));
+  };
+  SplitParts<1> split;
+  auto end_fn = [&](int tile) {
+    const float4 v[1] = {make_float4(acc[0], acc[1], acc[2], acc[3])};
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    const int ia = tile * n_grp;
+    if (split.take(c0, c1, ia, ia + n_grp, tile, v, cur_bias)) write_tile(tile, v, cur_bias);
+  };
+  fs.consume(start_fn, full_fn, tail_fn, end_fn);
+  split.settle(R, w, n_grp, a.parts, a.flat_cnt, slot_base, write_tile);
+}
+
+// mlp2 + bias over the virtual experts (groups of at most 8 consecutive
+// slots of one expert, from the routing kernel), with the weighted top-k
+// combine fused. The grid's CTAs are dealt to the virtual experts in equal
+// groups of gridDim.x / n_virtual (the remainder idles), so an expert with
+// many tokens gets one CTA group per 8 of them instead of looping over its
+// tokens in one place; inside a group the expert's weight chunks are split
+// flat over the group's warps. The group's n_e <= 4 * NCG slots are staged
+// once per CTA as f16 hi / lo rows of the SwiGLU output (row 2t: hi, 2t + 1:
+// lo, rows beyond 2 n_e zero), so an MMA column group of 8 holds the hi and lo
+// halves of four slots and y = hi part + lo part keeps ~22 bits of h.
+// Combine: when the last virtual expert finishes a 16-row tile, that warp
+// writes y[t, rows] = sum_j wts[t, j] * y_slot[slot_pos[t, j], rows] in j
+// order (the same expression as combine_kernel), so the result does not
+// depend on which group finishes last.
+template <int WARPS, int STAGES, int NCG>
+__global__ void __launch_bounds__(WARPS * 32, 1) mlp2_flat_kernel(const DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32;
+  extern __shared__ __align__(16) uint8_t smem[];
+
+  if (a.pdl) pdl_wait();
+  const int K = a.K, XS = flat_row_pitch(K);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int n_act = *a.n_virtual;  // groups that finish every tile (the combine's count)
+  const int per = (int)gridDim.x / max(n_act, 1);
+  const int ai = per > 0 ? (int)blockIdx.x / per : n_act;
+  if (ai >= n_act) return;
+  const int band = (int)blockIdx.x - ai * per;
+  const int e = a.v_expert[ai];
+  const int n_e = a.v_count[ai], pos0 = a.v_pos0[ai];
+  const int ngc = (2 * n_e + 7) / 8;  // column groups in use (<= NCG)
+  const int n_tiles = a.rows / 16;
+  const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0);
+
+  const FlatRange R = flat_range(n_tiles * n_grp, per * WARPS);
+  const int w = band * WARPS + warp;
+  const int c0 = R.lo(w), c1 = R.lo(w + 1);
+  const int slot_base = ai * per * WARPS;  // the group's first warp in the grid
+  uint8_t *ring = smem + 8 * NCG * XS + warp * (STAGES * kStageBytes);
+  auto item_ptr = [&](int tile) { return a.codes + ((size_t)e * n_tiles + tile) * a.item_bytes; };
+  FlatStream<STAGES, decltype(item_ptr)> fs(c0, c1, K, ring, item_ptr);
+  fs.prefill();
+
+  // stage the expert's h rows as f16 hi / lo (conflict-free 16-byte stores),
+  // the loads of kU units per thread issued together
+  constexpr int kU = 4;
+  const int units = 4 * NCG * (K / 8);
+  for (int u0 = tid; u0 < units; u0 += kU * kThreads) {
+    float4 v[kU][2];
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, tok = u / (K / 8), c8 = u - tok * (K / 8);
+      v[j][0] = v[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (u < units && tok < n_e) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.h + (size_t)(pos0 + tok) * K + c8 * 8);
+        v[j][0] = src[0];
+        v[j][1] = src[1];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = u0 + j * kThreads, tok = u / (K / 8), c8 = u - tok * (K / 8);
+      if (u >= units) continue;
+      const float f[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w, v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        hw[i] = pack_f16x2(f[2 * i], f[2 * i + 1]);
+        const float2 r = unpack_f16x2(hw[i]);
+        lw[i] = pack_f16x2(f[2 * i] - r.x, f[2 * i + 1] - r.y);
+      }
+      *reinterpret_cast<uint4 *>(smem + (2 * tok) * XS + c8 * 16) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4 *>(smem + (2 * tok + 1) * XS + c8 * 16) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  }
+  __syncthreads();
+  if (a.pdl) pdl_launch();
+
+  float acc[NCG][4];
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = acc[cg][2] = acc[cg][3] = 0.f;
+  const uint8_t *brow = smem + g * XS + q * 16;
+  const int fs_tail = nb % 4;
+  // one block: its A operands once, then the MMAs of each column group in use
+  auto block = [&](const uint8_t *bp, uint32_t wa, uint32_t wb, float s_a, float s_b) {
+    uint32_t A0[4], A1[4];
+    a_ops(wa, wb, A0, A1);
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg)
+      if (cg < ngc) mma_blk(A0, A1, *reinterpret_cast<const uint4 *>(bp + cg * 8 * XS), s_a, s_b, acc[cg]);
+  };
+  auto full_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    block(bp, d.va.x, d.vb.x, sa[0], sb[0]);
+    block(bp + 64, d.va.y, d.vb.y, sa[1], sb[1]);
+    block(bp + 128, d.va.z, d.vb.z, sa[2], sb[2]);
+    block(bp + 192, d.va.w, d.vb.w, sa[3], sb[3]);
+  };
+  auto tail_fn = [&](int grp, const SlotData &d) {
+    float sa[4], sb[4];
+    e8m0x4(d.sxa, sa);
+    e8m0x4(d.sxb, sb);
+    const uint8_t *bp = brow + grp * 256;
+    const uint32_t wa[4] = {d.va.x, d.va.y, d.va.z, d.va.w}, wb[4] = {d.vb.x, d.vb.y, d.vb.z, d.vb.w};
+#pragma unroll
+    for (int b = 0; b < 3; ++b)
+      if (b < fs_tail) block(bp + 64 * b, wa[b], wb[b], sa[b], sb[b]);
+  };
+  // bias + store of one finished tile's rows for the expert's tokens
+  auto write_tile = [&](int tile, const float4 (&v)[NCG], float2 bias) {
+    const int ra = tile * 16 + g, rb = ra + 8;  // rows g and g + 8 of the tile
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+      const int tok = cg * 4 + q;  // columns 2q (hi) and 2q + 1 (lo) of the group
+      if (cg < ngc && tok < n_e) {
+        const size_t pos = (size_t)(pos0 + tok);
+        a.out[pos * a.out_ld + ra] = (v[cg].x + v[cg].y) + bias.x;
+        a.out[pos * a.out_ld + rb] = (v[cg].z + v[cg].w) + bias.y;
+      }
+    }
+  };
+  // the biases of the lane's two rows, loaded when the warp starts a tile
+  float2 cur_bias = make_float2(0.f, 0.f);
+  auto start_fn = [&](int tile) {
+    const uint16_t *bp = a.bias + (size_t)e * a.rows + tile * 16 + g;
+    cur_bias = make_float2(bf16_to_f32(bp[0]), bf16_to_f32(bp[8]));
+  };
+  // a tile's rows are in y_slot (fenced): the last active expert to get there
+  // writes y[t, rows] = sum_j wts[t, j] * y_slot[slot_pos[t, j], rows]
+  auto combine_tile = [&](int tile) {
+    if (!arrive_last(&a.band_done[tile], (uint32_t)n_act)) return;
+    if (lane == 0) a.band_done[tile] = 0u;  // zero again for the next launch
+    const int k = a.topk;
+    for (int i = lane; i < a.T * 4; i += 32) {
+      const int t = i >> 2, r = tile * 16 + 4 * (i & 3);
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < k; ++j) {
+        const int p = __ldcg(a.slot_pos + t * k + j);
+        if (p < 0) continue;
+        const float wj = __ldcg(a.wts + t * k + j);
+        const float4 y4 = __ldcg(reinterpret_cast<const float4 *>(a.out + (size_t)p * a.out_ld + r));
+        s.x = fmaf(wj, y4.x, s.x);
+        s.y = fmaf(wj, y4.y, s.y);
+        s.z = fmaf(wj, y4.z, s.z);
+        s.w = fmaf(wj, y4.w, s.w);
+      }
+      *reinterpret_cast<float4 *>(a.y + (size_t)t * a.out_ld + r) = s;
+    }
+  };
+  SplitParts<NCG> split;
+  auto end_fn = [&](int tile) {
+    float4 v[NCG];
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+      v[cg] = make_float4(acc[cg][0], acc[cg][1], acc[cg][2], acc[cg][3]);
+      acc[cg][0] = acc[cg][1] = acc[cg][2] = acc[cg][3] = 0.f;
+    }
+    const int ia = tile * n_grp;
+    if (split.take(c0, c1, ia, ia + n_grp, tile, v, cur_bias)) write_tile(tile, v, cur_bias);
+  };
+  fs.consume(start_fn, full_fn, tail_fn, end_fn);
+
+  // the ring is empty: publish the whole tiles, then settle the split ones
+  if (c1 > c0) {
+    const int t_lo = (int)((c0 + n_grp - 1) / n_grp), t_hi = (int)(c1 / n_grp);  // tiles wholly in range
+    if (a.band_done)
+      for (int t = t_lo; t < t_hi; ++t) combine_tile(t);
+    split.settle(R, w, n_grp, a.parts, a.flat_cnt, slot_base, [&](int tile, const float4 (&v)[NCG], float2 bias) {
+      write_tile(tile, v, bias);
+      if (a.band_done) combine_tile(tile);
+    });
+  }
+}
 
 // One band of one expert's tiles x its n_e tokens.
 //   MODE 1: mlp1 + bias + clamped SwiGLU -> a.out = h
@@ -867,14 +1668,34 @@ cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
   a.T = T;
   a.idx = idx;
   a.err = s.err;
+  a.parts = s.parts;
+  a.flat_cnt = s.flat_cnt;
+  a.v_expert = s.v_expert;
+  a.v_pos0 = s.v_pos0;
+  a.v_count = s.v_count;
+  a.n_virtual = s.n_virtual;
+  const size_t flat_smem = (size_t)8 * flat_row_pitch(a.K) + (size_t)kWf1 * kSf1 * kStageBytes;
+  const bool flat_ok = kUseFlat && s.parts && s.flat_cnt && s.n_sms * kWf1 <= kFlatMaxWarps &&
+                       flat_smem <= kMaxFlatSmem;
   if (T <= 8 && T * w.k <= kMaxAllTokActive && w.E <= 256) {
     if (T <= kDeepTokens) {
       const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1d * kS1d * kStageBytes;
       return launch_ex(mlp1_alltok_kernel<kW1d, kS1d, kK1d>, dim3(s.n_sms), kW1d * 32, smem, a.pdl, stream, a);
     }
+    // The all-token kernel gives each warp whole tiles: measured fastest when
+    // the expected tiles fill its warps evenly (at 8 tokens, ~22 experts x
+    // 360 tiles over 148 x 28 warps: 1.9 rounds), slower than the flat split
+    // when the last round is half empty (4 tokens: ~14 experts, 1.2 rounds).
+    const double rounds = (double)s.exp_active * (a.rows / 16) / ((double)s.n_sms * kW1);
+    if (flat_ok && rounds / std::ceil(rounds) < 0.8)
+      return launch_ex(mlp1_flat_kernel<kWf1, kSf1>, dim3(s.n_sms), kWf1 * 32, flat_smem, a.pdl, stream, a);
     const size_t smem = (size_t)(a.K / 32) * 2 * 32 * 8 + (size_t)kW1 * kS1 * kStageBytes;
     return launch_ex(mlp1_alltok_kernel<kW1, kS1>, dim3(s.n_sms), kW1 * 32, smem, a.pdl, stream, a);
   }
+  // above 8 tokens: equal CTA groups per virtual expert (at most 8 of an
+  // expert's slots each), so a hot expert's tokens spread over the GPU
+  if (flat_ok && s.v_expert && s.max_virtual <= s.n_sms)
+    return launch_ex(mlp1_group_kernel<kWf1, kSf1>, dim3(s.n_sms), kWf1 * 32, flat_smem, a.pdl, stream, a);
   a.bands = s.bands1;
   return launch_decode<1, 1>(a, s.max_active, stream);
 }
@@ -896,6 +1717,19 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
   a.slot_pos = slot_pos;
   a.wts = wts;
   a.y = y;
+  a.parts = s.parts;
+  a.flat_cnt = s.flat_cnt;
+  a.v_expert = s.v_expert;
+  a.v_pos0 = s.v_pos0;
+  a.v_count = s.v_count;
+  a.n_virtual = s.n_virtual;
+  if (T > 8 && kUseFlat && s.parts && s.flat_cnt && s.v_expert && s.max_virtual <= s.n_sms) {
+    // equal CTA groups per virtual expert (at most 8 slots: two column groups
+    // of four slots' hi / lo halves), flat split inside each group
+    const size_t smem = (size_t)16 * flat_row_pitch(a.K) + (size_t)kWf2b * kSf2b * kStageBytes;
+    if (s.n_sms * kWf2b <= kFlatMaxWarps && smem <= kMaxFlatSmem)
+      return launch_ex(mlp2_flat_kernel<kWf2b, kSf2b, 2>, dim3(s.n_sms), kWf2b * 32, smem, a.pdl, stream, a);
+  }
   if (T <= 8 && s.max_active <= s.n_sms) {
     // persistent grid, bands per expert from the device's active count
     a.dyn_bands = 1;

@@ -58,12 +58,14 @@ constexpr int kMaxBands = 1024;
 // 256-column tiles run half empty, while fewer chunks leave longer copies
 // that cannot overlap.
 constexpr int kHostChunkTokens = 1600;
-constexpr size_t kCounterBytes = (2 + kMaxBands) * sizeof(uint32_t);  // done, err, bands
+// done, err, per-band counters, the flat-split decode kernels' counters
+constexpr size_t kCounterBytes = (2 + kMaxBands + oxg::kFlatMaxWarps) * sizeof(uint32_t);
 
 struct Scratch {
   void *base = nullptr;
   size_t bytes = 0;
-  uint32_t *done = nullptr, *band_done = nullptr;
+  uint32_t *done = nullptr, *band_done = nullptr, *flat_cnt = nullptr;
+  float4 *parts = nullptr;  // flat-split decode partial sums
   int *err = nullptr;  // prefill pipeline timeout code
   uint16_t *xp = nullptr, *h_hi = nullptr, *h_lo = nullptr;
   float *pos_scale = nullptr;
@@ -71,6 +73,7 @@ struct Scratch {
   int32_t *idx = nullptr, *sigma = nullptr, *counts = nullptr, *offsets = nullptr;
   int32_t *perm = nullptr, *slot_pos = nullptr;
   int32_t *cta_hist = nullptr, *local_rank = nullptr;  // batched router's counting-sort halves
+  int32_t *v_expert = nullptr, *v_pos0 = nullptr, *v_count = nullptr, *n_virtual = nullptr;  // virtual experts
   float *wts = nullptr, *logits = nullptr, *h = nullptr, *y_slot = nullptr;
   uint16_t *x_stage = nullptr;
   float *y_stage = nullptr;
@@ -262,7 +265,7 @@ int check_dims(oxg_ctx *ctx, const oxg_moe_dims *d) {
 }
 
 // Scratch layout for T tokens of a layer with dims d.
-size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
+size_t scratch_bytes(const oxg_moe_dims &d, int T, int n_sms, Scratch *s, char *base) {
   const size_t S = (size_t)T * d.top_k;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -271,6 +274,7 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
     return base ? base + o : nullptr;
   };
   char *p_cnt = take(kCounterBytes);
+  char *p_parts = take(oxg::flat_parts_bytes(n_sms));
   char *p_active = take((size_t)d.n_experts * 4), *p_nactive = take(4);
   char *p_idx = take(S * 4), *p_wts = take(S * 4), *p_sigma = take((size_t)T * 4);
   char *p_logits = take((size_t)T * d.n_experts * 4);
@@ -284,6 +288,8 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
   char *p_xp = take(S * d.hidden * 2), *p_hhi = take(S * d.intermediate * 2);
   char *p_hlo = take(S * d.intermediate * 2), *p_psc = take(S * 4);
   char *p_hist = take((size_t)oxg::router_mma_ctas(T) * d.n_experts * 4), *p_rank = take(S * 4);
+  const size_t n_virt = (size_t)oxg::max_virtual(d.n_experts, T, d.top_k) + 1;
+  char *p_vexp = take(n_virt * 4), *p_vpos = take(n_virt * 4), *p_vcnt = take(n_virt * 4), *p_nvirt = take(4);
   const size_t xq_b = (size_t)2 * T * d.hidden, xsf_b = (size_t)(d.hidden + 127) / 128 * 512;
   const size_t hq_b = 4 * S * d.intermediate;
   const size_t hsf_b = (size_t)d.n_experts * ((d.intermediate + 127) / 128) * 512;
@@ -310,6 +316,8 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
     s->done = (uint32_t *)p_cnt;
     s->err = (int *)(s->done + 1);
     s->band_done = s->done + 2;
+    s->flat_cnt = s->band_done + kMaxBands;
+    s->parts = (float4 *)p_parts;
     s->xp = (uint16_t *)p_xp;
     s->h_hi = (uint16_t *)p_hhi;
     s->h_lo = (uint16_t *)p_hlo;
@@ -326,6 +334,10 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
     s->slot_pos = (int32_t *)p_slot;
     s->cta_hist = (int32_t *)p_hist;
     s->local_rank = (int32_t *)p_rank;
+    s->v_expert = (int32_t *)p_vexp;
+    s->v_pos0 = (int32_t *)p_vpos;
+    s->v_count = (int32_t *)p_vcnt;
+    s->n_virtual = (int32_t *)p_nvirt;
     s->h = (float *)p_h;
     s->y_slot = (float *)p_y;
     s->x_stage = (uint16_t *)p_xs;
@@ -336,7 +348,7 @@ size_t scratch_bytes(const oxg_moe_dims &d, int T, Scratch *s, char *base) {
 
 int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
   const int Tc = T < 1 ? 1 : T;
-  const size_t need = scratch_bytes(d, Tc, nullptr, nullptr);
+  const size_t need = scratch_bytes(d, Tc, ctx->n_sms, nullptr, nullptr);
   const size_t key = ((size_t)Tc * 1000003u + (size_t)d.hidden) * 1000003u +
                      ((size_t)d.intermediate * 4099u + (size_t)d.n_experts * 17u + (size_t)d.top_k);
   auto zero_terms = [&]() -> int {
@@ -349,7 +361,7 @@ int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
     return OXG_OK;
   };
   if (need <= ctx->ws.bytes) {
-    scratch_bytes(d, Tc, &ctx->ws, (char *)ctx->ws.base);
+    scratch_bytes(d, Tc, ctx->n_sms, &ctx->ws, (char *)ctx->ws.base);
     return zero_terms();
   }
   if (ctx->ws.base) {
@@ -362,7 +374,7 @@ int ensure_scratch(oxg_ctx *ctx, const oxg_moe_dims &d, int T) {
   OXG_CUDA(ctx, cudaMalloc(&p, need), "cudaMalloc(scratch)");
   ctx->ws.base = p;
   ctx->ws.bytes = need;
-  scratch_bytes(d, Tc, &ctx->ws, (char *)p);
+  scratch_bytes(d, Tc, ctx->n_sms, &ctx->ws, (char *)p);
   OXG_CUDA(ctx, cudaMemsetAsync(p, 0, kCounterBytes, ctx->stream), "cudaMemsetAsync(counters)");
   return zero_terms();
 }
@@ -516,11 +528,19 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
   sched.n_sms = ctx->n_sms;
   sched.pdl = true;
   sched.err = ctx->ws.err;
+  sched.parts = ctx->ws.parts;
+  sched.flat_cnt = ctx->ws.flat_cnt;
+  sched.exp_active = exp_active;
+  sched.v_expert = ctx->ws.v_expert;
+  sched.v_pos0 = ctx->ws.v_pos0;
+  sched.v_count = ctx->ws.v_count;
+  sched.n_virtual = ctx->ws.n_virtual;
+  sched.max_virtual = oxg::max_virtual(d.n_experts, T, d.top_k);
   // counters the mlp2 kernel's fused combine uses (zeroed by route_small):
-  // per 128-row band quarter (block-scaled), per band (f16; at most 8 tokens
-  // the bands are chosen on the device, at most one per 16-row tile and SM)
+  // per 128-row band quarter (block-scaled), per band (f16 per-expert bands),
+  // per 16-row tile (f16 flat split at most 8 tokens)
   const int n_bands = mxf ? 4 * ((d.hidden + 127) / 128)
-                          : std::max(sched.bands2, std::min(d.hidden / 16, ctx->n_sms));
+                          : std::max(sched.bands2, d.hidden / 16);
   if (n_bands > kMaxBands) return fail(ctx, OXG_ERR_UNSUPPORTED, "too many row bands (%d)", n_bands);
   oxg::RouteSmallArgs ra{};
   ra.x = x;
@@ -543,6 +563,10 @@ int forward_small(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, bo
   ra.done = ctx->ws.done;
   ra.band_done = ctx->ws.band_done;
   ra.n_bands = n_bands;
+  ra.v_expert = ctx->ws.v_expert;
+  ra.v_pos0 = ctx->ws.v_pos0;
+  ra.v_count = ctx->ws.v_count;
+  ra.n_virtual = ctx->ws.n_virtual;
   if (mxf) {
     ra.xq = ctx->ws.xq;
     ra.xsf = ctx->ws.xsf;

@@ -208,6 +208,17 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) route_small_kernel(RouteSma
     off_s[E] = run;
     a.offsets[E] = run;
     a.n_active[0] = n_active;
+    if (a.v_expert) {  // the active experts in groups of at most kVirtualTokens slots
+      int nv = 0;
+      for (int x = 0; x < E; ++x)
+        for (int j = 0; j < cnt_s[x]; j += kVirtualTokens) {
+          a.v_expert[nv] = x;
+          a.v_pos0[nv] = off_s[x] + j;
+          a.v_count[nv] = min(kVirtualTokens, cnt_s[x] - j);
+          ++nv;
+        }
+      a.n_virtual[0] = nv;
+    }
   }
   __syncthreads();
   for (int s = tid; s < S; s += blockDim.x) {
