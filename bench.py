@@ -766,6 +766,10 @@ def model_batch_config(args, d):
     cfg.update(workload="gpt_oss_20b_batched_decode", batch=args.batch, kv_length=args.prompt,
                router=f"bias -{ZIPF_S} ln(rank) per layer (seeded rank permutation): Zipf-like expert loads",
                l2="inputs larger than L2: every step streams the weights of all hit experts and every KV run")
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        cfg["parallelism"] = (f"ep{ws}: experts {d['n_experts']}/{ws} per GPU, {args.batch // ws} sequences per "
+                              f"GPU; per layer and step the rows and output rows cross NVLink peer memory")
     return cfg
 
 
@@ -900,7 +904,8 @@ def run_model(args, ws, rank, local):
 
 
 ZIPF_S = 1.1
-BATCH_KERNELS = MODEL_KERNELS + ("router_topk", "permute", "combine")
+BATCH_KERNELS = MODEL_KERNELS + ("router_topk", "permute", "combine", "router_mma", "ep_counts", "ep_wait",
+                                  "ep_scatter", "ep_segments", "moe_ep_decode", "ep_signal")
 
 
 def zipf_router(m, s, seed):
@@ -932,33 +937,108 @@ def run_model_batch(args, ws, rank, local):
 
     device = torch.device("cuda", local)
     over = {} if args.model_layers is None else {"n_layers": args.model_layers}
-    m = synth.model_weights_device(seed=rank, device=device, **over)
-    zipf_router(m, ZIPF_S, 77 + rank)
+    # one model on every rank (expert parallel over N > 1 GPUs: the same weights)
+    m = synth.model_weights_device(seed=0, device=device, **over)
+    zipf_router(m, ZIPF_S, 77)
     d = m["dims"]
     B, P = args.batch, args.prompt
+    if B % ws:
+        raise SystemExit(f"--batch {B} must be a multiple of the GPU count {ws}")
+    Br = B // ws  # this rank's sequences
     chunk = 2048
-    n_prof, n_e2e = 4, max(4, min(args.steps, 16))
-    max_seq = P + args.warmup + args.steps + n_prof + n_e2e + 8
-    g = GPTModel(m, max_seq=max_seq, max_tokens=min(chunk, max_seq), max_batch=B)
+    n_prof, n_e2e, n_par = 4, max(4, min(args.steps, 16)), 4
+    max_seq = P + args.warmup + args.steps + n_prof + n_e2e + n_par + 8
+    from oxidized_gpt_oss_b200 import ep
+    shard = ep.shard_range(d["n_experts"], ws, rank) if ws > 1 else None
+    g = GPTModel(m, max_seq=max_seq, max_tokens=min(chunk, max_seq), max_batch=Br, experts=shard)
+    if ws > 1:
+        g.connect_expert_parallel()
+        # every expert on this GPU too, for the parity check of the same
+        # sequences; and a control: the first half of them as a batch of Br / 2
+        g_full = GPTModel(m, max_seq=max_seq, max_tokens=min(chunk, max_seq), max_batch=Br)
+        g_half = GPTModel(m, max_seq=max_seq, max_tokens=min(chunk, max_seq), max_batch=max(Br // 2, 1))
     del m
     torch.cuda.empty_cache()
     ctx = g.ctx
-    rng = np.random.default_rng(4321 + rank)
     stream = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    cur = torch.zeros(B, dtype=torch.int32, device=device)
+    cur = torch.zeros(Br, dtype=torch.int32, device=device)
+
+    def prompts():
+        rng = np.random.default_rng(4321 + rank)
+        return [torch.from_numpy(rng.integers(0, d["vocab"], P).astype(np.int32)).to(device) for _ in range(Br)]
+
     ev[0].record(stream)
-    for sq in range(B):
-        prompt = torch.from_numpy(rng.integers(0, d["vocab"], P).astype(np.int32)).to(device)
+    for sq, prompt in enumerate(prompts()):
         for c0 in range(0, P, chunk):
             nx = g.prefill_seq(sq, prompt[c0:c0 + chunk])
         cur[sq:sq + 1].copy_(nx)
     ev[1].record(stream)
+    torch.cuda.synchronize()
+    g.sync()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    parity = None
+    if ws > 1:
+        # expert-parallel steps against every expert on this GPU, same
+        # sequences, teacher-forced with the expert-parallel tokens (outside
+        # every timed region). The decode kernels' split of each expert's
+        # weights depends on how many groups of slots share the GPU, so the
+        # two runs round differently; a random-init 24-layer model amplifies
+        # that (a router near-tie flips an expert, an attention weight moves),
+        # which the control measures on one GPU: the first Br / 2 sequences
+        # stepped as a batch of Br / 2 against the same sequences in the batch
+        # of Br. Routing agreement counts (layer, token) expert sets.
+        hb = max(Br // 2, 1)
+        for sq, prompt in enumerate(prompts()):
+            for c0 in range(0, P, chunk):
+                g_full.prefill_seq(sq, prompt[c0:c0 + chunk])
+                if sq < hb:
+                    g_half.prefill_seq(sq, prompt[c0:c0 + chunk])
+        lg_ep = torch.empty((Br, d["vocab"]), dtype=torch.float32, device=device)
+        lg_full = torch.empty_like(lg_ep)
+        lg_half = torch.empty((hb, d["vocab"]), dtype=torch.float32, device=device)
+        tap_ep, tap_full, tap_half = g.route_tap(Br), g_full.route_tap(Br), g_half.route_tap(hb)
+        diff, same, diff_c, same_c, r_same, r_same_c, first = 0.0, 0, 0.0, 0, 0, 0, []
+        for _ in range(n_par):
+            nx_ep = g.step_batch(cur, logits=lg_ep)
+            nx_full = g_full.step_batch(cur, logits=lg_full)
+            nx_half = g_half.step_batch(cur[:hb], logits=lg_half)
+            torch.cuda.synchronize()
+            g.sync()
+            d_step = (lg_ep - lg_full).abs().max(dim=1).values
+            first.append(float(d_step.max().item()))
+            diff = max(diff, first[-1])
+            same += int((nx_ep == nx_full).sum().item())
+            diff_c = max(diff_c, float((lg_full[:hb] - lg_half).abs().max().item()))
+            same_c += int((nx_full[:hb] == nx_half).sum().item())
+            sf = torch.sort(tap_full, dim=2).values
+            r_same += int((torch.sort(tap_ep, dim=2).values == sf).all(dim=2).sum().item())
+            r_same_c += int((torch.sort(tap_half, dim=2).values == sf[:, :hb]).all(dim=2).sum().item())
+            cur = nx_ep
+        for gm in (g, g_full, g_half):
+            gm.route_tap(None)
+        import torch.distributed as dist
+        L_ = d["n_layers"]
+        t = torch.tensor([diff, -same / (n_par * Br), diff_c, -same_c / (n_par * hb), -r_same / (n_par * Br * L_),
+                          -r_same_c / (n_par * hb * L_), first[0]], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        v = t.tolist()
+        for gm in (g_full, g_half):
+            gm.release()
+        del g_full, g_half
+        torch.cuda.empty_cache()
+        parity = {"steps_checked": n_par, "sequences_per_rank": Br,
+                  "against": "the same sequences with every expert on one GPU, teacher-forced",
+                  "max_logit_abs_diff": v[0], "first_step_max_logit_abs_diff": v[6],
+                  "greedy_tokens_agree_min_over_ranks": -v[1], "routing_sets_agree_min_over_ranks": -v[4],
+                  "control_one_gpu_batch_half_vs_full": {"max_logit_abs_diff": v[2],
+                                                         "greedy_tokens_agree_min_over_ranks": -v[3],
+                                                         "routing_sets_agree_min_over_ranks": -v[5]},
+                  "moe_block": "tests/test_ep_gpu.py checks the expert-parallel decode block against the oracle"}
     for _ in range(args.warmup):
         cur = g.step_batch(cur)
     torch.cuda.synchronize()
     g.sync()
-    prefill_ms = ev[0].elapsed_time(ev[1])
     launches0 = ctx.launches()
     with ClockSampler(local) as clk:
         barrier(ws)
@@ -976,7 +1056,7 @@ def run_model_batch(args, ws, rank, local):
 
     # per-kernel device time: steps queued behind a GPU sleep, library CUDA
     # events per launch; the routing of the last one gives the experts hit
-    tap = g.route_tap(B)
+    tap = g.route_tap(Br)
     ctx.profile(True)
     ctx.profile_reset()
     for _ in range(n_prof):
@@ -986,11 +1066,19 @@ def run_model_batch(args, ws, rank, local):
     k_ms = {n: ctx.profile_read(n) for n in BATCH_KERNELS}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     ctx.profile(False)
-    routes = tap.cpu().numpy()  # [L, B, k]
+    if ws > 1:  # every rank's routing: the experts hit anywhere, and on this GPU
+        import torch.distributed as dist
+        allr = [torch.empty_like(tap) for _ in range(ws)]
+        dist.all_gather(allr, tap.contiguous())
+        routes = torch.cat([a.reshape(a.shape[0], -1) for a in allr], dim=1).cpu().numpy()  # [L, B * k]
+    else:
+        routes = tap.cpu().numpy().reshape(tap.shape[0], -1)
     g.route_tap(None)
     L, E = d["n_layers"], d["n_experts"]
-    loads = np.stack([np.bincount(routes[li].ravel(), minlength=E) for li in range(L)])
+    loads = np.stack([np.bincount(routes[li], minlength=E) for li in range(L)])
     hit = (loads > 0).sum(axis=1)
+    e0, ne = shard if shard is not None else (0, E)
+    hit_here = (loads[:, e0:e0 + ne] > 0).sum(axis=1)  # experts this GPU streams per layer
 
     H, V = d["hidden"], d["vocab"]
     nh, nkv, hd, W = d["n_heads"], d["n_kv_heads"], d["head_dim"], d["sliding_window"]
@@ -999,11 +1087,15 @@ def run_model_batch(args, ws, rank, local):
     o_b = H * Nq * 2
     mlp1_w = 2 * d["intermediate"] * H // 2 + 2 * d["intermediate"] * H // 32 + 2 * d["intermediate"] * 2
     mlp2_w = H * d["intermediate"] // 2 + H * d["intermediate"] // 32 + H * 2
-    head_b = V * H * 2 + B * V * 4
-    pos_mid = P + args.warmup + args.steps / 2
-    kv_b = B * sum(2 * nkv * hd * 2 * (min(W, pos_mid) if (li % 2 == 0 and W) else pos_mid) for li in range(L))
-    per_kernel_bytes = {"linear_qkv": L * qkv_b, "linear_o": L * o_b, "moe_mlp1_decode": int(hit.sum()) * mlp1_w,
-                        "moe_mlp2_decode": int(hit.sum()) * mlp2_w, "lm_head": head_b, "attention": kv_b}
+    head_b = V * H * 2 + Br * V * 4
+    pos_mid = P + n_par + args.warmup + args.steps / 2
+    kv_b = Br * sum(2 * nkv * hd * 2 * (min(W, pos_mid) if (li % 2 == 0 and W) else pos_mid) for li in range(L))
+    per_kernel_bytes = {"linear_qkv": L * qkv_b, "linear_o": L * o_b, "lm_head": head_b, "attention": kv_b}
+    if ws > 1:
+        per_kernel_bytes["moe_ep_decode"] = int(hit_here.sum()) * (mlp1_w + mlp2_w)
+    else:
+        per_kernel_bytes["moe_mlp1_decode"] = int(hit.sum()) * mlp1_w
+        per_kernel_bytes["moe_mlp2_decode"] = int(hit.sum()) * mlp2_w
     step_bytes = sum(per_kernel_bytes.values()) + L * E * H * 2
     hbm, hbm_kind = peaks()
     kern = {}
@@ -1019,18 +1111,19 @@ def run_model_batch(args, ws, rank, local):
 
     # end to end through the public API: each step's tokens from pinned host
     # memory, the greedy tokens back to pinned host memory
-    host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    host_tok = torch.empty(Br, dtype=torch.int32, pin_memory=True)
     host_tok.copy_(cur)
     torch.cuda.synchronize()
+    barrier(ws)
     t0 = time.perf_counter()
     for _ in range(n_e2e):
         nx = g.step_batch(host_tok.to(device, non_blocking=True))
         host_tok.copy_(nx)
     torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
 
     cfg = model_batch_config(args, d)
-    out = {"metric": METRIC, "value": ws * B * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+    out = {"metric": METRIC, "value": ws * Br * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "bf16 activations and attention weights, mxfp4 experts, f32 accumulate",
@@ -1041,16 +1134,21 @@ def run_model_batch(args, ws, rank, local):
                         "avg_launch_us": dom_ms / max(dom_n, 1) * 1e3},
            "step": {"hbm_gbs": step_bytes / (ms / args.steps * 1e-3) / 1e9,
                     "frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / hbm, "bytes": step_bytes,
-                    "kernels": kern, "prefill_ms": prefill_ms, "prefill_tokens": B * P,
+                    "kernels": kern, "prefill_ms": prefill_ms, "prefill_tokens": Br * P,
                     "experts_hit_per_layer": float(hit.mean()),
+                    "experts_streamed_per_layer_this_gpu": float(hit_here.mean()),
                     "max_expert_load_over_mean": float((loads.max(axis=1) / loads.mean(axis=1)).mean()),
                     "kernel_times": "steps queued behind a GPU sleep, library CUDA events per launch"},
-           "e2e": {"value": B * n_e2e / e2e_s, "unit": "tokens/s",
-                   "what": f"oxg_model_step_batch x {n_e2e}: {B} tokens from pinned host memory in, "
-                           f"{B} greedy tokens to pinned host memory out per step",
-                   "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
+           "e2e": {"value": ws * Br * n_e2e / e2e_s, "unit": "tokens/s",
+                   "what": f"oxg_model_step_batch x {n_e2e}: {Br} tokens per GPU from pinned host memory in, "
+                           f"{Br} greedy tokens to pinned host memory out per step",
+                   "h2d_bytes_per_step": Br * 4, "d2h_bytes_per_step": Br * 4},
            "gpu_launches": launches,
            "clocks": clk.summary()}
+    if parity is not None:
+        out["parity"] = parity
+    if ws > 1:
+        g.close_expert_parallel()
     if rank == 0 and ws == 1:
         cb = cpu_baseline_model(d)
         cb["sample"] += "; the reference decodes one sequence at a time, so its rate does not grow with the batch"

@@ -235,6 +235,14 @@ OXG_API int oxg_ep_connect(oxg_ctx *ctx, const void *handles);
 OXG_API int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x_dev, int n_tokens,
                                float *y_dev);
 OXG_API int oxg_ep_close(oxg_ctx *ctx);
+/* Decode-sized exchanges (no counterpart in the reference): forwards of at
+ * most `tokens` tokens (<= 64; 0, the default: none) process the rows this
+ * process receives with the grouped decode kernels (the rows of each resident
+ * expert in groups of at most 8, each group an equal share of the GPU)
+ * instead of the prefill GEMMs; outputs agree with oxg_moe_forward within the
+ * layer tolerance instead of bit for bit. Set the same value on every process
+ * after oxg_ep_connect. */
+OXG_API int oxg_ep_set_decode_tokens(oxg_ctx *ctx, int tokens);
 /* Rows this process received in its last oxg_moe_forward_ep (waits for it). */
 OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
 

@@ -31,6 +31,11 @@ int ctx_n_sms(const oxg_ctx *ctx);
 // context's stream with the library's automatic kernel choice, exactly as
 // oxg_moe_forward; ctx_moe_reserve sizes the scratch for T tokens once.
 int ctx_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y);
+// Expert parallelism: the hidden size of layer `layer` when it is a shard that
+// the context's peer-memory exchange serves (0 otherwise), and its forward
+// (oxg_moe_forward_ep; every process of the exchange must make the same calls).
+int ctx_moe_ep_hidden(oxg_ctx *ctx, int layer);
+int ctx_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y);
 int ctx_moe_reserve(oxg_ctx *ctx, int layer, int T);
 // Hidden size of uploaded MoE layer `layer` (0 when absent), its top-k, and
 // the expert ids [T, k] the context's last MoE forward chose (device).

@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_scatter_kernel(
 // to s's return rows from that expert's first position in s's dispatch order.
 __global__ void __launch_bounds__(256) ep_segments_kernel(EpLayout L, EpPeers P, uint32_t epoch,
                                                           int *err, int *ok_word, int32_t *seg,
-                                                          float **seg_ptr) {
+                                                          float **seg_ptr, EpVirtual virt) {
   __shared__ int ok_s;
   if (threadIdx.x < 32) {
     const bool ok = wait_flags(L, P, 1, epoch, err, 12);
@@ -232,6 +232,18 @@ __global__ void __launch_bounds__(256) ep_segments_kernel(EpLayout L, EpPeers P,
       run += seg[v];
     }
     seg[kEpMaxSegments + nv] = run;
+    if (virt.n) {  // each segment in groups of at most kVirtualTokens rows
+      int g = 0;
+      for (int v = 0; v < nv; ++v)
+        for (int j = 0; j < seg[v] && g < virt.cap; j += kVirtualTokens) {
+          virt.expert[g] = v % L.per;
+          virt.row0[g] = seg[kEpMaxSegments + v] + j;
+          virt.count[g] = min(kVirtualTokens, seg[v] - j);
+          virt.out[g] = seg_ptr[v] + (size_t)j * L.H;
+          ++g;
+        }
+      virt.n[0] = g;
+    }
   }
 }
 
@@ -294,8 +306,9 @@ cudaError_t launch_ep_scatter(const EpLayout &L, const EpPeers &P, const int32_t
 }
 
 cudaError_t launch_ep_segments(const EpLayout &L, const EpPeers &P, uint32_t epoch, int *err,
-                               int *ok_word, int32_t *seg, float **seg_ptr, cudaStream_t stream) {
-  ep_segments_kernel<<<1, 256, 0, stream>>>(L, P, epoch, err, ok_word, seg, seg_ptr);
+                               int *ok_word, int32_t *seg, float **seg_ptr, const EpVirtual &virt,
+                               cudaStream_t stream) {
+  ep_segments_kernel<<<1, 256, 0, stream>>>(L, P, epoch, err, ok_word, seg, seg_ptr, virt);
   return cudaGetLastError();
 }
 

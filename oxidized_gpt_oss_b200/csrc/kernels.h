@@ -299,11 +299,30 @@ cudaError_t launch_ep_scatter(const EpLayout &L, const EpPeers &P, const int32_t
                               const int32_t *idx, const int32_t *local_rank, int T, const uint16_t *x,
                               const int32_t *sigma, int32_t *slot_pos, uint32_t *done_ctr,
                               int *ok_word, int *err, uint32_t epoch, cudaStream_t stream);
-// seg: counts [kEpMaxSegments] then offsets [kEpMaxSegments + 1]; seg_ptr [kEpMaxSegments]
+// Groups of at most kVirtualTokens received rows of one segment (the
+// grouped decode kernels' virtual experts): resident expert, first row, row
+// count and first output row (in the source's return rows) of each.
+struct EpVirtual {
+  int32_t *expert, *row0, *count, *n;
+  float **out;
+  int cap;  // entries the arrays hold
+};
+// seg: counts [kEpMaxSegments] then offsets [kEpMaxSegments + 1]; seg_ptr
+// [kEpMaxSegments]; virt (optional, its arrays may be null): the groups
 cudaError_t launch_ep_segments(const EpLayout &L, const EpPeers &P, uint32_t epoch, int *err,
-                               int *ok_word, int32_t *seg, float **seg_ptr, cudaStream_t stream);
+                               int *ok_word, int32_t *seg, float **seg_ptr, const EpVirtual &virt,
+                               cudaStream_t stream);
 cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch,
                              const int *ok_word, cudaStream_t stream);
+
+// Expert-parallel decode on the receiving rank: the resident experts' MLPs
+// over the received rows (f16 x * 2^-sigma [R, H] with their 2^sigma), in the
+// groups of EpVirtual (grouped mlp1 into h [R, I], grouped mlp2 storing each
+// group's output rows from its out pointer). ep_decode_supported is false when
+// the grouped kernels' shared memory does not fit these widths.
+bool ep_decode_supported(int H, int I, int n_sms, int max_groups);
+cudaError_t launch_ep_decode(const MoeDeviceWeights &w, const uint16_t *rows, const float *row_scale, float *h,
+                             const EpVirtual &virt, const DecodeSched &s, cudaStream_t stream);
 
 // out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,

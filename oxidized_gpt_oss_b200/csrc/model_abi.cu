@@ -223,12 +223,21 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
   cudaStream_t s = ctx_stream(ctx);
   const int n_sms = ctx_n_sms(ctx);
   if (!M.embed) return mfail(ctx, OXG_ERR_STATE, "embeddings have not been uploaded");
+  bool ep = false;  // the MoE blocks are expert-parallel shards (every process runs the same steps)
   for (int l = 0; l < L; ++l) {
     if (!M.layers[l].block) return mfail(ctx, OXG_ERR_STATE, "attention of layer %d has not been uploaded", l);
-    const int mh = ctx_moe_hidden(ctx, l);
-    if (!mh) return mfail(ctx, OXG_ERR_STATE, "MoE layer %d has not been uploaded (whole, not as a shard)", l);
+    int mh = ctx_moe_hidden(ctx, l);
+    if (!mh && (mh = ctx_moe_ep_hidden(ctx, l)) != 0) ep = true;
+    if (!mh)
+      return mfail(ctx, OXG_ERR_STATE,
+                   "MoE layer %d has not been uploaded (whole, or as this process's shard of a connected "
+                   "expert-parallel exchange)", l);
     if (mh != H) return mfail(ctx, OXG_ERR_STATE, "MoE layer %d has hidden %d, the model %d", l, mh, H);
   }
+  if (ep && dstate)
+    return mfail(ctx, OXG_ERR_UNSUPPORTED,
+                 "expert-parallel MoE blocks run eagerly (their exchange counts steps on the host): use "
+                 "oxg_model_forward / oxg_model_step_batch");
   if (!M.moe_reserved) {
     for (int l = 0; l < L; ++l) {
       const int rc = ctx_moe_reserve(ctx, l, d.max_tokens);
@@ -310,7 +319,7 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
       MCUDA(ctx, ctx_launch(ctx, "residual_norm", [&] { return launch_residual_norm(a, s); }),
             "residual norm launch");
     }
-    int rc = ctx_moe_forward(ctx, l, M.xn, T, M.y);
+    int rc = ctx_moe_hidden(ctx, l) ? ctx_moe_forward(ctx, l, M.xn, T, M.y) : ctx_moe_forward_ep(ctx, l, M.xn, T, M.y);
     if (rc) return rc;
     if (M.route_tap && !dstate && T <= M.tap_tokens) {
       const int k = ctx_moe_topk(ctx, l);

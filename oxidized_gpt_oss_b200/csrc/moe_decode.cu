@@ -138,6 +138,12 @@ struct DecodeArgs {
   // grouped kernels: virtual experts (expert id, first position, slot count
   // of each group of at most kVirtualTokens slots, and their number)
   const int32_t *v_expert, *v_pos0, *v_count, *n_virtual;
+  // received-rows mode (expert parallelism): mlp1 reads f16 rows x * 2^-sigma
+  // [pos, K] with their 2^sigma instead of gathering x through perm, and mlp2
+  // writes each group's rows from v_out[group] (another rank's return rows)
+  const uint16_t *xrows;
+  const float *row_scale;
+  float *const *v_out;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -973,28 +979,37 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_group_kernel(const DecodeA
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const int n_v = *a.n_virtual;
-  const int per = (int)gridDim.x / max(n_v, 1);
-  const int ai = per > 0 ? (int)blockIdx.x / per : n_v;
-  if (ai >= n_v) return;
-  const int band = (int)blockIdx.x - ai * per;
-  const int e = a.v_expert[ai];
-  const int n_e = a.v_count[ai], pos0 = a.v_pos0[ai];
+  // one group of `per` CTAs per virtual expert; with more virtual experts
+  // than CTAs, CTA c takes virtual experts c, c + gridDim.x, ... alone
+  const bool spread = n_v <= (int)gridDim.x;
+  const int per = spread ? (int)gridDim.x / max(n_v, 1) : 1;
+  const int band = spread ? (int)blockIdx.x % per : 0;
+  const int stride = spread ? (int)gridDim.x / per : (int)gridDim.x;
   const int n_tiles = a.rows / 16;
   const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0), fs_tail = nb % 4;
+#pragma unroll 1
+  for (int ai = (int)blockIdx.x / per; ai < n_v; ai += stride) {
+  const int e = a.v_expert[ai];
+  const int n_e = a.v_count[ai], pos0 = a.v_pos0[ai];
 
   const FlatRange R = flat_range(n_tiles * n_grp, per * WARPS);
   const int w = band * WARPS + warp;
   const int c0 = R.lo(w), c1 = R.lo(w + 1);
-  const int slot_base = ai * per * WARPS;  // the group's first warp in the grid
+  const int slot_base = (spread ? ai * per : (int)blockIdx.x) * WARPS;  // the group's first warp
   uint8_t *ring = smem + 8 * XS + warp * (STAGES * kStageBytes);
   auto item_ptr = [&](int tile) { return a.codes + ((size_t)e * n_tiles + tile) * a.item_bytes; };
   FlatStream<STAGES, decltype(item_ptr)> fs(c0, c1, K, ring, item_ptr);
   fs.prefill();
 
-  // stage the group's x rows (the loads of kU units per thread issued together)
-  if (tid < 8)
-    tok_scale[tid] =
-        tid < n_e ? __uint_as_float((uint32_t)(127 + a.sigma[a.perm[pos0 + tid] / a.topk]) << 23) : 1.f;
+  // stage the group's x rows (the loads of kU units per thread issued
+  // together): gathered from x through perm, or the received f16 rows as they are
+  if (tid < 8) {
+    float sc = 1.f;
+    if (tid < n_e)
+      sc = a.xrows ? a.row_scale[pos0 + tid]
+                   : __uint_as_float((uint32_t)(127 + a.sigma[a.perm[pos0 + tid] / a.topk]) << 23);
+    tok_scale[tid] = sc;
+  }
   constexpr int kU = 4;
   const int units = 8 * (K / 8);
   for (int u0 = tid; u0 < units; u0 += kU * kThreads) {
@@ -1006,15 +1021,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_group_kernel(const DecodeA
       v[j] = make_uint4(0u, 0u, 0u, 0u);
       inv[j] = 0.f;
       if (u < units && row < n_e) {
-        const int t = a.perm[pos0 + row] / a.topk;
-        v[j] = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + c8 * 8);
-        inv[j] = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
+        if (a.xrows) {
+          v[j] = *reinterpret_cast<const uint4 *>(a.xrows + (size_t)(pos0 + row) * K + c8 * 8);
+        } else {
+          const int t = a.perm[pos0 + row] / a.topk;
+          v[j] = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * K + c8 * 8);
+          inv[j] = __uint_as_float((uint32_t)(127 - a.sigma[t]) << 23);
+        }
       }
     }
 #pragma unroll
     for (int j = 0; j < kU; ++j) {
       const int u = u0 + j * kThreads, row = u / (K / 8), c8 = u - row * (K / 8);
-      if (u < units) {
+      if (u < units && a.xrows) {
+        *reinterpret_cast<uint4 *>(smem + row * XS + c8 * 16) = v[j];  // already f16 x * 2^-sigma
+      } else if (u < units) {
         uint4 o;
         o.x = pack_f16x2(bf16_to_f32(v[j].x & 0xFFFFu) * inv[j], bf16_to_f32(v[j].x >> 16) * inv[j]);
         o.y = pack_f16x2(bf16_to_f32(v[j].y & 0xFFFFu) * inv[j], bf16_to_f32(v[j].y >> 16) * inv[j]);
@@ -1081,6 +1102,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp1_group_kernel(const DecodeA
   };
   fs.consume(start_fn, full_fn, tail_fn, end_fn);
   split.settle(R, w, n_grp, a.parts, a.flat_cnt, slot_base, write_tile);
+  __syncthreads();  // the next virtual expert reuses the stage and the rings
+  }
 }
 
 // mlp2 + bias over the virtual experts (groups of at most 8 consecutive
@@ -1107,20 +1130,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp2_flat_kernel(const DecodeAr
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const int n_act = *a.n_virtual;  // groups that finish every tile (the combine's count)
-  const int per = (int)gridDim.x / max(n_act, 1);
-  const int ai = per > 0 ? (int)blockIdx.x / per : n_act;
-  if (ai >= n_act) return;
-  const int band = (int)blockIdx.x - ai * per;
+  // one group of `per` CTAs per virtual expert; with more virtual experts
+  // than CTAs, CTA c takes virtual experts c, c + gridDim.x, ... alone
+  const bool spread = n_act <= (int)gridDim.x;
+  const int per = spread ? (int)gridDim.x / max(n_act, 1) : 1;
+  const int band = spread ? (int)blockIdx.x % per : 0;
+  const int stride = spread ? (int)gridDim.x / per : (int)gridDim.x;
+  const int n_tiles = a.rows / 16;
+  const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0);
+#pragma unroll 1
+  for (int ai = (int)blockIdx.x / per; ai < n_act; ai += stride) {
   const int e = a.v_expert[ai];
   const int n_e = a.v_count[ai], pos0 = a.v_pos0[ai];
   const int ngc = (2 * n_e + 7) / 8;  // column groups in use (<= NCG)
-  const int n_tiles = a.rows / 16;
-  const int nb = K / 32, n_grp = nb / 4 + (nb % 4 ? 1 : 0);
 
   const FlatRange R = flat_range(n_tiles * n_grp, per * WARPS);
   const int w = band * WARPS + warp;
   const int c0 = R.lo(w), c1 = R.lo(w + 1);
-  const int slot_base = ai * per * WARPS;  // the group's first warp in the grid
+  const int slot_base = (spread ? ai * per : (int)blockIdx.x) * WARPS;  // the group's first warp
   uint8_t *ring = smem + 8 * NCG * XS + warp * (STAGES * kStageBytes);
   auto item_ptr = [&](int tile) { return a.codes + ((size_t)e * n_tiles + tile) * a.item_bytes; };
   FlatStream<STAGES, decltype(item_ptr)> fs(c0, c1, K, ring, item_ptr);
@@ -1194,16 +1221,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp2_flat_kernel(const DecodeAr
     for (int b = 0; b < 3; ++b)
       if (b < fs_tail) block(bp + 64 * b, wa[b], wb[b], sa[b], sb[b]);
   };
-  // bias + store of one finished tile's rows for the expert's tokens
+  // bias + store of one finished tile's rows for the group's slots (to
+  // y_slot, or from the group's output pointer: another rank's return rows)
+  float *const out0 = a.v_out ? a.v_out[ai] : a.out + (size_t)pos0 * a.out_ld;
   auto write_tile = [&](int tile, const float4 (&v)[NCG], float2 bias) {
     const int ra = tile * 16 + g, rb = ra + 8;  // rows g and g + 8 of the tile
 #pragma unroll
     for (int cg = 0; cg < NCG; ++cg) {
       const int tok = cg * 4 + q;  // columns 2q (hi) and 2q + 1 (lo) of the group
       if (cg < ngc && tok < n_e) {
-        const size_t pos = (size_t)(pos0 + tok);
-        a.out[pos * a.out_ld + ra] = (v[cg].x + v[cg].y) + bias.x;
-        a.out[pos * a.out_ld + rb] = (v[cg].z + v[cg].w) + bias.y;
+        out0[(size_t)tok * a.out_ld + ra] = (v[cg].x + v[cg].y) + bias.x;
+        out0[(size_t)tok * a.out_ld + rb] = (v[cg].z + v[cg].w) + bias.y;
       }
     }
   };
@@ -1257,6 +1285,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) mlp2_flat_kernel(const DecodeAr
       write_tile(tile, v, bias);
       if (a.band_done) combine_tile(tile);
     });
+  }
+  __syncthreads();  // the next virtual expert reuses the stage and the rings
   }
 }
 
@@ -1694,7 +1724,7 @@ cudaError_t launch_moe_mlp1_sched(const MoeDeviceWeights &w, const uint16_t *x,
   }
   // above 8 tokens: equal CTA groups per virtual expert (at most 8 of an
   // expert's slots each), so a hot expert's tokens spread over the GPU
-  if (flat_ok && s.v_expert && s.max_virtual <= s.n_sms)
+  if (flat_ok && s.v_expert)
     return launch_ex(mlp1_group_kernel<kWf1, kSf1>, dim3(s.n_sms), kWf1 * 32, flat_smem, a.pdl, stream, a);
   a.bands = s.bands1;
   return launch_decode<1, 1>(a, s.max_active, stream);
@@ -1723,7 +1753,7 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
   a.v_pos0 = s.v_pos0;
   a.v_count = s.v_count;
   a.n_virtual = s.n_virtual;
-  if (T > 8 && kUseFlat && s.parts && s.flat_cnt && s.v_expert && s.max_virtual <= s.n_sms) {
+  if (T > 8 && kUseFlat && s.parts && s.flat_cnt && s.v_expert) {
     // equal CTA groups per virtual expert (at most 8 slots: two column groups
     // of four slots' hi / lo halves), flat split inside each group
     const size_t smem = (size_t)16 * flat_row_pitch(a.K) + (size_t)kWf2b * kSf2b * kStageBytes;
@@ -1752,6 +1782,49 @@ cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const f
   unsigned grid = (unsigned)(want < 148 * 8 ? want : 148 * 8);
   combine_kernel<<<grid, 256, 0, stream>>>(y_slot, slot_pos, wts, T, H, k, out);
   return cudaGetLastError();
+}
+
+}  // namespace oxg
+
+namespace oxg {
+
+bool ep_decode_supported(int H, int I, int n_sms, int max_groups) {
+  const size_t s1 = (size_t)8 * flat_row_pitch(H) + (size_t)kWf1 * kSf1 * kStageBytes;
+  const size_t s2 = (size_t)16 * flat_row_pitch(I) + (size_t)kWf2b * kSf2b * kStageBytes;
+  (void)max_groups;  // any number: with more groups than CTAs each CTA takes several in turn
+  return kUseFlat && s1 <= kMaxFlatSmem && s2 <= kMaxFlatSmem && n_sms * kWf1 <= kFlatMaxWarps &&
+         n_sms * kWf2b <= kFlatMaxWarps;
+}
+
+cudaError_t launch_ep_decode(const MoeDeviceWeights &w, const uint16_t *rows, const float *row_scale, float *h,
+                             const EpVirtual &virt, const DecodeSched &s, cudaStream_t stream) {
+  if (!ep_decode_supported(w.H, w.I, s.n_sms, virt.cap) || !s.parts || !s.flat_cnt) return cudaErrorInvalidValue;
+  DecodeArgs a = mlp1_args(w, nullptr, nullptr, nullptr, nullptr, nullptr, h);
+  a.pdl = s.pdl;
+  a.err = s.err;
+  a.parts = s.parts;
+  a.flat_cnt = s.flat_cnt;
+  a.v_expert = virt.expert;
+  a.v_pos0 = virt.row0;
+  a.v_count = virt.count;
+  a.n_virtual = virt.n;
+  a.xrows = rows;
+  a.row_scale = row_scale;
+  cudaError_t st = launch_ex(mlp1_group_kernel<kWf1, kSf1>, dim3(s.n_sms), kWf1 * 32,
+                             (size_t)8 * flat_row_pitch(a.K) + (size_t)kWf1 * kSf1 * kStageBytes, a.pdl, stream, a);
+  if (st != cudaSuccess) return st;
+  DecodeArgs b = mlp2_args(w, h, nullptr, nullptr, nullptr);
+  b.pdl = s.pdl;
+  b.err = s.err;
+  b.parts = s.parts;
+  b.flat_cnt = s.flat_cnt;
+  b.v_expert = virt.expert;
+  b.v_pos0 = virt.row0;
+  b.v_count = virt.count;
+  b.n_virtual = virt.n;
+  b.v_out = virt.out;
+  return launch_ex(mlp2_flat_kernel<kWf2b, kSf2b, 2>, dim3(s.n_sms), kWf2b * 32,
+                   (size_t)16 * flat_row_pitch(b.K) + (size_t)kWf2b * kSf2b * kStageBytes, b.pdl, stream, b);
 }
 
 }  // namespace oxg

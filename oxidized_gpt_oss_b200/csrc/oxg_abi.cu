@@ -192,6 +192,12 @@ struct oxg_ctx {
     int *ok_word = nullptr;
     uint32_t epoch = 0;
     int I = 0;  // intermediate size the h buffers were sized for
+    // decode-sized exchanges: the received rows in groups of at most 8 run
+    // through the grouped decode kernels instead of the prefill GEMMs
+    oxg::EpVirtual virt{};
+    bool decode = false;   // the grouped kernels fit these widths
+    int decode_tokens = 0;  // forwards of at most this many tokens receive on them (oxg_ep_set_decode_tokens)
+    float *h_f32 = nullptr;  // [max_recv, I] f32 SwiGLU output of the grouped kernels
   } p2p;
 };
 
@@ -840,6 +846,20 @@ int ctx_moe_forward(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y)
 }
 
 int ctx_moe_reserve(oxg_ctx *ctx, int layer, int T) { return oxg_moe_reserve(ctx, layer, T); }
+
+int ctx_moe_ep_hidden(oxg_ctx *ctx, int layer) {
+  Layer *L = get_layer(ctx, layer);
+  const auto &q = ctx->p2p;
+  if (!L || !L->sharded() || !q.connected) return 0;
+  if (L->expert_begin != q.lay.rank * q.lay.per || L->expert_count != q.lay.per || L->dims.n_experts != q.lay.E ||
+      L->dims.hidden != q.lay.H || L->dims.intermediate != q.I || L->dims.top_k != q.lay.k)
+    return 0;
+  return L->dims.hidden;
+}
+
+int ctx_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float *y) {
+  return oxg_moe_forward_ep(ctx, layer, x, T, y);
+}
 
 int ctx_moe_hidden(oxg_ctx *ctx, int layer) {
   Layer *L = get_layer(ctx, layer);
@@ -1526,8 +1546,11 @@ int oxg_ep_init(oxg_ctx *ctx, int layer, int rank, int world, int max_tokens, lo
   OXG_CUDA(ctx, cudaMalloc(&q.sym, q.lay.bytes), "cudaMalloc(expert-parallel symmetric buffer)");
   OXG_CUDA(ctx, cudaMemset(q.sym, 0, q.lay.off_inbox), "zero the flags");
   const size_t hb = align_up((size_t)max_recv_rows * d.intermediate * 2, 256);
+  // groups of at most 8 received rows: at most one per segment plus one per 8 rows
+  const int vcap = q.lay.W * q.lay.per + (int)(max_recv_rows / oxg::kVirtualTokens) + 1;
+  const size_t vb = align_up((size_t)vcap * 4, 256), vpb = align_up((size_t)vcap * sizeof(float *), 256);
   const size_t local_bytes = 2 * hb + align_up((oxg::kEpMaxSegments * 2 + 1) * 4, 256) +
-                             align_up(oxg::kEpMaxSegments * sizeof(float *), 256) + 256;
+                             align_up(oxg::kEpMaxSegments * sizeof(float *), 256) + 256 + 3 * vb + 256 + vpb;
   OXG_CUDA(ctx, cudaMalloc(&q.local, local_bytes), "cudaMalloc(expert-parallel scratch)");
   OXG_CUDA(ctx, cudaMemset(q.local, 0, local_bytes), "zero the expert-parallel scratch");
   char *b = (char *)q.local;
@@ -1537,6 +1560,21 @@ int oxg_ep_init(oxg_ctx *ctx, int layer, int rank, int world, int max_tokens, lo
   q.seg_ptr = (float **)(b + 2 * hb + align_up((oxg::kEpMaxSegments * 2 + 1) * 4, 256));
   q.done_ctr = (uint32_t *)((char *)q.seg_ptr + align_up(oxg::kEpMaxSegments * sizeof(float *), 256));
   q.ok_word = (int *)(q.done_ctr + 1);
+  {
+    char *vbase = (char *)q.done_ctr + 256;
+    q.virt.expert = (int32_t *)vbase;
+    q.virt.row0 = (int32_t *)(vbase + vb);
+    q.virt.count = (int32_t *)(vbase + 2 * vb);
+    q.virt.n = (int32_t *)(vbase + 3 * vb);
+    q.virt.out = (float **)(vbase + 3 * vb + 256);
+    q.virt.cap = vcap;
+  }
+  q.decode = oxg::ep_decode_supported(d.hidden, d.intermediate, ctx->n_sms, vcap);
+  if (q.decode) {
+    // the grouped kernels keep h in f32: it takes the place of the f16 hi / lo pair
+    if ((size_t)max_recv_rows * d.intermediate * 4 <= 2 * hb) q.h_f32 = (float *)q.h_hi;
+    else q.decode = false;
+  }
   cudaIpcMemHandle_t h;
   OXG_CUDA(ctx, cudaIpcGetMemHandle(&h, q.sym), "cudaIpcGetMemHandle");
   std::memcpy(handle_out, &h, sizeof(h));
@@ -1564,6 +1602,19 @@ int oxg_ep_connect(oxg_ctx *ctx, const void *handles) {
     q.peers.base[r] = (char *)p;
   }
   q.connected = true;
+  return OXG_OK;
+}
+
+int oxg_ep_set_decode_tokens(oxg_ctx *ctx, int tokens) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  auto &q = ctx->p2p;
+  if (!q.init) return fail(ctx, OXG_ERR_STATE, "oxg_ep_init first");
+  if (tokens < 0 || tokens > oxg::kMaxRouteTokens)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "tokens must be in [0, %d], got %d", oxg::kMaxRouteTokens, tokens);
+  if (tokens > 0 && !q.decode)
+    return fail(ctx, OXG_ERR_UNSUPPORTED, "the grouped decode kernels do not fit hidden %d / intermediate %d",
+                q.lay.H, q.I);
+  q.decode_tokens = tokens;
   return OXG_OK;
 }
 
@@ -1647,12 +1698,32 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
              }),
              "ep_signal launch");
   }
+  // a decode-sized batch on this rank (the path is each receiver's own
+  // choice: both handle whatever rows the others sent); off while the
+  // decode size is 0, whatever this rank's batch
+  const bool grouped = q.decode && q.decode_tokens > 0 && T <= q.decode_tokens;
   OXG_CUDA(ctx, launch(ctx, "ep_segments", [&] {
              return oxg::launch_ep_segments(lay, peers, epoch, ctx->ws.err, q.ok_word, q.seg,
-                                            q.seg_ptr, ctx->stream);
+                                            q.seg_ptr, grouped ? q.virt : oxg::EpVirtual{}, ctx->stream);
            }),
            "ep_segments launch");
   const oxg::MoeDeviceWeights w = device_weights(*L);
+  if (grouped) {
+    // the grouped decode kernels over the received rows, each group's output
+    // rows stored straight into its source's return rows
+    oxg::DecodeSched sched{};
+    sched.n_sms = ctx->n_sms;
+    sched.err = ctx->ws.err;
+    sched.parts = ctx->ws.parts;
+    sched.flat_cnt = ctx->ws.flat_cnt;
+    OXG_CUDA(ctx, launch(ctx, "moe_ep_decode", [&] {
+               return oxg::launch_ep_decode(w, (const uint16_t *)((char *)q.sym + lay.off_recv_rows),
+                                            (const float *)((char *)q.sym + lay.off_recv_scale), q.h_f32, q.virt,
+                                            sched, ctx->stream);
+             }),
+             "ep decode launch");
+    ctx->launches += 1;  // two kernels
+  } else {
   oxg::PrefillIO io{};
   io.S = (int)lay.max_recv;
   io.counts = q.seg;
@@ -1674,6 +1745,7 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
              return oxg::launch_prefill_mlp2(w, io, ctx->n_sms, ctx->stream);
            }),
            "prefill mlp2 launch");
+  }
   OXG_CUDA(ctx, launch(ctx, "ep_signal", [&] {
              return oxg::launch_ep_signal(lay, peers, 2, epoch, q.ok_word, ctx->stream);
            }),

@@ -98,7 +98,11 @@ class PeerExpertParallelMoE:
     the IPC handles once, at construction. Every rank must call ``forward``
     the same number of times; ``close`` on every rank when all are done."""
 
-    def __init__(self, shard, max_tokens: int, group=None, max_recv_rows: int = 0):
+    def __init__(self, shard, max_tokens: int, group=None, max_recv_rows: int = 0, decode_tokens: int = 0):
+        """decode_tokens: forwards of at most that many tokens (<= 64) process
+        the received rows with the grouped decode kernels (within the layer
+        tolerance of one GPU's forward, not bit for bit); the same value on
+        every rank."""
         import ctypes
         from .mxfp4 import context
         self.shard = shard
@@ -117,6 +121,8 @@ class PeerExpertParallelMoE:
         dist.all_gather_object(handles, mine, group=group)
         blob = (ctypes.c_char * (64 * self.world)).from_buffer_copy(b"".join(handles))
         abi.check(c.lib.oxg_ep_connect(c.handle, blob), c.handle)
+        if decode_tokens:
+            abi.check(c.lib.oxg_ep_set_decode_tokens(c.handle, int(decode_tokens)), c.handle)
         self._abi = abi
 
     def forward(self, hidden: torch.Tensor, out: torch.Tensor | None = None, shard=None) -> torch.Tensor:

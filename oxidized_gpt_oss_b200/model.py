@@ -52,7 +52,10 @@ class GPTModel:
     """
 
     def __init__(self, weights: dict, *, max_seq: int = 4096, max_tokens: int = 2048, max_batch: int = 1,
-                 ctx: abi.Context | None = None):
+                 ctx: abi.Context | None = None, experts: tuple[int, int] | None = None):
+        """experts: (begin, count) to keep only that range of every MoE
+        block's experts (expert parallelism; then ``connect_expert_parallel``
+        on every process before the first forward)."""
         # a context of its own (its layer ids 0..n_layers-1 must not collide
         # with other MoE layers), bound to torch's current stream
         self.ctx = ctx if ctx is not None else abi.Context(torch.cuda.current_device())
@@ -82,11 +85,41 @@ class GPTModel:
                                int(mw["top_k"]), float(mw["alpha"]), float(mw["limit"]))
             ws = abi.MoeWeights(*[_ptr(mkeep[k]) for k in ("router_w", "router_b", "w1_blocks", "w1_scales",
                                                             "b1", "w2_blocks", "w2_scales", "b2")])
-            abi.check(lib.oxg_moe_upload(h, layer, ctypes.byref(dims), ctypes.byref(ws)), h)
+            if experts is None:
+                abi.check(lib.oxg_moe_upload(h, layer, ctypes.byref(dims), ctypes.byref(ws)), h)
+            else:
+                abi.check(lib.oxg_moe_upload_shard(h, layer, ctypes.byref(dims), ctypes.byref(ws),
+                                                   int(experts[0]), int(experts[1])), h)
+        self.experts = experts
+        self._ep = None
+        self._moe_hidden = int(weights["layers"][0]["moe"]["hidden"])
         dev = torch.device("cuda", self.ctx.device)
         self._dev = dev
         self._topk = int(weights["layers"][0]["moe"]["top_k"])
         self._tap = None
+
+    def connect_expert_parallel(self, group=None, max_recv_rows: int = 0) -> None:
+        """Expert parallelism over NVLink peer memory for every MoE block (all
+        layers share one exchange: the buffers depend only on the shapes and
+        the expert range). Collective over ``group``: every process, with the
+        shard ``ep.shard_range`` gives its rank, calls it once; afterwards
+        every process must run the same forwards / batched steps (the MoE
+        blocks exchange rows with the others), eagerly: ``decode`` and
+        ``generate`` capture CUDA graphs and refuse shard layers."""
+        from types import SimpleNamespace
+        from .ep import PeerExpertParallelMoE
+        if self.experts is None:
+            raise ValueError("the model holds whole MoE blocks: construct it with experts=(begin, count)")
+        shard = SimpleNamespace(ctx=self.ctx, layer=0, hidden=self._moe_hidden)
+        # batched decode steps (one token per sequence) receive on the grouped
+        # decode kernels; prompt chunks on the prefill GEMMs
+        self._ep = PeerExpertParallelMoE(shard, max_tokens=self.max_tokens, group=group,
+                                         max_recv_rows=max_recv_rows, decode_tokens=min(self.max_batch, 64))
+
+    def close_expert_parallel(self) -> None:
+        if self._ep is not None:
+            self._ep.close()
+            self._ep = None
 
     # -- reference-shaped API ------------------------------------------------
     def reset_kv_cache(self) -> None:

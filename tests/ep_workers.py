@@ -156,3 +156,92 @@ def gpu_p2p_worker(rank, world, port, layer_kw, tokens, out_dir):
         if moe is not None:
             moe.close()
         dist.destroy_process_group()
+
+
+def gpu_model_ep_worker(rank, world, port, out_dir):
+    """Batched decode of a 2-layer gpt-oss-architecture model (16 experts,
+    vocab 4096) with the MoE blocks expert parallel (8 experts per GPU, rows
+    over peer memory, decode steps received on the grouped kernels) against
+    the same sequences with every expert on this GPU: three sequences per
+    rank, four teacher-forced steps, logits compared."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    g = None
+    try:
+        from oxidized_gpt_oss_b200.model import GPTModel
+        m = synth.model_weights(seed=9, n_layers=2, vocab=4096, n_experts=16)
+        shard = ep.shard_range(16, world, rank)
+        g = GPTModel(m, max_seq=256, max_tokens=128, max_batch=3, experts=shard)
+        g.connect_expert_parallel()
+        full = GPTModel(m, max_seq=256, max_tokens=128, max_batch=3)
+        rng = np.random.default_rng(100 + rank)
+        cur = torch.zeros(3, dtype=torch.int32, device="cuda")
+        for sq, n in enumerate((40, 70, 20)):  # every rank runs the same steps
+            ids = torch.from_numpy(rng.integers(0, 4096, n).astype(np.int32)).cuda()
+            cur[sq:sq + 1].copy_(g.prefill_seq(sq, ids))
+            full.prefill_seq(sq, ids)
+        lg_ep = torch.empty((3, 4096), dtype=torch.float32, device="cuda")
+        lg_full = torch.empty_like(lg_ep)
+        diffs, agree = [], 0
+        for _ in range(4):
+            nx = g.step_batch(cur, logits=lg_ep)
+            nf = full.step_batch(cur, logits=lg_full)
+            torch.cuda.synchronize()
+            g.sync()
+            diffs.append(float((lg_ep - lg_full).abs().max()))
+            agree += int((nx == nf).sum())
+            cur = nx
+        full.release()
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump({"diffs": diffs, "agree": agree}, f)
+    finally:
+        if g is not None:
+            g.close_expert_parallel()
+        dist.destroy_process_group()
+
+
+def gpu_p2p_grouped_worker(rank, world, port, layer_kw, tokens, hot, out_dir):
+    """Peer-memory expert parallelism with decode-sized batches received on
+    the grouped decode kernels: two forwards per rank, each checked against
+    the oracle on the full layer's routing of the same tokens. A router bias
+    of -hot * ln(rank) skews the loads (segments of more than 8 rows)."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    moe = None
+    try:
+        from oxidized_gpt_oss_b200.moe import MoELayer
+        d = synth.moe_layer(**layer_kw)
+        E = d["n_experts"]
+        if hot:
+            rk = np.random.default_rng(E).permutation(E) + 1
+            b = oracle.np_bf16_to_f32(d["router_b"]) - hot * np.log(rk)
+            d["router_b"] = oracle.np_f32_to_bf16(b.astype(np.float32))
+        begin, count = ep.shard_range(E, world, rank)
+        shard = MoELayer(d, experts=(begin, count))
+        full = MoELayer(d)
+        moe = ep.PeerExpertParallelMoE(shard, max_tokens=max(tokens), decode_tokens=max(tokens))
+        res = []
+        for it in range(2):
+            x = synth.activations(100 * it + rank, tokens[rank], d["hidden"])
+            xt = torch.from_numpy(x.view(np.int16)).cuda()
+            y_ep = moe(xt).clone()
+            torch.cuda.synchronize()
+            shard.ctx.sync()
+            if tokens[rank] == 0:
+                res.append((0.0, 0.0, 0))
+                continue
+            idx, w, _ = full.route(xt)
+            full.ctx.sync()
+            idx_np = idx.cpu().numpy()
+            y_ref = oracle.moe_forward_spec(oracle.Weights(d), x, idx=idx_np, wts=w.cpu().numpy(), acc64=True)
+            err = np.abs(y_ep.cpu().numpy() - y_ref)
+            res.append((float(err.max()), float(err.sum() / max(np.abs(y_ref).sum(), 1e-30)),
+                        int(np.bincount(idx_np.ravel(), minlength=E).max())))
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump({"res": res}, f)
+    finally:
+        if moe is not None:
+            moe.close()
+        dist.destroy_process_group()
