@@ -243,6 +243,13 @@ OXG_API int oxg_ep_close(oxg_ctx *ctx);
  * layer tolerance instead of bit for bit. Set the same value on every process
  * after oxg_ep_connect. */
 OXG_API int oxg_ep_set_decode_tokens(oxg_ctx *ctx, int tokens);
+/* Failure detection (no counterpart in the reference): every wait of an
+ * expert-parallel forward on another process's flag gives up after `seconds`
+ * (default ~2 s of SM clock; at least 1e-4) and the forward then reports
+ * OXG_ERR_TIMEOUT at the next oxg_sync, the context still usable. A process
+ * that stops taking part (it left, or skips a step) is found this way. Set
+ * after oxg_ep_init. */
+OXG_API int oxg_ep_set_wait_budget(oxg_ctx *ctx, double seconds);
 /* Rows this process received in its last oxg_moe_forward_ep (waits for it). */
 OXG_API int oxg_ep_last_received(oxg_ctx *ctx, long long *rows);
 

@@ -97,6 +97,7 @@ SIGNATURES = {
     "oxg_moe_forward_ep": (_I, [_CTX, _I, _P, _I, _P]),
     "oxg_ep_close": (_I, [_CTX]),
     "oxg_ep_set_decode_tokens": (_I, [_CTX, _I]),
+    "oxg_ep_set_wait_budget": (_I, [_CTX, ctypes.c_double]),
     "oxg_ep_last_received": (_I, [_CTX, ctypes.POINTER(ctypes.c_longlong)]),
     "oxg_model_init": (_I, [_CTX, ctypes.POINTER(ModelDims)]),
     "oxg_model_upload_embeddings": (_I, [_CTX, _P, _P, _P]),

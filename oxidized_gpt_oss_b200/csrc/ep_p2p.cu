@@ -36,7 +36,7 @@ namespace oxg {
 namespace {
 
 constexpr uint32_t kPoison = 0x80000000u;
-constexpr long long kEpWaitCycles = 4000000000LL;
+constexpr long long kEpWaitCycles = 4000000000LL;  // the default budget (~2 s of SM clock)
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -78,7 +78,7 @@ __device__ bool wait_flags(const EpLayout &L, const EpPeers &P, int kind, uint32
         }
         break;
       }
-      if (clock64() - t0 > kEpWaitCycles) {
+      if (clock64() - t0 > L.wait_cycles) {
         ok = false;
         atomicCAS(err, 0, code);
         break;
@@ -263,6 +263,7 @@ EpLayout ep_layout(int W, int E, int H, int k, int rank, long long max_tokens, l
   L.per = W > 0 ? E / W : 0;
   L.max_tokens = max_tokens;
   L.max_recv = max_recv;
+  L.wait_cycles = kEpWaitCycles;
   auto up = [](size_t v) { return (v + 255) / 256 * 256; };
   size_t off = 0;
   L.off_flags = off;

@@ -283,6 +283,7 @@ constexpr int kEpMaxSegments = 256;
 struct EpLayout {
   int W, E, H, k, rank, per;
   long long max_tokens, max_recv;
+  long long wait_cycles;  // budget of every wait on another rank's flag (SM clock cycles)
   size_t off_flags, off_inbox, off_recv_scale, off_recv_rows, off_ret_rows, bytes;
 };
 struct EpPeers {

@@ -17,17 +17,23 @@
 // definitions apply: RoPE on the two halves of each head (x1 = d < 32,
 // x2 = d >= 32) with angles pos * theta^(-2i/hd) from host-built tables;
 // one learned sink logit per head that joins the softmax denominator only.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <math.h>
+
+#include <algorithm>
 
 #include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "model.h"
+#include "sm100.cuh"
 
 namespace oxg {
 namespace {
+
+using namespace sm100;
 
 // ---------------------------------------------------------------------------
 // bf16 helpers local to this file
@@ -599,17 +605,273 @@ __global__ void __launch_bounds__(kDecThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Batched decode attention on the tensor cores: one query token of each of T
+// sequences, G = 8 query heads per kv head. A work item is (token, kv head,
+// split of kAdKeys keys); every warp streams its own items (item ids gw,
+// gw + W, ... over the grid's W warps) through a ring of kAdStages K + V
+// tiles of 64 keys, which its lane 0 loads by TMA from the KV cache's tensor
+// map (128-byte swizzle, so the ldmatrix phases hit distinct banks) while the
+// warp computes the previous tiles:
+//   S^T (64 keys x 8 heads) = K Q^T    mma m16n8k16, keys as M, heads as N
+//   online softmax per head (a column), P^T moved into the B-operand layout
+//   with movmatrix, as a bf16 hi + lo pair (~16 significant bits, like the
+//   prefill kernel)
+//   O^T (64 dims x 8 heads) += V^T P^T
+// Each item's per-head (max, sum, unnormalised output) go to the partials
+// the combine kernel merges with kAdKeys keys per split. Keys past the
+// item's end are masked in S, and their V rows zeroed in shared memory (the
+// cache rows there may hold anything). Every wait is bounded: a timeout
+// records code 61 in *err and the warp drains its loads and stops.
+// ---------------------------------------------------------------------------
+constexpr int kAdWarps = 4;
+constexpr int kAdStages = 3;
+constexpr int kAdTile = 64;
+constexpr int kAdKeys = 4 * kAdTile;
+constexpr uint32_t kAdTileBytes = kAdTile * 128;  // one K or V tile: 64 rows of 64 bf16
+constexpr size_t kAdSmem = (size_t)kAdWarps * kAdStages * 2 * kAdTileBytes + 1024;
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+struct AdItem {
+  int t, kvh, sp, n_split, key0, nk;  // nk keys from position key0 of sequence t
+};
+
+// Item idx = (t * max_split + sp) * nkv + kvh; false past sequence t's splits.
+__device__ __forceinline__ bool ad_item(int idx, int nkv, int max_split, const int32_t *tok_pos, int window,
+                                        AdItem &it) {
+  it.kvh = idx % nkv;
+  const int r = idx / nkv;
+  it.sp = r % max_split;
+  it.t = r / max_split;
+  const int p = tok_pos[it.t];
+  const int lo = window > 0 ? max(0, p - window + 1) : 0;
+  it.n_split = (p - lo + kAdKeys) / kAdKeys;
+  if (it.sp >= it.n_split) return false;
+  it.key0 = lo + it.sp * kAdKeys;
+  it.nk = min(kAdKeys, p + 1 - it.key0);
+  return true;
+}
+
+struct AdCursor {
+  int idx, tile, n_tiles;
+  AdItem it;
+};
+
+// Moves c to the first tile of the next item at or after c.idx (stride W).
+__device__ __forceinline__ bool ad_seek(AdCursor &c, int W, int n_items, int nkv, int max_split,
+                                        const int32_t *tok_pos, int window) {
+  for (; c.idx < n_items; c.idx += W)
+    if (ad_item(c.idx, nkv, max_split, tok_pos, window, c.it)) {
+      c.tile = 0;
+      c.n_tiles = (c.it.nk + kAdTile - 1) / kAdTile;
+      return true;
+    }
+  return false;
+}
+
+__global__ void __launch_bounds__(kAdWarps * 32, 1)
+    attn_decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const uint16_t *__restrict__ q,
+                           const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_row0,
+                           long long k_row, long long v_row, long long kv_stride, int nkv, int Nq, int window,
+                           float scale, int max_split, int n_items, float *__restrict__ part, size_t part_tok,
+                           int *err) {
+  extern __shared__ __align__(16) uint8_t ad_raw[];
+  __shared__ __align__(8) uint64_t bars[kAdWarps][kAdStages];
+  uint8_t *smem = ad_raw + ((1024 - (smem_addr(ad_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, qd = lane & 3;
+  uint8_t *ring = smem + (size_t)warp * kAdStages * 2 * kAdTileBytes;
+  uint64_t *bar = bars[warp];
+  if (lane == 0) {
+    for (int s = 0; s < kAdStages; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+    prefetch_tmap(&kv_map);
+  }
+  __syncwarp();
+  const int W = gridDim.x * kAdWarps, gw = blockIdx.x * kAdWarps + warp;
+
+  // producer: lane 0 issues the K and V tiles at the producer cursor
+  AdCursor pc;
+  pc.idx = gw;
+  bool p_ok = ad_seek(pc, W, n_items, nkv, max_split, tok_pos, window);
+  int issued = 0;
+  auto issue = [&]() {
+    const int s = issued % kAdStages;
+    if (lane == 0) {
+      const long long r = (long long)pc.it.kvh * kv_stride + tok_row0[pc.it.t] + pc.it.key0 + pc.tile * kAdTile;
+      uint8_t *ks = ring + (size_t)s * 2 * kAdTileBytes;
+      mbar_arrive_expect_tx(&bar[s], 2 * kAdTileBytes);
+      tma_load_2d(ks, &kv_map, &bar[s], 0, (int)(k_row + r));
+      tma_load_2d(ks + kAdTileBytes, &kv_map, &bar[s], 0, (int)(v_row + r));
+    }
+    ++issued;
+    if (++pc.tile == pc.n_tiles) {
+      pc.idx += W;
+      p_ok = ad_seek(pc, W, n_items, nkv, max_split, tok_pos, window);
+    }
+  };
+  for (int i = 0; i < kAdStages && p_ok; ++i) issue();
+
+  AdCursor cc;
+  cc.idx = gw;
+  bool c_ok = ad_seek(cc, W, n_items, nkv, max_split, tok_pos, window);
+  int consumed = 0;
+  bool failed = false;
+  while (c_ok && !failed) {
+    const AdItem it = cc.it;
+    // Q^T as B operands: head g of the group, dims db * 16 + 2qd (+1) and + 8
+    const uint16_t *qh = q + (size_t)it.t * Nq + (size_t)(it.kvh * 8 + g) * 64 + 2 * qd;
+    uint32_t qf[4][2];
+#pragma unroll
+    for (int db = 0; db < 4; ++db) {
+      qf[db][0] = *reinterpret_cast<const uint32_t *>(qh + db * 16);
+      qf[db][1] = *reinterpret_cast<const uint32_t *>(qh + db * 16 + 8);
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2qd, 2qd + 1
+    float o[4][4];
+#pragma unroll
+    for (int mb = 0; mb < 4; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
+
+    for (; cc.tile < cc.n_tiles; ++cc.tile) {
+      const int s = consumed % kAdStages;
+      if (!mbar_wait(&bar[s], (uint32_t)(consumed / kAdStages) & 1u, err, 61)) {
+        failed = true;
+        break;
+      }
+      uint8_t *ks = ring + (size_t)s * 2 * kAdTileBytes;
+      uint8_t *vs = ks + kAdTileBytes;
+      const int nkt = min(kAdTile, it.nk - cc.tile * kAdTile);  // valid keys in this tile
+      if (nkt < kAdTile) {  // zero the V rows past the end (whole 128-byte rows)
+        for (int c = nkt * 8 + lane; c < kAdTile * 8; c += 32)
+          *reinterpret_cast<uint4 *>(vs + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+      }
+      // S^T = K Q^T per block of 16 keys
+      float sc[4][4];
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        sc[kb][0] = sc[kb][1] = sc[kb][2] = sc[kb][3] = 0.f;
+#pragma unroll
+        for (int db = 0; db < 4; ++db) {
+          const int row = kb * 16 + (lane & 15), ch = db * 2 + (lane >> 4);
+          uint32_t a[4];
+          ldmatrix_x4(a, ks + row * 128 + ((ch ^ (row & 7)) << 4));
+          mma_bf16_16816(sc[kb], a, qf[db][0], qf[db][1]);
+        }
+      }
+      // scale, mask, running max per head
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        const int ka = kb * 16 + g, kb8 = ka + 8;
+        sc[kb][0] = ka < nkt ? sc[kb][0] * scale : -INFINITY;
+        sc[kb][1] = ka < nkt ? sc[kb][1] * scale : -INFINITY;
+        sc[kb][2] = kb8 < nkt ? sc[kb][2] * scale : -INFINITY;
+        sc[kb][3] = kb8 < nkt ? sc[kb][3] * scale : -INFINITY;
+        mx0 = fmaxf(mx0, fmaxf(sc[kb][0], sc[kb][2]));
+        mx1 = fmaxf(mx1, fmaxf(sc[kb][1], sc[kb][3]));
+      }
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: the tile has a key
+      const float al0 = expf(m0 - mn0), al1 = expf(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        sc[kb][0] = expf(sc[kb][0] - mn0);
+        sc[kb][1] = expf(sc[kb][1] - mn1);
+        sc[kb][2] = expf(sc[kb][2] - mn0);
+        sc[kb][3] = expf(sc[kb][3] - mn1);
+        rs0 += sc[kb][0] + sc[kb][2];
+        rs1 += sc[kb][1] + sc[kb][3];
+      }
+      l0 = l0 * al0 + rs0;
+      l1 = l1 * al1 + rs1;
+#pragma unroll
+      for (int mb = 0; mb < 4; ++mb) {
+        o[mb][0] *= al0;
+        o[mb][1] *= al1;
+        o[mb][2] *= al0;
+        o[mb][3] *= al1;
+      }
+      // O^T += V^T P^T per block of 16 keys
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        const uint32_t x0 = pack_bf16x2(sc[kb][0], sc[kb][1]);  // key g: heads 2qd, 2qd + 1
+        const uint32_t x1 = pack_bf16x2(sc[kb][2], sc[kb][3]);  // key g + 8
+        const uint32_t y0 = pack_bf16x2(sc[kb][0] - __uint_as_float(x0 << 16),
+                                        sc[kb][1] - __uint_as_float(x0 & 0xFFFF0000u));
+        const uint32_t y1 = pack_bf16x2(sc[kb][2] - __uint_as_float(x1 << 16),
+                                        sc[kb][3] - __uint_as_float(x1 & 0xFFFF0000u));
+        const uint32_t b0h = movmatrix_trans(x0), b1h = movmatrix_trans(x1);  // head g: keys 2qd.., 2qd + 8..
+        const uint32_t b0l = movmatrix_trans(y0), b1l = movmatrix_trans(y1);
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) {
+          const int key = kb * 16 + (lane & 7) + ((lane >> 4) << 3), ch = mb * 2 + ((lane >> 3) & 1);
+          uint32_t a[4];
+          ldmatrix_x4_trans(a, vs + key * 128 + ((ch ^ (key & 7)) << 4));
+          mma_bf16_16816(o[mb], a, b0h, b1h);
+          mma_bf16_16816(o[mb], a, b0l, b1l);
+        }
+      }
+      // every lane is done with the stage (and its zeroed V rows are ordered
+      // before the next TMA write into it)
+      if (nkt < kAdTile) fence_proxy_async_smem();
+      __syncwarp();
+      ++consumed;
+      if (p_ok) issue();
+    }
+    if (failed) break;
+    // the item's partials: sums over the quad columns' eight key rows
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    float *dst = part + (size_t)it.t * part_tok + (size_t)(it.kvh * it.n_split + it.sp) * 8 * 66;
+    float *d0 = dst + (2 * qd) * 66, *d1 = d0 + 66;
+#pragma unroll
+    for (int mb = 0; mb < 4; ++mb) {
+      d0[2 + mb * 16 + g] = o[mb][0];
+      d1[2 + mb * 16 + g] = o[mb][1];
+      d0[2 + mb * 16 + g + 8] = o[mb][2];
+      d1[2 + mb * 16 + g + 8] = o[mb][3];
+    }
+    if (g == 0) {
+      d0[0] = m0;
+      d0[1] = l0;
+      d1[0] = m1;
+      d1[1] = l1;
+    }
+    cc.idx += W;
+    c_ok = ad_seek(cc, W, n_items, nkv, max_split, tok_pos, window);
+  }
+  // after a timeout: the loads still in flight land before the CTA exits
+  for (; consumed < issued; ++consumed)
+    if (!mbar_wait(&bar[consumed % kAdStages], (uint32_t)(consumed / kAdStages) & 1u, err, 61)) break;
+}
+
 // One CTA of 64 threads per (query head, token): merges the decode splits and
 // the sink.
 __global__ void __launch_bounds__(64)
     attn_combine_kernel(const float *__restrict__ part, int G, int n_split, const int32_t *__restrict__ pos_dev,
                         int window, const uint16_t *__restrict__ sinks, uint16_t *__restrict__ out,
-                        const int32_t *__restrict__ tok_pos, int Nq, size_t part_tok) {
+                        const int32_t *__restrict__ tok_pos, int Nq, size_t part_tok, int keys_per_split) {
   const int h = blockIdx.x, kvh = h / G, hl = h % G, d = threadIdx.x;
   if (pos_dev || tok_pos) {
     const int t = blockIdx.y;
     const int hi = tok_pos ? tok_pos[t] : *pos_dev, lo = window > 0 ? max(0, hi - window + 1) : 0;
-    n_split = (hi - lo + kDecKeys) / kDecKeys;
+    n_split = (hi - lo + keys_per_split) / keys_per_split;
     if (tok_pos) {
       part += (size_t)t * part_tok;
       out += (size_t)t * Nq;
@@ -938,6 +1200,26 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
   const int G = a.nh / a.nkv;
   const int Nq = a.nh * 64;
   const int rows = a.split_rows > 0 ? a.split_rows : a.max_seq;  // positions of one sequence
+  if (a.tok_pos && a.kv_map && G == 8 && a.n_sms > 0) {  // one query of each of T sequences, tensor cores
+    const size_t part_tok = attn_part_floats(a.nkv, G, rows);
+    // the longest span in keys (an upper bound from the 64-key split count)
+    const int span = a.window > 0 && a.window < rows ? std::min(a.window, a.max_splits * kDecKeys)
+                                                     : a.max_splits * kDecKeys;
+    const int max_split = (span + kAdKeys - 1) / kAdKeys;
+    if (max_split <= 0 || a.max_splits > attn_decode_splits(rows)) return cudaErrorInvalidValue;
+    const int n_items = a.T * max_split * a.nkv;
+    const int grid = std::min((n_items + kAdWarps - 1) / kAdWarps, a.n_sms);
+    cudaError_t st = cudaFuncSetAttribute(attn_decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kAdSmem);
+    if (st != cudaSuccess) return st;
+    attn_decode_mma_kernel<<<grid, kAdWarps * 32, kAdSmem, stream>>>(
+        *reinterpret_cast<const CUtensorMap *>(a.kv_map), a.q, a.tok_pos, a.tok_row0, a.k_row, a.v_row,
+        (long long)a.max_seq, a.nkv, Nq, a.window, a.scale, max_split, n_items, a.part, part_tok, a.err);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, max_split, nullptr, a.window, a.sinks,
+                                                           a.out, a.tok_pos, Nq, part_tok, kAdKeys);
+    return cudaGetLastError();
+  }
   if (a.tok_pos) {  // one query of each of T sequences
     const size_t part_tok = attn_part_floats(a.nkv, G, rows);
     const int window_splits = attn_decode_splits(a.window > 0 && a.window < rows ? a.window : rows);
@@ -949,7 +1231,7 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, grid_split, nullptr, a.window, a.sinks,
-                                                           a.out, a.tok_pos, Nq, part_tok);
+                                                           a.out, a.tok_pos, Nq, part_tok, kDecKeys);
     return cudaGetLastError();
   }
   if (a.T == 1) {
@@ -964,7 +1246,7 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     attn_combine_kernel<<<a.nh, 64, 0, stream>>>(a.part, G, grid_split, a.pos_dev, a.window, a.sinks, a.out,
-                                                 nullptr, Nq, 0);
+                                                 nullptr, Nq, 0, kDecKeys);
     return cudaGetLastError();
   }
   attn_prefill_kernel<<<dim3((a.T + kAttQ - 1) / kAttQ, a.nh), 128, 0, stream>>>(
@@ -977,6 +1259,32 @@ size_t attn_part_floats(int nkv, int G, int max_seq) {
 }
 
 int attn_max_group() { return kMaxGroup; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+cudaError_t make_kv_map(void *map, const uint16_t *kv, long long rows) {
+  if (!map || !kv || ((uintptr_t)kv & 15) || rows <= 0 || rows >= (1LL << 31)) return cudaErrorInvalidValue;
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return cudaErrorNotSupported;
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  // rows of 64 bf16 (128 bytes); boxes of 64 rows with the 128-byte swizzle
+  const cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kAdTile};
+  const cuuint32_t es[2] = {1u, 1u};
+  CUresult r = fn(reinterpret_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<uint16_t *>(kv), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *next, int32_t *state, int32_t *out_seq,
                           cudaStream_t stream) {

@@ -71,7 +71,18 @@ struct AttnArgs {
   float *part = nullptr;         // decode split partials (attn_part_floats per query token)
   const int32_t *pos_dev = nullptr;  // T == 1: the query position read on the device (graph replays)
   uint16_t *out = nullptr;       // [T, nh * 64] bf16
+  // with tok_pos and G = 8: the tensor-core decode kernel, which loads K / V
+  // tiles through kv_map (a CUtensorMap over the whole KV cache, make_kv_map);
+  // k_row / v_row are the map rows of this layer's K and V caches (kv head 0,
+  // cache row 0)
+  const void *kv_map = nullptr;
+  long long k_row = 0, v_row = 0;
+  int n_sms = 0;
+  int *err = nullptr;            // timeout code of the tensor-core decode kernel
 };
+// A 2-D tensor map over the KV cache `kv` of `rows` rows of 64 bf16 (128-byte
+// swizzle, 64-row boxes) into map (128 bytes, 64-byte aligned); rows < 2^31.
+cudaError_t make_kv_map(void *map, const uint16_t *kv, long long rows);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream);
 size_t attn_part_floats(int nkv, int G, int max_seq);
 int attn_max_group();

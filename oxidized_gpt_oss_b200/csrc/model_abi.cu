@@ -44,6 +44,10 @@ struct ModelState {
   std::vector<Attn> layers;
   void *state = nullptr;
   uint16_t *kv = nullptr;
+  // a tensor map (CUtensorMap) over the whole KV cache for the batched decode
+  // attention's TMA loads; kv_map_ok false: the cache is too large for one
+  alignas(64) unsigned char kv_map[128] = {};
+  bool kv_map_ok = false;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float *res = nullptr, *part = nullptr, *y = nullptr, *apart = nullptr, *logits = nullptr;
   uint16_t *xn = nullptr, *qb = nullptr, *cb = nullptr;
@@ -298,6 +302,13 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     at.sinks = A.sinks;
     at.part = M.apart;
     at.pos_dev = dstate;
+    if (batch && M.kv_map_ok) {
+      at.kv_map = M.kv_map;
+      at.k_row = (long long)l * 2 * d.n_kv_heads * (long long)M.kv_stride;
+      at.v_row = at.k_row + (long long)d.n_kv_heads * (long long)M.kv_stride;
+      at.n_sms = n_sms;
+      at.err = M.err;
+    }
     at.out = M.cb;
     MCUDA(ctx, ctx_launch(ctx, "attention", [&] { return launch_attention(at, s); }), "attention launch");
     const int s_o = linear_splits(H, M.Nq, T, n_sms, M.part_rows);
@@ -487,6 +498,8 @@ int model_check_error(oxg_ctx *ctx) {
   MCUDA(ctx, cudaMemcpy(&h, M->err, sizeof(int), cudaMemcpyDeviceToHost), "read model status");
   if (h) {
     MCUDA(ctx, cudaMemset(M->err, 0, sizeof(int)), "clear model status");
+    if (h == 61)
+      return mfail(ctx, OXG_ERR_TIMEOUT, "a KV tile load of the decode attention did not complete (code 61)");
     return mfail(ctx, OXG_ERR_INVALID_ARG, "a token id outside [0, vocab = %d) was given (code %d)", M->d.vocab, h);
   }
   return OXG_OK;
@@ -585,6 +598,8 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
     oxg::free_model(M);
     return oxg::mcuda(ctx, e, "model state initialisation");
   }
+  M->kv_map_ok = oxg::make_kv_map(M->kv_map, M->kv,
+                                  (long long)d.n_layers * 2 * d.n_kv_heads * (long long)M->kv_stride) == cudaSuccess;
   oxg::ctx_model(ctx) = M;
   return OXG_OK;
 }

@@ -1618,6 +1618,18 @@ int oxg_ep_set_decode_tokens(oxg_ctx *ctx, int tokens) {
   return OXG_OK;
 }
 
+int oxg_ep_set_wait_budget(oxg_ctx *ctx, double seconds) {
+  if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  auto &q = ctx->p2p;
+  if (!q.init) return fail(ctx, OXG_ERR_STATE, "oxg_ep_init first");
+  if (!(seconds >= 1e-4) || seconds > 60.0)
+    return fail(ctx, OXG_ERR_INVALID_ARG, "the wait budget must be in [1e-4, 60] seconds, got %g", seconds);
+  int khz = 0;
+  OXG_CUDA(ctx, cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, ctx->device), "cudaDeviceGetAttribute");
+  q.lay.wait_cycles = (long long)(seconds * 1e3 * (double)(khz > 0 ? khz : 2000000));
+  return OXG_OK;
+}
+
 int oxg_ep_close(oxg_ctx *ctx) {
   if (!ctx) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
   DeviceGuard g(ctx->device);

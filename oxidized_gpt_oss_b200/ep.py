@@ -139,6 +139,13 @@ class PeerExpertParallelMoE:
                                                  out.data_ptr() if T else None), c.handle)
         return out
 
+    def set_wait_budget(self, seconds: float) -> None:
+        """Every wait of a forward on another rank's flag gives up after
+        ``seconds`` (default ~2 s): a rank that skips a step, or stopped,
+        then shows as OXG_ERR_TIMEOUT at the next synchronisation, with the
+        context still usable."""
+        self._abi.check(self._ctx.lib.oxg_ep_set_wait_budget(self._ctx.handle, float(seconds)), self._ctx.handle)
+
     def last_received(self) -> int:
         """Rows this rank received in the last forward (waits for it)."""
         import ctypes

@@ -245,3 +245,87 @@ def gpu_p2p_grouped_worker(rank, world, port, layer_kw, tokens, hot, out_dir):
         if moe is not None:
             moe.close()
         dist.destroy_process_group()
+
+
+def gpu_timeout_worker(rank, world, port, out_dir):
+    """Failure detection without a GPU fault. Both ranks connect a peer-memory
+    exchange (gloo carries the handles; with one GPU both processes share it
+    and only rank 0 ever launches a kernel that waits). With two GPUs both
+    first run one forward together. Then rank 1 skips a step: rank 0's
+    forward waits on flags nothing sets, gives up after the 50 ms budget and
+    reports OXG_ERR_TIMEOUT at the synchronisation; rank 0's context then
+    still runs the whole layer."""
+    import time
+    n_dev = torch.cuda.device_count()
+    torch.cuda.set_device(rank % n_dev)
+    _init(rank, world, port, "gloo")
+    moe = None
+    out = {}
+    try:
+        from oxidized_gpt_oss_b200 import abi
+        from oxidized_gpt_oss_b200.moe import MoELayer
+        d = synth.moe_layer(seed=41, hidden=256, intermediate=256, n_experts=16, top_k=4)
+        begin, count = ep.shard_range(16, world, rank)
+        shard = MoELayer(d, experts=(begin, count))
+        moe = ep.PeerExpertParallelMoE(shard, max_tokens=64)
+        x = torch.from_numpy(synth.activations(300 + rank, 48, 256).view(np.int16)).cuda()
+        full = MoELayer(d) if rank == 0 else None
+        y_ref = full.forward(x).clone() if full else None
+        if n_dev >= world:  # a good step on separate GPUs first
+            y = moe(x).clone()
+            shard.ctx.sync()
+            out["first_step_equal"] = bool(torch.equal(y, y_ref)) if full else True
+        dist.barrier()
+        if rank == 0:
+            moe.set_wait_budget(0.05)
+            t0 = time.perf_counter()
+            status = 0
+            try:
+                moe(x)
+                shard.ctx.sync()
+            except abi.OxgError as e:
+                status = e.status
+                out["message"] = e.message
+            out["status"] = status
+            out["seconds"] = time.perf_counter() - t0
+            y2 = full.forward(x)
+            full.ctx.sync()
+            out["usable_after"] = bool(torch.equal(y2, y_ref))
+        dist.barrier()  # rank 1 skipped the step: it waits here, on the host
+    finally:
+        if moe is not None:
+            moe.close()
+        with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+            pickle.dump(out, f)
+        dist.destroy_process_group()
+
+
+def cpu_leave_worker(rank, world, port, out_dir):
+    """A rank that leaves between steps: after one step together rank 1 exits
+    (no collective in flight). Rank 0's next step fails in its first
+    collective instead of hanging (the process group's 10 s timeout bounds it
+    even where the backend does not notice the closed connection)."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    d = synth.moe_layer(seed=42, hidden=64, intermediate=64, n_experts=4, top_k=2)
+    begin, count = ep.shard_range(4, world, rank)
+    moe = ep.ExpertParallelMoE(NumpyShard(d, begin, count))
+    x = torch.from_numpy(synth.activations(400 + rank, 5, 64).view(np.int16))
+    moe(x)
+    if rank == 1:
+        return  # leaves between steps: the process exits
+    out = {"raised": None}
+    t0 = time.perf_counter()
+    try:
+        moe(x)
+    except Exception as e:  # the backend's error for a lost peer or a timeout
+        out["raised"] = type(e).__name__
+    out["seconds"] = time.perf_counter() - t0
+    with open(os.path.join(out_dir, "rank0.pkl"), "wb") as f:
+        pickle.dump(out, f)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass

@@ -49,3 +49,14 @@ def test_two_ranks_match_single_process(tmp_path, bias_rank0):
         assert np.allclose(got["y"], ref, rtol=1e-5, atol=1e-6), np.abs(got["y"] - ref).max()
         if bias_rank0:  # nothing goes to rank 1's experts
             assert got["splits"][0][1] == 0
+
+
+def test_rank_that_leaves_between_steps_is_reported(tmp_path):
+    """Failure detection on the host: after one step together, rank 1 exits
+    between steps; rank 0's next step raises from its first collective within
+    the process group's timeout instead of hanging."""
+    mp.spawn(ep_workers.cpu_leave_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    with open(os.path.join(tmp_path, "rank0.pkl"), "rb") as f:
+        got = pickle.load(f)
+    assert got["raised"] is not None, "the step with a departed rank did not fail"
+    assert got["seconds"] < 30.0, got
