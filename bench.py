@@ -2,15 +2,18 @@
 """Benchmark of the MXFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_prefill|moe_decode|dequant|model_decode] [--tokens T] [--layers L]
+                    [--workload moe_prefill|moe_decode|dequant|model_decode|model_batch|tensor_peak]
+                    [--tokens T] [--layers L]
 
 Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
   moe_prefill (default) 8192 tokens per GPU through one MoE block on the
               tcgen05 grouped-GEMM path (router logits ~N(0, 1), so expert
               loads are roughly uniform). Metric: tokens/s; roofline: TFLOP/s
               of the gate/up GEMM against the measured dense 16-bit tensor
-              peak. On N GPUs the experts are split 32/N per GPU (expert
-              parallel) with NCCL all-to-all dispatch and return; on one GPU
+              peak, and beside it the dense MXFP4 (kind::mxf4) rate measured
+              in the same run. On N GPUs the experts are split 32/N per GPU
+              (expert parallel; rows exchanged over NVLink peer memory, or
+              NCCL all-to-all with --ep nccl); on one GPU
               the line also carries a "decode" object (the moe_decode
               workload measured in the same process) and a "model_decode"
               object (the model_decode workload, 64 timed steps).
@@ -28,6 +31,12 @@ Workloads (seeded synthetic inputs, random-init gpt-oss-20b shapes):
   dequant     standalone MXFP4 -> bf16 dequant of one layer's expert tensors
               (32x5760x2880 + 32x2880x2880, E8M0 in [110, 135]). Metric: GB/s
               of algorithmic traffic (423,014,400 B read + 1,592,524,800 B written).
+  model_batch  64 sequences at KV length 8192 over the 24-layer model,
+              Zipf-skewed expert loads, one batched greedy step per timed
+              step (expert parallel over N GPUs under torchrun).
+  tensor_peak  issue rate of tcgen05 kind::f16, kind::mxf8f6f4 (E2M1 x E4M3)
+              and kind::mxf4 (E2M1 x E2M1) MMAs, one CTA per SM, from shared
+              memory: the measured tensor denominators.
 
 Steps cycle over L uploaded layers (default 4 x 424 MB of packed weights), so
 inputs are larger than L2 and no step finds the previous step's weights
@@ -78,6 +87,17 @@ def tensor_peak():
         return float(p["bf16_tflops"]), "measured"
     except Exception:
         return FALLBACK_TFLOPS, "fallback"
+
+
+MMA_KINDS = (("f16", "tcgen05.mma.kind::f16, f16 x f16 -> f32, M128 N256 K16"),
+             ("mxf8f6f4", "tcgen05.mma.kind::mxf8f6f4.block_scale, E2M1 x E4M3, UE8M0, M128 N256 K32"),
+             ("mxf4", "tcgen05.mma.kind::mxf4.block_scale.block32, E2M1 x E2M1, UE8M0, M128 N256 K64"))
+
+
+def mma_rates(ctx, iters: int = 65536, repeats: int = 3):
+    """Measured tensor-core issue rate (TFLOP/s, best of `repeats`) of each
+    instruction kind, one CTA per SM issuing back to back from shared memory."""
+    return {name: max(ctx.mma_rate(k, iters) for _ in range(repeats)) for k, (name, _) in enumerate(MMA_KINDS)}
 
 
 def ncu_traffic(kernel: str, key: str):
@@ -573,7 +593,8 @@ def run_prefill(args, ws, rank, local):
     count_rows[0] = False
     rows_profiled = rows_done[0]
     names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
-             "moe_mlp2_prefill", "scatter_e4m3", "gather_e4m3", "mxf_gemm1", "mxf_gemm2", "combine")
+             "moe_mlp2_prefill", "scatter_e4m3", "gather_e4m3", "mxf_gemm1", "mxf_gemm2", "combine",
+             "ep_counts", "ep_wait", "ep_scatter", "ep_signal", "ep_segments")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     mxf = "mxf_gemm1" in k_ms
@@ -588,6 +609,7 @@ def run_prefill(args, ws, rank, local):
     rows_per_step = rows_profiled / args.steps
     flop1, flop2 = f1_row * rows_per_step, f2_row * rows_per_step
     peak, peak_kind = tensor_peak()
+    rates = mma_rates(ctx) if ws == 1 else None
     m1_ms, m1_n = k_ms[k1]
     m2_ms, m2_n = k_ms[k2]
     achieved = f1_row * rows_profiled / (m1_ms * 1e-3) / 1e12
@@ -628,7 +650,10 @@ def run_prefill(args, ws, rank, local):
                         "traffic": ncu_traffic(k1, f"T{T}") if ws == 1 else None,
                         "algorithmic_flop_per_launch": flop1,
                         "flop_per_unit": f1_row, "unit_of_work": "expert row (token, slot)",
-                        "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3},
+                        "avg_launch_us": m1_ms / max(m1_n, 1) * 1e3,
+                        # the dense MXFP4 tensor rate measured in this run (kind::mxf4, E2M1 x E2M1)
+                        "mxfp4_peak": rates["mxf4"] if rates else None,
+                        "frac_of_mxfp4_peak": achieved / rates["mxf4"] if rates else None},
            "e2e": {"value": T * ws * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
            "gpu_launches": launches,
@@ -665,6 +690,32 @@ def run_prefill(args, ws, rank, local):
         ctx.sync()
         out["parity"] = oracle_parity(d0, xs_np[0], y0.cpu().numpy(), idx0.cpu().numpy(), w0.cpu().numpy(),
                                       lg0.cpu().numpy(), n_sample=32, seed=T)
+    return out
+
+
+def run_tensor_peak(args, ws, rank, local):
+    """Issue rate of the tensor-core instruction kinds the MoE kernels use
+    (and the dense MXFP4 one), measured on this GPU: the denominators of the
+    prefill GEMMs' tensor roofline beside the cuBLAS bf16 figure."""
+    import torch
+    from oxidized_gpt_oss_b200 import abi
+    ctx = abi.Context(local)
+    for k in range(len(MMA_KINDS)):  # warm-up
+        ctx.mma_rate(k, 4096)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        rates = mma_rates(ctx, iters=max(65536, args.steps * 4096), repeats=max(args.warmup, 3))
+        barrier(ws)
+    peak, peak_kind = tensor_peak()
+    out = {"metric": "tensor-core issue rate (dense, back to back from shared memory)",
+           "value": rates["mxf4"], "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 x e2m1 (mxf4)",
+           "data": "none (zero tiles in shared memory)",
+           "config": {"workload": "tensor_peak", "ctas": "one per SM", "tile": "M128 N256, one accumulator"},
+           "kinds": {name: {"tflops": rates[name], "instruction": what} for name, what in MMA_KINDS},
+           "bf16_cublas_tflops": {"value": peak, "kind": peak_kind},
+           "clocks": clk.summary(), "gpu_launches": None}
+    ctx.close()
     return out
 
 
@@ -1182,7 +1233,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant", "model_decode", "model_batch"],
+    ap.add_argument("--workload", choices=["moe_decode", "moe_prefill", "dequant", "model_decode", "model_batch",
+                                           "tensor_peak"],
                     default="moe_prefill")
     ap.add_argument("--prompt", type=int, default=None,
                     help="model_decode: prompt tokens (default 2048); model_batch: KV length per sequence (8192)")
@@ -1220,7 +1272,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         run = {"dequant": run_dequant, "moe_prefill": run_prefill, "moe_decode": run_moe,
-               "model_decode": run_model, "model_batch": run_model_batch}[args.workload]
+               "model_decode": run_model, "model_batch": run_model_batch,
+               "tensor_peak": run_tensor_peak}[args.workload]
         out = run(args, ws, rank, local)
         def brief(r):
             # the figures a reader of the line needs, kept short so that the

@@ -390,6 +390,15 @@ OXG_API int oxg_profile_read(oxg_ctx *ctx, const char *name, double *total_ms, i
 OXG_API int oxg_profile_reset(oxg_ctx *ctx);
 /* Number of kernels this context has launched since it was created. */
 OXG_API int oxg_kernel_launches(const oxg_ctx *ctx, long long *count);
+/* Tensor-core issue rate of one instruction kind, measured on this
+ * context's device: one CTA per SM issues `iters` back-to-back MMAs of
+ * M 128 x N 256 from shared memory into TMEM (no global traffic) and the
+ * rate is the algorithmic FLOPs over the launch's CUDA-event time.
+ * kind: 0 = kind::f16 (K 16), 1 = kind::mxf8f6f4.block_scale with E2M1 x
+ * E4M3 (K 32, the block-scaled MoE kernels' instruction), 2 =
+ * kind::mxf4.block_scale with E2M1 x E2M1 (K 64, the dense MXFP4 rate).
+ * Synchronous; *tflops receives TFLOP/s. */
+OXG_API int oxg_measure_mma_rate(oxg_ctx *ctx, int kind, int iters, double *tflops);
 
 #ifdef __cplusplus
 }

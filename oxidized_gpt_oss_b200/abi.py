@@ -115,6 +115,7 @@ SIGNATURES = {
     "oxg_profile_read": (_I, [_CTX, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_int)]),
     "oxg_profile_reset": (_I, [_CTX]),
+    "oxg_measure_mma_rate": (_I, [_CTX, _I, _I, ctypes.POINTER(ctypes.c_double)]),
     "oxg_kernel_launches": (_I, [_CTX, ctypes.POINTER(ctypes.c_longlong)]),
 }
 
@@ -190,6 +191,13 @@ class Context:
         check(self.lib.oxg_profile_read(self.handle, name.encode(), ctypes.byref(ms), ctypes.byref(n)),
               self.handle)
         return ms.value, n.value
+
+    def mma_rate(self, kind: int, iters: int = 65536) -> float:
+        """TFLOP/s of one tensor-core instruction kind issued back to back on
+        every SM (0 kind::f16, 1 kind::mxf8f6f4 E2M1 x E4M3, 2 kind::mxf4)."""
+        v = ctypes.c_double()
+        check(self.lib.oxg_measure_mma_rate(self.handle, int(kind), int(iters), ctypes.byref(v)), self.handle)
+        return v.value
 
     def launches(self) -> int:
         n = ctypes.c_longlong()

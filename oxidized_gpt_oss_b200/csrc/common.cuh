@@ -165,22 +165,136 @@ __device__ __forceinline__ float2 unpack_f16x2(uint32_t v) {
 
 // One bf16 activation row to f16 x * 2^-sigma (exact within the token's
 // range, see router.cu) by one warp; H a multiple of 8, both rows 16-byte
-// aligned.
+// aligned. The lane's loads of up to 12 16-byte chunks (H <= 3072 in one
+// pass) are all issued before the first conversion, so a row costs one
+// memory round trip instead of one per chunk.
 __device__ __forceinline__ void stage_row_f16(const uint16_t *__restrict__ src,
                                               uint16_t *__restrict__ dst, int H, int sigma,
                                               int lane) {
+  constexpr int kPer = 12;
   const float inv = __uint_as_float((uint32_t)(127 - sigma) << 23);
   const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
   uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-  for (int c = lane; c < H / 8; c += 32) {
-    const uint4 v = s4[c];
-    uint4 o;
-    o.x = pack_f16x2(bf16_to_f32(v.x & 0xFFFFu) * inv, bf16_to_f32(v.x >> 16) * inv);
-    o.y = pack_f16x2(bf16_to_f32(v.y & 0xFFFFu) * inv, bf16_to_f32(v.y >> 16) * inv);
-    o.z = pack_f16x2(bf16_to_f32(v.z & 0xFFFFu) * inv, bf16_to_f32(v.z >> 16) * inv);
-    o.w = pack_f16x2(bf16_to_f32(v.w & 0xFFFFu) * inv, bf16_to_f32(v.w >> 16) * inv);
-    d4[c] = o;
+  const int nch = H / 8;
+  for (int c0 = 0; c0 < nch; c0 += 32 * kPer) {
+    uint4 v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = c0 + lane + 32 * i;
+      v[i] = c < nch ? s4[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = c0 + lane + 32 * i;
+      if (c < nch) {
+        uint4 o;
+        o.x = pack_f16x2(bf16_to_f32(v[i].x & 0xFFFFu) * inv, bf16_to_f32(v[i].x >> 16) * inv);
+        o.y = pack_f16x2(bf16_to_f32(v[i].y & 0xFFFFu) * inv, bf16_to_f32(v[i].y >> 16) * inv);
+        o.z = pack_f16x2(bf16_to_f32(v[i].z & 0xFFFFu) * inv, bf16_to_f32(v[i].z >> 16) * inv);
+        o.w = pack_f16x2(bf16_to_f32(v[i].w & 0xFFFFu) * inv, bf16_to_f32(v[i].w >> 16) * inv);
+        d4[c] = o;
+      }
+    }
   }
+}
+
+// Per expert e < E: the slots of e in router CTAs before CTA c (before_s[e])
+// and in all n_cta CTAs (tot_s[e]), from the CTAs' histograms hist[cc, e].
+// All THREADS threads of the block share the n_cta x E loads (independent
+// loads, THREADS / E of them per expert) through part_s (2 x THREADS ints of
+// shared memory); ends with the block synchronised.
+template <int THREADS>
+__device__ __forceinline__ void hist_prefix(const int32_t *__restrict__ hist, int n_cta, int E, int c,
+                                            int *before_s, int *tot_s, int *part_s) {
+  const int parts = THREADS / E;  // E <= THREADS
+  const int tid = threadIdx.x;
+  if (tid < parts * E) {
+    const int e = tid % E, pt = tid / E;
+    int tot = 0, before = 0;
+#pragma unroll 4
+    for (int cc = pt; cc < n_cta; cc += parts) {
+      const int v = hist[(size_t)cc * E + e];
+      tot += v;
+      before += cc < c ? v : 0;
+    }
+    part_s[tid] = tot;
+    part_s[THREADS + tid] = before;
+  }
+  __syncthreads();
+  if (tid < E) {
+    int tot = 0, before = 0;
+    for (int pt = 0; pt < parts; ++pt) {
+      tot += part_s[pt * E + tid];
+      before += part_s[THREADS + pt * E + tid];
+    }
+    tot_s[tid] = tot;
+    before_s[tid] = before;
+  }
+  __syncthreads();
+}
+
+// ----------------------------------------------------------------------------
+// Top-k selection + softmax (MoELayer::forward, src/moe.rs:51-73, softmax_inplace
+// src/utils.rs:91-111)
+// ----------------------------------------------------------------------------
+constexpr int kRankTopKMax = 16;  // k <= 16
+
+// The k largest of the E <= 64 logits of one token (logit_s) in the order of
+// a stable descending sort, by rank counting: the logit of expert e ranks
+// #{e' : v' > v} + #{e' < e : v' == v} (a NaN logit counts as -inf). Lane l
+// holds experts l and l + 32; the 64 comparisons per expert are independent,
+// so the selection costs one pass of broadcasts instead of k rounds of
+// dependent shuffle reductions. Lane 0 then forms the softmax over the k
+// (max-subtracted, sum in j order, uniform if the sum is 0) exactly as
+// select_topk_softmax does.
+__device__ __forceinline__ void rank_topk_softmax(const float *logit_s, int E, int k, int lane,
+                                                  int32_t *__restrict__ idx_out,
+                                                  float *__restrict__ wts_out, int32_t *idx_smem,
+                                                  float *top_v_s, int *top_e_s) {
+  float v0 = lane < E ? logit_s[lane] : -INFINITY;
+  float v1 = lane + 32 < E ? logit_s[lane + 32] : -INFINITY;
+  if (v0 != v0) v0 = -INFINITY;
+  if (v1 != v1) v1 = -INFINITY;
+  int r0 = 0, r1 = 0;
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    const float a = __shfl_sync(0xFFFFFFFFu, v0, l);   // expert l
+    const float b = __shfl_sync(0xFFFFFFFFu, v1, l);   // expert l + 32
+    r0 += (a > v0 || (a == v0 && l < lane)) ? 1 : 0;
+    r0 += b > v0 ? 1 : 0;                               // l + 32 > lane: ties do not count
+    r1 += (a > v1 || a == v1) ? 1 : 0;                  // l < lane + 32: ties count
+    r1 += (b > v1 || (b == v1 && l < lane)) ? 1 : 0;
+  }
+  // experts beyond E (padding at -inf) rank after every real expert
+  if (lane < E && r0 < k) {
+    top_v_s[r0] = v0;
+    top_e_s[r0] = lane;
+  }
+  if (lane + 32 < E && r1 < k) {
+    top_v_s[r1] = v1;
+    top_e_s[r1] = lane + 32;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    float tv[kRankTopKMax];
+    float mx = -INFINITY;
+    for (int j = 0; j < k; ++j) {
+      tv[j] = top_v_s[j];
+      mx = fmaxf(mx, tv[j]);
+    }
+    float sum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      tv[j] = expf(tv[j] - mx);
+      sum += tv[j];
+    }
+    for (int j = 0; j < k; ++j) {
+      const int e = top_e_s[j];
+      idx_out[j] = e;
+      wts_out[j] = sum == 0.f ? 1.0f / (float)k : tv[j] / sum;
+      idx_smem[j] = e;
+    }
+  }
+  __syncwarp();
 }
 
 }  // namespace oxg

@@ -50,6 +50,33 @@ __device__ __forceinline__ uint4 decode8(uint32_t w, float s) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Fast path for one 32-element block whose scale is finite (E8M0 bytes 0..254,
+// bf16 scales with exponent field below 0xFF): each code byte becomes two
+// exact f16 values (cvt.rn.f16x2.e2m1x2), then two exact f32 values, one f32
+// multiply each (the reference's f32 multiply; a finite scale times an E2M1
+// value is never NaN) and one round-to-nearest-even pack of the pair to bf16
+// (cvt.rn.bf16x2.f32, subnormals kept) — the same bits as scaled_code +
+// f32_to_bf16_bits. A non-finite scale takes the exact slow path (NaN rules).
+__device__ __forceinline__ uint32_t bf16x2_of(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint4 decode8_fast(uint32_t w, float s) {
+  uint32_t f[4], o[4];
+  e2m1x8_to_f16x8(w, f);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 v = unpack_f16x2(f[p]);
+    o[p] = bf16x2_of(__fmul_rn(v.x, s), __fmul_rn(v.y, s));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+template <int FMT>
+__device__ __forceinline__ bool scale_finite(float s) {
+  return (__float_as_uint(s) & 0x7F800000u) != 0x7F800000u;
+}
+
 template <int FMT, int UNR>
 __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint32_t *__restrict__ codes,
                                                           const void *__restrict__ scales,
@@ -65,11 +92,14 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint32_t *__rest
       s[u] = load_scale<FMT>(scales, (i + u * stride) >> 2);
     }
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) stg_stream_v4(out + i + u * stride, decode8(w[u], s[u]));
+    for (int u = 0; u < UNR; ++u)
+      stg_stream_v4(out + i + u * stride,
+                    __builtin_expect(scale_finite<FMT>(s[u]), 1) ? decode8_fast(w[u], s[u]) : decode8(w[u], s[u]));
   }
   for (; i < n_q; i += stride) {
-    uint32_t w = ldg_stream_u32(codes + i);
-    stg_stream_v4(out + i, decode8(w, load_scale<FMT>(scales, i >> 2)));
+    const uint32_t w = ldg_stream_u32(codes + i);
+    const float s = load_scale<FMT>(scales, i >> 2);
+    stg_stream_v4(out + i, scale_finite<FMT>(s) ? decode8_fast(w, s) : decode8(w, s));
   }
 }
 

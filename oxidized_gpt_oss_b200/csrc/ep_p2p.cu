@@ -94,15 +94,10 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpLayout L, EpPeers P,
                                                         const int32_t *__restrict__ cta_hist,
                                                         int n_cta, int32_t *counts, int32_t *offsets,
                                                         int *ok_word, uint32_t epoch) {
-  __shared__ int tot_s[kEpMaxExperts];
+  __shared__ int tot_s[kEpMaxExperts], before_s[kEpMaxExperts], part_s[2 * 256];
   if (threadIdx.x == 0) *ok_word = 1;
-  for (int e = threadIdx.x; e < L.E; e += blockDim.x) {
-    int t = 0;
-    for (int c = 0; c < n_cta; ++c) t += cta_hist[(size_t)c * L.E + e];
-    tot_s[e] = t;
-    counts[e] = t;
-  }
-  __syncthreads();
+  hist_prefix<256>(cta_hist, n_cta, L.E, n_cta, before_s, tot_s, part_s);
+  for (int e = threadIdx.x; e < L.E; e += blockDim.x) counts[e] = tot_s[e];
   if (threadIdx.x == 0) {
     int run = 0;
     for (int e = 0; e < L.E; ++e) {
@@ -143,12 +138,13 @@ __global__ void __launch_bounds__(kEpThreads) ep_scatter_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t *in = inbox(L, P);
   const int32_t *mine = in + (size_t)L.rank * L.E;
+  __shared__ int before_s[kEpMaxExperts], tot_s[kEpMaxExperts], part_s[2 * kEpThreads];
   if (threadIdx.x == 0) ok_s = *(volatile int *)ok_word;
+  hist_prefix<kEpThreads>(cta_hist, n_cta, L.E, c, before_s, tot_s, part_s);
   for (int e = threadIdx.x; e < L.E; e += blockDim.x) {
-    int off = 0, before = 0;
+    int off = 0;
     for (int e2 = 0; e2 < e; ++e2) off += mine[e2];
-    for (int cc = 0; cc < c; ++cc) before += cta_hist[(size_t)cc * L.E + e];
-    base_s[e] = off + before;
+    base_s[e] = off + before_s[e];
   }
   for (int d = threadIdx.x; d < L.W; d += blockDim.x) {
     long long b = 0;
@@ -166,23 +162,46 @@ __global__ void __launch_bounds__(kEpThreads) ep_scatter_kernel(
   const int per = (kEpTokens * L.k + kEpSub - 1) / kEpSub;
   const int my_begin = s_begin + sub * per, my_end = min(s_end, my_begin + per);
   bool overflow = false;
-  for (int sl = my_begin + warp; sl < my_end; sl += kEpThreads / 32) {
-    const int e = idx[sl];
-    const int p = base_s[e] + local_rank[sl];
-    if (lane == 0) slot_pos[sl] = p;
-    if (!ok) continue;
-    const int d = e / L.per;
-    const long long drow = dbase_s[d] + (p - doff_s[d]);
-    if (drow >= L.max_recv) {
-      overflow = true;
-      continue;
+  // This warp's slots are my_begin + warp + W i (W warps): their positions,
+  // destinations and sigma are fetched one slot per lane, all at once, then
+  // the rows are stored one after another (one metadata round trip per 32
+  // slots instead of three per slot).
+  constexpr int W = kEpThreads / 32;
+  const int n_mine = my_end - my_begin;
+  const int n_w = n_mine > warp ? (n_mine - warp + W - 1) / W : 0;
+  for (int i0 = 0; i0 < n_w; i0 += 32) {
+    const int li = i0 + lane;
+    const int sl_l = my_begin + warp + W * li;
+    int d_l = -1, sg_l = 0;
+    long long drow_l = 0;
+    if (li < n_w) {
+      const int e = idx[sl_l];
+      const int p = base_s[e] + local_rank[sl_l];
+      slot_pos[sl_l] = p;
+      if (ok) {
+        const int d = e / L.per;
+        const long long drow = dbase_s[d] + (p - doff_s[d]);
+        if (drow >= L.max_recv) {
+          overflow = true;
+        } else {
+          d_l = d;
+          drow_l = drow;
+          sg_l = sigma[sl_l / L.k];
+          reinterpret_cast<float *>(P.base[d] + L.off_recv_scale)[drow] =
+              __uint_as_float((uint32_t)(127 + sg_l) << 23);
+        }
+      }
     }
-    const int t = sl / L.k, sg = sigma[t];
-    char *db = P.base[d];
-    if (lane == 0)
-      reinterpret_cast<float *>(db + L.off_recv_scale)[drow] = __uint_as_float((uint32_t)(127 + sg) << 23);
-    stage_row_f16(x + (size_t)t * L.H, reinterpret_cast<uint16_t *>(db + L.off_recv_rows) + drow * L.H,
-                  L.H, sg, lane);
+    const int n_here = min(32, n_w - i0);
+    for (int j = 0; j < n_here; ++j) {
+      const int d = __shfl_sync(0xFFFFFFFFu, d_l, j);
+      const long long drow = __shfl_sync(0xFFFFFFFFu, drow_l, j);
+      const int sg = __shfl_sync(0xFFFFFFFFu, sg_l, j);
+      if (d < 0) continue;  // the same for every lane of the warp
+      const int t = (my_begin + warp + W * (i0 + j)) / L.k;
+      stage_row_f16(x + (size_t)t * L.H,
+                    reinterpret_cast<uint16_t *>(P.base[d] + L.off_recv_rows) + drow * L.H, L.H, sg, lane);
+    }
   }
   if (overflow) {
     atomicCAS(err, 0, 51);

@@ -256,7 +256,20 @@ struct PrefillIO {
   float *y_slot;                    // [S, H] f32 expert outputs
   float *const *y_seg;              // or per segment: its rows' destination (null: y_slot)
   int *err;                         // pipeline timeout code (0 = none)
+  // GEMM2 with the weighted top-k combine fused (one GPU, y_seg null): the
+  // layer output y [T, H] f32, each token's k slot positions and weights,
+  // the slot of each position, and one arrival counter per (token, 128-row
+  // tile of H), zero on entry and left at zero (comb_mtiles = ceil(H / 128))
+  float *y;
+  const int32_t *perm, *slot_pos;
+  const float *wts;
+  uint32_t *comb_cnt;
+  int topk;
 };
+// 128-row tiles of H: the fused combine's counters per token.
+constexpr int prefill_comb_mtiles(int H) { return (H + 127) / 128; }
+// The fused combine handles top-k up to this (larger k: combine_kernel).
+constexpr int kPrefillCombineMaxK = 4;
 // min over non-zero and max of E8M0 scale bytes into minmax[0..1] (which
 // must hold 255 and 0 on entry).
 cudaError_t launch_scale_range(const uint8_t *scales, size_t n, unsigned *minmax,
@@ -328,5 +341,11 @@ cudaError_t launch_ep_decode(const MoeDeviceWeights &w, const uint16_t *rows, co
 // out[t, :] = sum_j wts[t, j] * y_slot[slot_pos[t*k + j], :], j in order.
 cudaError_t launch_combine(const float *y_slot, const int32_t *slot_pos, const float *wts, int T,
                            int H, int k, float *out, cudaStream_t stream);
+
+// ---- tensor-core issue rate (peak.cu) ------------------------------------------
+// kind 0 kind::f16, 1 kind::mxf8f6f4 (E2M1 x E4M3), 2 kind::mxf4; n_ctas CTAs
+// each issue `iters` M 128 x N 256 MMAs; err receives 31 if the final wait ran out.
+double mma_flops_per_instr(int kind);
+cudaError_t launch_mma_rate(int kind, int iters, int n_ctas, int *err, cudaStream_t stream);
 
 }  // namespace oxg

@@ -93,6 +93,11 @@ constexpr int kWf2b = OXG_FLAT_W2B, kSf2b = OXG_FLAT_S2B;
 #ifndef OXG_DEC_FLAT
 #define OXG_DEC_FLAT 1
 #endif
+// Token counts from which mlp2 runs the flat-split kernel over virtual
+// experts (below: the persistent per-expert band kernel).
+#ifndef OXG_FLAT2_MIN_TOKENS
+#define OXG_FLAT2_MIN_TOKENS 9
+#endif
 constexpr bool kUseFlat = OXG_DEC_FLAT != 0;
 constexpr size_t kMaxFlatSmem = 220 * 1024;  // dynamic shared memory (static arrays take the rest of 227 KB)
 
@@ -1753,7 +1758,7 @@ cudaError_t launch_moe_mlp2_sched(const MoeDeviceWeights &w, const float *h,
   a.v_pos0 = s.v_pos0;
   a.v_count = s.v_count;
   a.n_virtual = s.n_virtual;
-  if (T > 8 && kUseFlat && s.parts && s.flat_cnt && s.v_expert) {
+  if (T >= OXG_FLAT2_MIN_TOKENS && kUseFlat && s.parts && s.flat_cnt && s.v_expert) {
     // equal CTA groups per virtual expert (at most 8 slots: two column groups
     // of four slots' hi / lo halves), flat split inside each group
     const size_t smem = (size_t)16 * flat_row_pitch(a.K) + (size_t)kWf2b * kSf2b * kStageBytes;

@@ -65,6 +65,7 @@ constexpr int kGroupThreads = kConvThreads / kGroups;
 constexpr int kTasks = BM * 4 / kGroupThreads;
 constexpr int kTmemCols = 512;
 constexpr int kMaxExpertsP = 256;
+constexpr int kCombMaxK = kPrefillCombineMaxK;  // top-k of the fused combine
 
 struct PrefillArgs {
   const uint8_t *codes;   // tile chunks of [E, rows, K] (codes + scales, relayout.cu)
@@ -87,6 +88,12 @@ struct PrefillArgs {
   float *const *y_seg;
   int H;
   int *err;
+  // fused weighted combine (GEMM2, y_slot only): see PrefillIO
+  float *y;
+  const int32_t *perm, *slot_pos;
+  const float *wts;
+  uint32_t *comb_cnt;
+  int topk;
 };
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
@@ -139,6 +146,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   __shared__ int ntile_prefix[kMaxExpertsP + 1];
   __shared__ int epi_ok;
   __shared__ float col_scale[BN];  // GEMM1: 2^sigma of each column of the current item
+  __shared__ int comb_tok[GEMM == 2 ? BN : 1], comb_n;  // GEMM2: tokens this CTA combines
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -469,6 +477,75 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&acc_empty[buf]), 0));
+      if (GEMM == 2 && a.y) {
+        // Fused weighted top-k combine (src/moe.rs:90-96). Each (token,
+        // 128-row tile of H) has an arrival counter; the CTA that stores the
+        // last of the token's k slot rows for its 128 rows sums the k rows in
+        // j order with the combine's arithmetic (so the result does not
+        // depend on which CTA came last) and resets the counter to zero for
+        // the next call. The accumulator buffer is already released, so the
+        // MMAs of the next item overlap this.
+        const int f0 = c.m0 + (int)rank * BM;
+        __threadfence();  // this thread's slot-row stores before the arrivals
+        if (ew == 0 && lane == 0) comb_n = 0;
+        named_bar_sync(1, kEpiWarps * 32);
+        const int col = ew * 32 + lane;
+        if (f0 < a.rows && col < c.nvalid) {
+          const int t = a.perm[pos_base + col] / a.topk;
+          uint32_t *cnt = a.comb_cnt + (size_t)t * ((a.rows + BM - 1) / BM) + f0 / BM;
+          if (atomicAdd(cnt, 1u) == (uint32_t)a.topk - 1u) {
+            *cnt = 0u;
+            comb_tok[atomicAdd(&comb_n, 1)] = t;
+          }
+        }
+        __threadfence();  // the other CTAs' rows are visible past the arrivals
+        named_bar_sync(1, kEpiWarps * 32);
+        const int nf = min(BM, a.rows - f0);  // a multiple of 64
+        const int n_comb = comb_n, K = a.topk;  // K <= kCombMaxK (checked at launch)
+        // Two tokens per warp and round: lanes 4u + j fetch slot j's position
+        // and weight of token u, then every lane issues the 2 x K row loads
+        // of its 4 features before the first use, so a round costs two
+        // memory round trips whatever K is.
+        for (int i0 = 2 * ew; i0 < n_comb; i0 += 2 * kEpiWarps) {
+          const int mu = lane >> 2, mj = lane & 3;
+          int mp = -1;
+          float mw = 0.f;
+          if (lane < 8 && i0 + mu < n_comb && mj < K) {
+            const int t = comb_tok[i0 + mu];
+            mp = a.slot_pos[t * K + mj];
+            mw = a.wts[t * K + mj];
+          }
+          const bool cols_ok = 4 * lane < nf;
+          float4 v[2][kCombMaxK];
+          int pj[2][kCombMaxK];
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int jj = 0; jj < kCombMaxK; ++jj) {
+              pj[u][jj] = __shfl_sync(0xFFFFFFFFu, mp, 4 * u + jj);
+              v[u][jj] = pj[u][jj] >= 0 && cols_ok
+                             ? __ldcg(reinterpret_cast<const float4 *>(a.y_slot + (size_t)pj[u][jj] * a.H + f0) + lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            float wj[kCombMaxK];
+#pragma unroll
+            for (int jj = 0; jj < kCombMaxK; ++jj) wj[jj] = __shfl_sync(0xFFFFFFFFu, mw, 4 * u + jj);
+            if (i0 + u >= n_comb || !cols_ok) continue;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int jj = 0; jj < kCombMaxK; ++jj) {
+              if (pj[u][jj] < 0) continue;  // j >= K, or an unrouted slot
+              acc.x = fmaf(wj[jj], v[u][jj].x, acc.x);
+              acc.y = fmaf(wj[jj], v[u][jj].y, acc.y);
+              acc.z = fmaf(wj[jj], v[u][jj].z, acc.z);
+              acc.w = fmaf(wj[jj], v[u][jj].w, acc.w);
+            }
+            reinterpret_cast<float4 *>(a.y + (size_t)comb_tok[i0 + u] * a.H + f0)[lane] = acc;
+          }
+        }
+      }
     }
   }
 
@@ -685,6 +762,18 @@ cudaError_t launch_prefill_mlp2(const MoeDeviceWeights &w, const PrefillIO &io, 
   a.I = w.I;
   a.H = w.H;
   a.err = io.err;
+  if (io.y) {  // fused combine: one GPU's slot rows only, float4 rows
+    if (io.y_seg || !io.y_slot || !io.perm || !io.slot_pos || !io.wts || !io.comb_cnt || io.topk < 1 ||
+        io.topk > kCombMaxK ||
+        ((uintptr_t)io.y & 15) || ((uintptr_t)io.y_slot & 15))
+      return cudaErrorInvalidValue;
+    a.y = io.y;
+    a.perm = io.perm;
+    a.slot_pos = io.slot_pos;
+    a.wts = io.wts;
+    a.comb_cnt = io.comb_cnt;
+    a.topk = io.topk;
+  }
   (void)n_sms;
   return launch_gemm<2, 4>(m0, m1, a, stream);
 }

@@ -168,6 +168,12 @@ struct oxg_ctx {
     int32_t *seg = nullptr;  // counts [256] then offsets [257]
   } ep;
   std::vector<int32_t> seg_host;
+  // Arrival counters of the prefill GEMM2's fused combine, one per (token,
+  // 128-row tile of H): zero between calls (each call leaves them at zero;
+  // cleared again after a failed call). Kept apart from ws, whose layout
+  // moves with the batch size.
+  uint32_t *comb_cnt = nullptr;
+  size_t comb_cnt_n = 0;
   // Host-buffer forwards of large batches run in token chunks whose copies
   // overlap the neighbouring chunks' compute (oxg_moe_forward_host).
   struct {
@@ -685,6 +691,19 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, 
     return OXG_OK;
   }
   if ((rc = sort_slots(ctx, L, x, T, ranked, true))) return rc;
+  // the fused combine's counters: T x (128-row tiles of H), zero on entry
+  const size_t n_cnt = (size_t)T * oxg::prefill_comb_mtiles(d.hidden);
+  if (ctx->comb_cnt_n < n_cnt) {
+    OXG_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (ctx->comb_cnt) cudaFree(ctx->comb_cnt);
+    ctx->comb_cnt = nullptr;
+    ctx->comb_cnt_n = 0;
+    OXG_CUDA(ctx, cudaMalloc(&ctx->comb_cnt, n_cnt * sizeof(uint32_t)), "cudaMalloc(combine counters)");
+    ctx->comb_cnt_n = n_cnt;
+    OXG_CUDA(ctx, cudaMemsetAsync(ctx->comb_cnt, 0, n_cnt * sizeof(uint32_t), ctx->stream),
+             "cudaMemsetAsync(combine counters)");
+    ctx->epoch += 1;
+  }
   const oxg::MoeDeviceWeights w = device_weights(L);
   oxg::PrefillIO io{};
   io.S = S;
@@ -698,6 +717,15 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, 
   io.h_lo = ctx->ws.h_lo;
   io.y_slot = ctx->ws.y_slot;
   io.err = ctx->ws.err;
+  const bool fused = d.top_k <= oxg::kPrefillCombineMaxK;
+  if (fused) {  // GEMM2 sums each token's k rows (the weighted combine) itself
+    io.y = y;
+    io.perm = ctx->ws.perm;
+    io.slot_pos = ctx->ws.slot_pos;
+    io.wts = ctx->ws.wts;
+    io.comb_cnt = ctx->comb_cnt;
+    io.topk = d.top_k;
+  }
   OXG_CUDA(ctx, launch(ctx, "moe_mlp1_prefill", [&] {
              return oxg::launch_prefill_mlp1(w, io, ctx->n_sms, ctx->stream);
            }),
@@ -706,11 +734,12 @@ int forward_prefill(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, float *y, 
              return oxg::launch_prefill_mlp2(w, io, ctx->n_sms, ctx->stream);
            }),
            "prefill mlp2 launch");
-  OXG_CUDA(ctx, launch(ctx, "combine", [&] {
-             return oxg::launch_combine(ctx->ws.y_slot, ctx->ws.slot_pos, ctx->ws.wts, T,
-                                        d.hidden, d.top_k, y, ctx->stream);
-           }),
-           "combine launch");
+  if (!fused)
+    OXG_CUDA(ctx, launch(ctx, "combine", [&] {
+               return oxg::launch_combine(ctx->ws.y_slot, ctx->ws.slot_pos, ctx->ws.wts, T, d.hidden, d.top_k, y,
+                                          ctx->stream);
+             }),
+             "combine launch");
   ctx->prefill_pending = true;
   return OXG_OK;
 }
@@ -765,6 +794,8 @@ int read_pipeline_error(oxg_ctx *ctx) {
   ctx->prefill_pending = false;
   if (h) {
     cudaMemsetAsync(ctx->ws.err, 0, sizeof(int), ctx->stream);
+    // a pipeline that gave up may have left combine counters part-way
+    if (ctx->comb_cnt) cudaMemsetAsync(ctx->comb_cnt, 0, ctx->comb_cnt_n * sizeof(uint32_t), ctx->stream);
     if (h == 50)
       return fail(ctx, OXG_ERR_STATE, "another rank reported a failed expert-parallel step");
     if (h == 51)
@@ -954,6 +985,7 @@ int oxg_ctx_destroy(oxg_ctx *ctx) {
   oxg::model_free(ctx);
   for (Layer &L : ctx->layers) free_layer(L);
   if (ctx->ws.base) cudaFree(ctx->ws.base);
+  if (ctx->comb_cnt) cudaFree(ctx->comb_cnt);
   if (ctx->ep.base) cudaFree(ctx->ep.base);
   if (ctx->pipe.h2d) cudaStreamSynchronize(ctx->pipe.h2d);
   if (ctx->pipe.d2h) cudaStreamSynchronize(ctx->pipe.d2h);
@@ -1813,6 +1845,42 @@ int oxg_kernel_launches(const oxg_ctx *ctx, long long *count) {
   if (!ctx || !count) return fail(nullptr, OXG_ERR_INVALID_ARG, "ctx and count must be non-NULL");
   *count = ctx->launches;
   return OXG_OK;
+}
+
+int oxg_measure_mma_rate(oxg_ctx *ctx, int kind, int iters, double *tflops) {
+  if (!ctx || !tflops) return fail(ctx, OXG_ERR_INVALID_ARG, "ctx and tflops must be non-NULL");
+  if (kind < 0 || kind > 2) return fail(ctx, OXG_ERR_INVALID_ARG, "kind must be 0, 1 or 2, got %d", kind);
+  if (iters < 1 || iters > (1 << 22)) return fail(ctx, OXG_ERR_INVALID_ARG, "iters must be in [1, 2^22]");
+  DeviceGuard g(ctx->device);
+  int *err = nullptr;
+  OXG_CUDA(ctx, cudaMalloc(&err, sizeof(int)), "cudaMalloc(error word)");
+  cudaEvent_t a = nullptr, b = nullptr;
+  int rc = OXG_OK, h = 0;
+  float ms = 0.f;
+  do {
+    cudaError_t st;
+    if ((st = cudaMemsetAsync(err, 0, sizeof(int), ctx->stream)) != cudaSuccess ||
+        (st = cudaEventCreate(&a)) != cudaSuccess || (st = cudaEventCreate(&b)) != cudaSuccess ||
+        (st = cudaEventRecord(a, ctx->stream)) != cudaSuccess ||
+        (st = oxg::launch_mma_rate(kind, iters, ctx->n_sms, err, ctx->stream)) != cudaSuccess ||
+        (st = cudaEventRecord(b, ctx->stream)) != cudaSuccess ||
+        (st = cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream)) != cudaSuccess ||
+        (st = cudaStreamSynchronize(ctx->stream)) != cudaSuccess ||
+        (st = cudaEventElapsedTime(&ms, a, b)) != cudaSuccess) {
+      rc = fail(ctx, OXG_ERR_CUDA, "mma rate measurement: %s", cudaGetErrorString(st));
+      break;
+    }
+    ctx->launches += 1;
+    if (h) {
+      rc = fail(ctx, OXG_ERR_TIMEOUT, "mma rate measurement: the final wait ran out");
+      break;
+    }
+    *tflops = oxg::mma_flops_per_instr(kind) * iters * ctx->n_sms / (ms * 1e-3) / 1e12;
+  } while (0);
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  cudaFree(err);
+  return rc;
 }
 
 }  // extern "C"

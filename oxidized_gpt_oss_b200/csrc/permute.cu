@@ -150,19 +150,10 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
     uint16_t *__restrict__ xp, float *__restrict__ pos_scale, int pad, uint8_t *__restrict__ xq,
     uint8_t *__restrict__ xsf, int rows_cap) {
   __shared__ int base_s[kScatterMaxE], tot_s[kScatterMaxE];
+  __shared__ int part_s[2 * kScatterThreads];
   const int c = blockIdx.x / kScatterSub, sub = blockIdx.x % kScatterSub;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int e = threadIdx.x; e < E; e += kScatterThreads) {
-    int tot = 0, before = 0;
-    for (int cc = 0; cc < n_cta; ++cc) {
-      const int v = cta_hist[(size_t)cc * E + e];
-      tot += v;
-      before += cc < c ? v : 0;
-    }
-    tot_s[e] = tot;
-    base_s[e] = before;
-  }
-  __syncthreads();
+  hist_prefix<kScatterThreads>(cta_hist, n_cta, E, c, base_s, tot_s, part_s);
   if (threadIdx.x == 0) {
     int run = 0;
     for (int e = 0; e < E; ++e) {
@@ -180,21 +171,37 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(
   const int s_end = min(T, (c + 1) * kScatterTokens) * k;
   const int per = (kScatterTokens * k + kScatterSub - 1) / kScatterSub;
   const int my_begin = s_begin + sub * per, my_end = min(s_end, my_begin + per);
-  for (int sl = my_begin + warp; sl < my_end; sl += kScatterThreads / 32) {
-    const int e = idx[sl];
-    const int p = base_s[e] + local_rank[sl];
-    if (lane == 0) {
-      perm[p] = sl;
-      slot_pos[sl] = p;
+  // This warp's slots are my_begin + warp + W i (W warps). Their positions (and the
+  // tokens' sigma) are fetched one slot per lane, all at once, before the rows
+  // are staged one after another: one memory round trip of metadata per 32
+  // slots instead of three per slot.
+  const int n_mine = my_end - my_begin;
+  constexpr int W = kScatterThreads / 32;
+  const int n_w = n_mine > warp ? (n_mine - warp + W - 1) / W : 0;
+  for (int i0 = 0; i0 < n_w; i0 += 32) {
+    const int li = i0 + lane;
+    const int sl_l = my_begin + warp + W * li;
+    int p_l = 0, sg_l = 0;
+    if (li < n_w) {
+      const int e = idx[sl_l];
+      p_l = base_s[e] + local_rank[sl_l];
+      perm[p_l] = sl_l;
+      slot_pos[sl_l] = p_l;
+      if (xp) {
+        sg_l = sigma[sl_l / k];
+        pos_scale[p_l] = __uint_as_float((uint32_t)(127 + sg_l) << 23);
+      }
     }
-    if (xp) {
-      const int t = sl / k, sg = sigma[t];
-      if (lane == 0) pos_scale[p] = __uint_as_float((uint32_t)(127 + sg) << 23);
-      stage_row_f16(x + (size_t)t * H, xp + (size_t)p * H, H, sg, lane);
-    }
-    if (xq) {
-      const size_t sf_plane = (size_t)(rows_cap / 128) * ((H + 127) / 128) * mxf::kAtomBytes;
-      stage_row_e4m3(x + (size_t)(sl / k) * H, xq, (size_t)rows_cap * H, xsf, sf_plane, p, H, lane);
+    const int n_here = min(32, n_w - i0);
+    for (int j = 0; j < n_here; ++j) {
+      const int p = __shfl_sync(0xFFFFFFFFu, p_l, j);
+      const int sg = __shfl_sync(0xFFFFFFFFu, sg_l, j);
+      const int t = (my_begin + warp + W * (i0 + j)) / k;
+      if (xp) stage_row_f16(x + (size_t)t * H, xp + (size_t)p * H, H, sg, lane);
+      if (xq) {
+        const size_t sf_plane = (size_t)(rows_cap / 128) * ((H + 127) / 128) * mxf::kAtomBytes;
+        stage_row_e4m3(x + (size_t)t * H, xq, (size_t)rows_cap * H, xsf, sf_plane, p, H, lane);
+      }
     }
   }
 }

@@ -154,19 +154,24 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
 
 
 // ---- batched router on the tensor cores -------------------------------------
-// CTAs of 64 tokens (4 warps x 16) compute the [64, E] logits with
-// mma.sync.m16n8k16 on bf16 operands (exact products, f32 accumulation),
-// streaming x and W through shared memory in 128-column chunks (cp.async,
-// double-buffered, 16-byte chunks XOR-swizzled by row so the ldmatrix reads
-// are conflict-free). max|x| per token comes from the A fragments. After the
-// bias and the same top-k/softmax as above, warp 0 ranks the CTA's T*k slots
-// per expert in slot order (the counting sort's first half): local_rank of
-// each slot and the CTA's histogram, which scatter_kernel turns into
-// positions.
+// CTAs of 64 tokens and 16 warps: warp w computes the logits of token block
+// w % 4 (16 tokens) against expert n-tiles w / 4 and w / 4 + 4 (8 experts
+// each) with mma.sync.m16n8k16 on bf16 operands (exact products, f32
+// accumulation), streaming x and W through a kRmStages-deep shared-memory
+// ring of 128-column chunks (cp.async, 16-byte chunks XOR-swizzled by row so
+// the ldmatrix reads are conflict-free; one barrier per chunk). max|x| per
+// token comes from the A fragments. After the bias, each warp selects the
+// top k of 4 tokens (rank_topk_softmax, the same selection and softmax as
+// above); then warp 0 ranks the CTA's T*k slots per expert in slot order
+// (the counting sort's first half): local_rank of each slot and the CTA's
+// histogram, which scatter_kernel turns into positions. (Four warps of 16
+// tokens x all experts each measured issue-bound: one warp per scheduler.)
 constexpr int kRmTokens = 64;
-constexpr int kRmThreads = 128;
+constexpr int kRmWarps = 16;
+constexpr int kRmThreads = kRmWarps * 32;
 constexpr int kRmKC = 128;  // columns per chunk
 constexpr int kRmMaxE = 64;
+constexpr int kRmStages = 4;
 
 __global__ void __launch_bounds__(kRmThreads) router_mma_kernel(
     const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, const uint16_t *__restrict__ b,
@@ -177,101 +182,109 @@ __global__ void __launch_bounds__(kRmThreads) router_mma_kernel(
   __shared__ float logit_s[kRmTokens][kRmMaxE];
   __shared__ int32_t idx_s[kRmTokens * kMaxTopK];
   __shared__ int cnt_s[kRmMaxE];
+  __shared__ float top_v_s[kRmWarps][kMaxTopK];
+  __shared__ int top_e_s[kRmWarps][kMaxTopK];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tb = warp & 3, eq = warp >> 2;  // token block (16 rows), first expert n-tile
   const int t0 = blockIdx.x * kRmTokens;
   const int stage_bytes = (kRmTokens + E) * kRmKC * 2;
   const int n_chunks = (H + kRmKC - 1) / kRmKC;
+  const int NT = E / 8;  // n-tiles of 8 experts (E is a multiple of 16)
+  const bool has0 = eq < NT, has1 = eq + 4 < NT;
 
-  auto load_chunk = [&](int c, int buf) {
-    uint8_t *xs = rm_smem + buf * stage_bytes;
-    uint8_t *ws = xs + kRmTokens * kRmKC * 2;
-    const int k0 = c * kRmKC;
-    for (int i = threadIdx.x; i < (kRmTokens + E) * 16; i += kRmThreads) {
-      const int r = i >> 4, ch = i & 15, col = k0 + ch * 8;
-      const bool is_x = r < kRmTokens;
-      const int row = is_x ? r : r - kRmTokens;
-      const bool ok = col < H && (!is_x || t0 + row < T);
-      const uint16_t *src = is_x ? x + (size_t)(ok ? t0 + row : 0) * H + (ok ? col : 0)
-                                 : w + (size_t)row * H + (ok ? col : 0);
-      uint8_t *dst = (is_x ? xs : ws) + row * (kRmKC * 2) + ((ch ^ (row & 7)) << 4);
-      cp_async_16_zfill(dst, src, ok ? 16u : 0u);
+  // chunk c into ring slot c % kRmStages (one commit group per call, empty
+  // past the last chunk so the group count stays uniform)
+  auto load_chunk = [&](int c) {
+    if (c < n_chunks) {
+      uint8_t *xs = rm_smem + (c % kRmStages) * stage_bytes;
+      uint8_t *ws = xs + kRmTokens * kRmKC * 2;
+      const int k0 = c * kRmKC;
+      for (int i = threadIdx.x; i < (kRmTokens + E) * 16; i += kRmThreads) {
+        const int r = i >> 4, ch = i & 15, col = k0 + ch * 8;
+        const bool is_x = r < kRmTokens;
+        const int row = is_x ? r : r - kRmTokens;
+        const bool ok = col < H && (!is_x || t0 + row < T);
+        const uint16_t *src = is_x ? x + (size_t)(ok ? t0 + row : 0) * H + (ok ? col : 0)
+                                   : w + (size_t)row * H + (ok ? col : 0);
+        uint8_t *dst = (is_x ? xs : ws) + row * (kRmKC * 2) + ((ch ^ (row & 7)) << 4);
+        cp_async_16_zfill(dst, src, ok ? 16u : 0u);
+      }
     }
     cp_async_commit();
   };
 
-  const int NT = E / 8;  // n-tiles of 8 experts (E is a multiple of 16)
-  float acc[kRmMaxE / 8][4];
-#pragma unroll
-  for (int j = 0; j < kRmMaxE / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   uint32_t amax_lo = 0u, amax_hi = 0u;  // |x| bf16 bits of rows g and g + 8, two per register
   const int mi = lane >> 3, ri = lane & 7;
+  const int arow = tb * 16 + ri + 8 * (mi & 1);
+  // B matrices 0, 1: n-tile eq (k 0-7, 8-15); 2, 3: n-tile eq + 4 (or eq again)
+  const int brow = 8 * ((mi >> 1) && has1 ? eq + 4 : eq) + ri;
 
-  load_chunk(0, 0);
+#pragma unroll
+  for (int c = 0; c < kRmStages - 1; ++c) load_chunk(c);
   for (int c = 0; c < n_chunks; ++c) {
-    if (c + 1 < n_chunks)
-      load_chunk(c + 1, (c + 1) & 1);
-    else
-      cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint8_t *xs = rm_smem + (c & 1) * stage_bytes;
+    cp_async_wait<kRmStages - 2>();  // chunk c has landed (this thread's copies)
+    __syncthreads();                 // ... everyone's; and slot (c - 1) % S is free
+    load_chunk(c + kRmStages - 1);
+    if (!has0) continue;
+    const uint8_t *xs = rm_smem + (c % kRmStages) * stage_bytes;
     const uint8_t *ws = xs + kRmTokens * kRmKC * 2;
 #pragma unroll
     for (int kk = 0; kk < kRmKC / 16; ++kk) {
-      const int arow = warp * 16 + ri + 8 * (mi & 1), ach = 2 * kk + (mi >> 1);
-      uint32_t a[4];
+      const int ach = 2 * kk + (mi >> 1), bch = 2 * kk + (mi & 1);
+      uint32_t a[4], bq[4];
       ldmatrix_x4(a, xs + arow * (kRmKC * 2) + ((ach ^ (arow & 7)) << 4));
-      amax_lo = __vmaxu2(amax_lo, __vmaxu2(a[0] & 0x7FFF7FFFu, a[2] & 0x7FFF7FFFu));
-      amax_hi = __vmaxu2(amax_hi, __vmaxu2(a[1] & 0x7FFF7FFFu, a[3] & 0x7FFF7FFFu));
-#pragma unroll
-      for (int j = 0; j < kRmMaxE / 8; j += 2) {
-        if (j < NT) {
-          const int brow = 8 * (j + (mi >> 1)) + ri, bch = 2 * kk + (mi & 1);
-          uint32_t bq[4];
-          ldmatrix_x4(bq, ws + brow * (kRmKC * 2) + ((bch ^ (brow & 7)) << 4));
-          mma_bf16_16816(acc[j], a, bq[0], bq[1]);
-          mma_bf16_16816(acc[j + 1], a, bq[2], bq[3]);
-        }
+      ldmatrix_x4(bq, ws + brow * (kRmKC * 2) + ((bch ^ (brow & 7)) << 4));
+      if (eq == 0) {
+        amax_lo = __vmaxu2(amax_lo, __vmaxu2(a[0] & 0x7FFF7FFFu, a[2] & 0x7FFF7FFFu));
+        amax_hi = __vmaxu2(amax_hi, __vmaxu2(a[1] & 0x7FFF7FFFu, a[3] & 0x7FFF7FFFu));
       }
+      mma_bf16_16816(acc[0], a, bq[0], bq[1]);
+      if (has1) mma_bf16_16816(acc[1], a, bq[2], bq[3]);
     }
-    __syncthreads();  // the buffer is refilled by the next iteration's load
   }
+  cp_async_wait<0>();
 
-  // logits (+ bias) of rows g and g + 8 of this warp, experts 8j + 2q + {0, 1}
+  // logits (+ bias) of rows g and g + 8 of token block tb, experts
+  // 8 tile + 2q + {0, 1}
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
-  for (int j = 0; j < kRmMaxE / 8; ++j) {
-    if (j < NT) {
-      const int e0 = 8 * j + 2 * q;
+  for (int u = 0; u < 2; ++u) {
+    if (u == 0 ? has0 : has1) {
+      const int e0 = 8 * (eq + 4 * u) + 2 * q;
       const float b0 = b ? bf16_to_f32(b[e0]) : 0.f, b1 = b ? bf16_to_f32(b[e0 + 1]) : 0.f;
-      logit_s[warp * 16 + g][e0] = acc[j][0] + b0;
-      logit_s[warp * 16 + g][e0 + 1] = acc[j][1] + b1;
-      logit_s[warp * 16 + g + 8][e0] = acc[j][2] + b0;
-      logit_s[warp * 16 + g + 8][e0 + 1] = acc[j][3] + b1;
+      logit_s[tb * 16 + g][e0] = acc[u][0] + b0;
+      logit_s[tb * 16 + g][e0 + 1] = acc[u][1] + b1;
+      logit_s[tb * 16 + g + 8][e0] = acc[u][2] + b0;
+      logit_s[tb * 16 + g + 8][e0 + 1] = acc[u][3] + b1;
     }
   }
-  // max|x| of the rows: halves of the packed maxima, then over the quad
-  uint32_t mlo = max(amax_lo & 0xFFFFu, amax_lo >> 16), mhi = max(amax_hi & 0xFFFFu, amax_hi >> 16);
+  if (eq == 0) {
+    // max|x| of the rows: halves of the packed maxima, then over the quad
+    uint32_t mlo = max(amax_lo & 0xFFFFu, amax_lo >> 16), mhi = max(amax_hi & 0xFFFFu, amax_hi >> 16);
 #pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    mlo = max(mlo, __shfl_xor_sync(0xFFFFFFFFu, mlo, o));
-    mhi = max(mhi, __shfl_xor_sync(0xFFFFFFFFu, mhi, o));
+    for (int o = 1; o <= 2; o <<= 1) {
+      mlo = max(mlo, __shfl_xor_sync(0xFFFFFFFFu, mlo, o));
+      mhi = max(mhi, __shfl_xor_sync(0xFFFFFFFFu, mhi, o));
+    }
+    if (q == 0) {
+      const int ta = t0 + tb * 16 + g, tbb = ta + 8;
+      if (ta < T) sigma_out[ta] = sigma_of(mlo >> 7);  // bf16 bits >> 7 = f32 exponent
+      if (tbb < T) sigma_out[tbb] = sigma_of(mhi >> 7);
+    }
   }
-  if (q == 0) {
-    const int ta = t0 + warp * 16 + g, tb = ta + 8;
-    if (ta < T) sigma_out[ta] = sigma_of(mlo >> 7);  // bf16 bits >> 7 = f32 exponent
-    if (tb < T) sigma_out[tb] = sigma_of(mhi >> 7);
+  __syncthreads();  // every expert column of every token is in logit_s
+  const int n_tok = min(kRmTokens, T - t0);
+  constexpr int kTokPerWarp = kRmTokens / kRmWarps;
+  for (int tl = warp * kTokPerWarp; tl < (warp + 1) * kTokPerWarp && tl < n_tok; ++tl) {
+    const size_t t = (size_t)t0 + tl;
+    rank_topk_softmax(logit_s[tl], E, k, lane, idx + t * k, wts + t * k, idx_s + tl * k, top_v_s[warp],
+                      top_e_s[warp]);
   }
   __syncthreads();
-  const int n_tok = min(kRmTokens, T - t0);
   if (logits_out)
     for (int i = threadIdx.x; i < n_tok * E; i += kRmThreads)
       logits_out[(size_t)t0 * E + i] = logit_s[i / E][i % E];
-  for (int tl = warp; tl < n_tok; tl += kRmThreads / 32) {
-    const size_t t = (size_t)t0 + tl;
-    select_topk_softmax(logit_s[tl], E, k, lane, idx + t * k, wts + t * k, idx_s + tl * k);
-  }
-  __syncthreads();
   if (warp == 0) {
     for (int e = lane; e < E; e += 32) cnt_s[e] = 0;
     __syncwarp();
@@ -324,7 +337,7 @@ cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16
   if (T == 0) return cudaSuccess;
   if (!router_mma_supported(H, E, k)) return cudaErrorInvalidValue;
   if ((uintptr_t)x & 15 || (uintptr_t)w & 15) return cudaErrorInvalidValue;
-  const size_t smem = 2 * (size_t)(kRmTokens + E) * kRmKC * 2;
+  const size_t smem = (size_t)kRmStages * (kRmTokens + E) * kRmKC * 2;
   cudaError_t st = cudaFuncSetAttribute(router_mma_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (st != cudaSuccess) return st;
