@@ -73,7 +73,10 @@ constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
 // At most kDeepTokens tokens (4-8 active experts): each tile's K is split
 // over 4 warps — mlp1 28 warps x 5 stages (7 tiles in flight per SM), mlp2
 // 20 x 7 (5 tiles, a band being ~5 tiles of one expert).
-constexpr int kDeepTokens = 2;
+#ifndef OXG_DEEP_TOKENS
+#define OXG_DEEP_TOKENS 2
+#endif
+constexpr int kDeepTokens = OXG_DEEP_TOKENS;
 constexpr int kW1d = 28, kS1d = 5, kK1d = 4;  // mlp1: 7 groups of 4 warps splitting K
 constexpr int kW3d = 20, kS3d = 7, kK3d = 4;  // mlp2: 5 groups of 4 warps splitting K
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)

@@ -326,15 +326,32 @@ __global__ void __launch_bounds__(kThreadsM, 1)
         prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
         if (prev == (uint32_t)(n_act - 1)) {
           __threadfence();
-          if (valid)
-            for (int t = 0; t < a.T; ++t) {
-              float acc = 0.f;
-              for (int jj = 0; jj < a.k; ++jj) {
-                const int p = __ldcg(a.slot_pos + t * a.k + jj);
-                acc = fmaf(__ldcg(a.wts + t * a.k + jj), __ldcg(a.y_slot + (size_t)p * a.H + m), acc);
+          // tokens in batches of 32 / k: lane l fetches the position and
+          // weight of the batch's slot l, then every lane issues the loads
+          // of a token's k rows together (two memory round trips per batch)
+          const int tb = 32 / a.k;
+          for (int t0 = 0; t0 < a.T; t0 += tb) {
+            const int sl = t0 * a.k + lane;
+            const bool have = lane < tb * a.k && sl < a.T * a.k;
+            const int p_l = have ? __ldcg(a.slot_pos + sl) : 0;
+            const float w_l = have ? __ldcg(a.wts + sl) : 0.f;
+            for (int t = t0; t < min(a.T, t0 + tb); ++t) {
+              const int base = (t - t0) * a.k;
+              float v[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int p = __shfl_sync(0xFFFFFFFFu, p_l, (base + jj) & 31);
+                v[jj] = (jj < a.k && valid) ? __ldcg(a.y_slot + (size_t)p * a.H + m) : 0.f;
               }
-              a.y[(size_t)t * a.H + m] = acc;
+              float acc = 0.f;
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const float w = __shfl_sync(0xFFFFFFFFu, w_l, (base + jj) & 31);
+                if (jj < a.k) acc = fmaf(w, v[jj], acc);
+              }
+              if (valid) a.y[(size_t)t * a.H + m] = acc;
             }
+          }
           if (lane == 0) a.band_done[4 * rt + q] = 0u;
         }
       }

@@ -267,8 +267,11 @@ def gpu_timeout_worker(rank, world, port, out_dir):
         d = synth.moe_layer(seed=41, hidden=256, intermediate=256, n_experts=16, top_k=4)
         begin, count = ep.shard_range(16, world, rank)
         shard = MoELayer(d, experts=(begin, count))
-        moe = ep.PeerExpertParallelMoE(shard, max_tokens=64)
-        x = torch.from_numpy(synth.activations(300 + rank, 48, 256).view(np.int16)).cuda()
+        # 80 tokens per rank: above the small-batch path, so the whole layer on
+        # one GPU takes the same router and expert kernels as the exchange and
+        # the first step must match it bit for bit
+        moe = ep.PeerExpertParallelMoE(shard, max_tokens=96)
+        x = torch.from_numpy(synth.activations(300 + rank, 80, 256).view(np.int16)).cuda()
         full = MoELayer(d) if rank == 0 else None
         y_ref = full.forward(x).clone() if full else None
         if n_dev >= world:  # a good step on separate GPUs first
