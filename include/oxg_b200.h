@@ -303,8 +303,11 @@ typedef struct {
   int max_tokens;      /* largest n_tokens of one oxg_model_forward (prompts are chunked) */
   float rope_theta;    /* 150000 (src/config.rs:122) */
   float rms_eps;       /* 1e-5 (src/model.rs:433) */
-  int max_batch;       /* sequences with a KV cache of their own (0 or 1: one), at most min(128, max_tokens);
-                          the cache holds max_batch * max_seq positions per layer and kv head */
+  int max_batch;       /* sequences with a KV cache of their own (0 or 1: one), at most min(128, max_tokens) */
+  int kv_pages;        /* paged KV cache: pages of 64 positions in the pool every sequence draws from as it
+                          grows (per layer and kv head); 0: max_batch * ceil(max_seq / 64), room for every
+                          sequence at max_seq. A step that needs a page when none is free fails with
+                          OXG_ERR_OOM and changes nothing; oxg_model_reset / oxg_model_reset_seq free them. */
 } oxg_model_dims;
 
 /* One layer's attention weights (host or device pointers, bf16 unless noted;
@@ -329,6 +332,12 @@ OXG_API int oxg_model_upload_embeddings(oxg_ctx *ctx, const uint16_t *embed, con
 OXG_API int oxg_model_upload_attention(oxg_ctx *ctx, int layer, const oxg_attn_weights *w);
 /* Empties the KV cache (GPTModel::reset_kv_cache, src/model.rs:743-747). */
 OXG_API int oxg_model_reset(oxg_ctx *ctx);
+/* Empties one sequence's KV cache and returns its pages to the pool (the
+ * reference keeps one sequence per model: this is reset_kv_cache,
+ * src/model.rs:743-747, for sequence `seq` of a batched model). */
+OXG_API int oxg_model_reset_seq(oxg_ctx *ctx, int seq);
+/* Pages of the KV-cache pool in use and in total. */
+OXG_API int oxg_model_kv_pages(oxg_ctx *ctx, int *used, int *total);
 /* Number of positions in the KV cache. */
 OXG_API int oxg_model_position(oxg_ctx *ctx, int *pos);
 /* GPTModel::forward (src/model.rs:713-741) on device data: appends n_tokens

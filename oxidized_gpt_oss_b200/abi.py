@@ -54,7 +54,8 @@ class ModelDims(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("n_heads", ctypes.c_int),
                 ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int),
                 ("sliding_window", ctypes.c_int), ("max_seq", ctypes.c_int), ("max_tokens", ctypes.c_int),
-                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_batch", ctypes.c_int)]
+                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_batch", ctypes.c_int),
+                ("kv_pages", ctypes.c_int)]
 
 
 class AttnWeights(ctypes.Structure):
@@ -100,6 +101,8 @@ SIGNATURES = {
     "oxg_ep_set_wait_budget": (_I, [_CTX, ctypes.c_double]),
     "oxg_ep_last_received": (_I, [_CTX, ctypes.POINTER(ctypes.c_longlong)]),
     "oxg_model_init": (_I, [_CTX, ctypes.POINTER(ModelDims)]),
+    "oxg_model_reset_seq": (_I, [_CTX, _I]),
+    "oxg_model_kv_pages": (_I, [_CTX, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "oxg_model_upload_embeddings": (_I, [_CTX, _P, _P, _P]),
     "oxg_model_upload_attention": (_I, [_CTX, _I, ctypes.POINTER(AttnWeights)]),
     "oxg_model_reset": (_I, [_CTX]),

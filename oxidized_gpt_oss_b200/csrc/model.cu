@@ -418,18 +418,29 @@ __global__ void __launch_bounds__(kLinThreads)
 
 // ---------------------------------------------------------------------------
 // q/k/v epilogue: sum of the split partials + bias, RoPE on q and k, bf16
-// q rows and the K/V cache rows of positions pos0 .. pos0 + T - 1 (one
-// sequence), or, with tok_pos, token t at position tok_pos[t] and cache row
-// tok_row0[t] + tok_pos[t] (one token of each of T sequences).
-// One CTA per token.
+// q rows and the K/V cache rows of positions pos0 .. pos0 + T - 1 of
+// sequence seq, or, with tok_pos, token t at position tok_pos[t] of sequence
+// tok_seq[t] (one token of each of T sequences); cache rows through the page
+// table (kv_row). One CTA per token.
 // ---------------------------------------------------------------------------
+// Paged KV cache: a kv head's cache is a pool of pages of kKvPage rows;
+// position pos of sequence seq lives in page pages[seq * max_pages + pos / 64]
+// (the table the host fills as sequences grow), row pos % 64 of it.
+constexpr int kKvPage = 64;
+__device__ __forceinline__ long long kv_row(const int32_t *__restrict__ pages, int max_pages, int seq, int pos) {
+  return (long long)__ldg(pages + (size_t)seq * max_pages + (pos >> 6)) * kKvPage + (pos & (kKvPage - 1));
+}
+// Splits of kKvPage keys (one page each) of the keys lo .. hi.
+__host__ __device__ __forceinline__ int page_splits(int lo, int hi) { return (hi >> 6) - (lo >> 6) + 1; }
+
 constexpr int kQkvThreads = 256;
 
 __global__ void __launch_bounds__(kQkvThreads)
     qkv_post_kernel(const float *__restrict__ part, int S, int T, int nh, int nkv,
                     const uint16_t *__restrict__ bias, const float *__restrict__ rope_cos,
                     const float *__restrict__ rope_sin, int pos0, const int32_t *__restrict__ pos_dev,
-                    const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_row0, int max_seq,
+                    const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_seq,
+                    const int32_t *__restrict__ pages, int max_pages, int seq, int max_seq,
                     uint16_t *__restrict__ q_out, uint16_t *__restrict__ kc, uint16_t *__restrict__ vc) {
   const int t = blockIdx.x;
   const int Nq = nh * 64, Nkv = nkv * 64, N = Nq + 2 * Nkv;
@@ -437,7 +448,7 @@ __global__ void __launch_bounds__(kQkvThreads)
   const int it = blockIdx.y * kQkvThreads + threadIdx.x;  // one RoPE pair or one v element
   if (it >= n_pairs + Nkv) return;
   const int pos = tok_pos ? tok_pos[t] : (pos_dev ? *pos_dev : pos0) + t;
-  const int row = tok_pos ? tok_row0[t] + pos : pos;  // cache row within a kv head's run
+  const long long row = kv_row(pages, max_pages, tok_pos ? tok_seq[t] : seq, pos);  // within a kv head's pool
   const float *pt = part + (size_t)t * N;
   const size_t ps = (size_t)T * N;
   if (it < n_pairs) {
@@ -486,11 +497,12 @@ __global__ void __launch_bounds__(kQkvThreads)
 
 // ---------------------------------------------------------------------------
 // Decode attention (one query token at position key_hi): CTA (kv head, split)
-// handles up to 64 keys of [key_lo, key_hi] for the G query heads sharing the
-// kv head and writes (max, sum, unnormalised output) per head; the combine
-// kernel merges the splits with the sink. With tok_pos, grid z runs over T
-// tokens of T sequences: token t's keys are cache rows tok_row0[t] + (lo ..
-// tok_pos[t]), its q row t * Nq and its partials part_tok floats apart.
+// handles the keys of [key_lo, key_hi] in one page of the cache (split sp:
+// page key_lo / 64 + sp) for the G query heads sharing the kv head and
+// writes (max, sum, unnormalised output) per head; the combine kernel merges
+// the splits with the sink. With tok_pos, grid z runs over T tokens of T
+// sequences: token t's keys are positions lo .. tok_pos[t] of sequence
+// tok_seq[t], its q row t * Nq and its partials part_tok floats apart.
 // ---------------------------------------------------------------------------
 constexpr int kDecKeys = 64;
 constexpr int kMaxGroup = 16;
@@ -502,34 +514,38 @@ __global__ void __launch_bounds__(kDecThreads)
                        const uint16_t *__restrict__ vc, int max_seq, int G, int key_lo, int key_hi,
                        float scale, int n_split, const int32_t *__restrict__ pos_dev, int window,
                        float *__restrict__ part, const int32_t *__restrict__ tok_pos,
-                       const int32_t *__restrict__ tok_row0, int Nq, size_t part_tok) {
+                       const int32_t *__restrict__ tok_seq, const int32_t *__restrict__ pages, int max_pages,
+                       int seq, int Nq, size_t part_tok) {
   __shared__ float qs[kMaxGroup][64];
   __shared__ __align__(16) uint16_t Kt[64][kKtPad];     // K transposed: [dim][key]
   __shared__ __align__(16) uint16_t Vs[kDecKeys][64];   // V as stored: [key][dim]
   __shared__ float ps[kMaxGroup][kDecKeys];
   __shared__ float ms[kMaxGroup], ls[kMaxGroup];
   const int kvh = blockIdx.x, sp = blockIdx.y;
+  int sq = seq;
   if (pos_dev) {  // position from the device (graph replays): the grid covers the most splits
     key_hi = *pos_dev;
     key_lo = window > 0 ? max(0, key_hi - window + 1) : 0;
-    n_split = (key_hi - key_lo + kDecKeys) / kDecKeys;
+    n_split = page_splits(key_lo, key_hi);
     if (sp >= n_split) return;
   } else if (tok_pos) {  // one token per sequence: the grid covers the longest sequence
-    const int t = blockIdx.z, p = tok_pos[t], r0 = tok_row0[t];
+    const int t = blockIdx.z, p = tok_pos[t];
     const int lo = window > 0 ? max(0, p - window + 1) : 0;
-    n_split = (p - lo + kDecKeys) / kDecKeys;
+    n_split = page_splits(lo, p);
     if (sp >= n_split) return;
-    key_lo = r0 + lo;
-    key_hi = r0 + p;
+    sq = tok_seq[t];
+    key_lo = lo;
+    key_hi = p;
     q += (size_t)t * Nq;
     part += (size_t)t * part_tok;
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int k0 = key_lo + sp * kDecKeys;
-  const int nk = min(kDecKeys, key_hi + 1 - k0);
+  const int kp = (key_lo >> 6) + sp;  // this split's page
+  const int k0 = max(key_lo, kp * kKvPage);
+  const int nk = min(key_hi, kp * kKvPage + kKvPage - 1) + 1 - k0;
   // stage q (pre-scaled), K transposed and V: every 16-byte load in flight at once
   for (int i = tid; i < G * 64; i += kDecThreads) qs[i >> 6][i & 63] = bf16_to_f32(q[(size_t)kvh * G * 64 + i]) * scale;
-  const size_t base = ((size_t)kvh * max_seq + k0) * 64;
+  const size_t base = ((size_t)kvh * max_seq + (size_t)kv_row(pages, max_pages, sq, k0)) * 64;  // nk rows of one page
 #pragma unroll 4
   for (int c = tid; c < nk * 8; c += kDecThreads) {
     const int key = c >> 3, ch = c & 7;
@@ -638,10 +654,14 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
 }
 
 struct AdItem {
-  int t, kvh, sp, n_split, key0, nk;  // nk keys from position key0 of sequence t
+  int t, kvh, sp, n_split;
+  int pg0, n_pages;  // the item's cache pages (tiles) of sequence t: pg0 .. pg0 + n_pages - 1
+  int lo, hi;        // its token's keys
 };
+constexpr int kAdPages = kAdKeys / 64;  // pages per item
 
 // Item idx = (t * max_split + sp) * nkv + kvh; false past sequence t's splits.
+// Split sp covers pages lo / 64 + kAdPages sp .. (at most kAdPages of them).
 __device__ __forceinline__ bool ad_item(int idx, int nkv, int max_split, const int32_t *tok_pos, int window,
                                         AdItem &it) {
   it.kvh = idx % nkv;
@@ -650,10 +670,13 @@ __device__ __forceinline__ bool ad_item(int idx, int nkv, int max_split, const i
   it.t = r / max_split;
   const int p = tok_pos[it.t];
   const int lo = window > 0 ? max(0, p - window + 1) : 0;
-  it.n_split = (p - lo + kAdKeys) / kAdKeys;
+  const int pages = page_splits(lo, p);
+  it.n_split = (pages + kAdPages - 1) / kAdPages;
   if (it.sp >= it.n_split) return false;
-  it.key0 = lo + it.sp * kAdKeys;
-  it.nk = min(kAdKeys, p + 1 - it.key0);
+  it.pg0 = (lo >> 6) + it.sp * kAdPages;
+  it.n_pages = min(kAdPages, (p >> 6) - it.pg0 + 1);
+  it.lo = lo;
+  it.hi = p;
   return true;
 }
 
@@ -668,7 +691,7 @@ __device__ __forceinline__ bool ad_seek(AdCursor &c, int W, int n_items, int nkv
   for (; c.idx < n_items; c.idx += W)
     if (ad_item(c.idx, nkv, max_split, tok_pos, window, c.it)) {
       c.tile = 0;
-      c.n_tiles = (c.it.nk + kAdTile - 1) / kAdTile;
+      c.n_tiles = c.it.n_pages;
       return true;
     }
   return false;
@@ -676,7 +699,8 @@ __device__ __forceinline__ bool ad_seek(AdCursor &c, int W, int n_items, int nkv
 
 __global__ void __launch_bounds__(kAdWarps * 32, 1)
     attn_decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const uint16_t *__restrict__ q,
-                           const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_row0,
+                           const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_seq,
+                           const int32_t *__restrict__ pages, int max_pages,
                            long long k_row, long long v_row, long long kv_stride, int nkv, int Nq, int window,
                            float scale, int max_split, int n_items, float *__restrict__ part, size_t part_tok,
                            int *err) {
@@ -703,7 +727,9 @@ __global__ void __launch_bounds__(kAdWarps * 32, 1)
   auto issue = [&]() {
     const int s = issued % kAdStages;
     if (lane == 0) {
-      const long long r = (long long)pc.it.kvh * kv_stride + tok_row0[pc.it.t] + pc.it.key0 + pc.tile * kAdTile;
+      // tile = one whole cache page (64 rows)
+      const long long r = (long long)pc.it.kvh * kv_stride +
+                          kv_row(pages, max_pages, tok_seq[pc.it.t], (pc.it.pg0 + pc.tile) * kAdTile);
       uint8_t *ks = ring + (size_t)s * 2 * kAdTileBytes;
       mbar_arrive_expect_tx(&bar[s], 2 * kAdTileBytes);
       tma_load_2d(ks, &kv_map, &bar[s], 0, (int)(k_row + r));
@@ -745,7 +771,11 @@ __global__ void __launch_bounds__(kAdWarps * 32, 1)
       }
       uint8_t *ks = ring + (size_t)s * 2 * kAdTileBytes;
       uint8_t *vs = ks + kAdTileBytes;
-      const int nkt = min(kAdTile, it.nk - cc.tile * kAdTile);  // valid keys in this tile
+      // valid keys of this page: rows kf .. nkt - 1 (keys before the window
+      // start are masked; their V rows hold earlier positions of the sequence)
+      const int pbase = (it.pg0 + cc.tile) * kAdTile;
+      const int kf = max(0, it.lo - pbase);
+      const int nkt = min(kAdTile, it.hi + 1 - pbase);
       if (nkt < kAdTile) {  // zero the V rows past the end (whole 128-byte rows)
         for (int c = nkt * 8 + lane; c < kAdTile * 8; c += 32)
           *reinterpret_cast<uint4 *>(vs + c * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -769,10 +799,11 @@ __global__ void __launch_bounds__(kAdWarps * 32, 1)
 #pragma unroll
       for (int kb = 0; kb < 4; ++kb) {
         const int ka = kb * 16 + g, kb8 = ka + 8;
-        sc[kb][0] = ka < nkt ? sc[kb][0] * scale : -INFINITY;
-        sc[kb][1] = ka < nkt ? sc[kb][1] * scale : -INFINITY;
-        sc[kb][2] = kb8 < nkt ? sc[kb][2] * scale : -INFINITY;
-        sc[kb][3] = kb8 < nkt ? sc[kb][3] * scale : -INFINITY;
+        const bool oka = ka >= kf && ka < nkt, okb = kb8 >= kf && kb8 < nkt;
+        sc[kb][0] = oka ? sc[kb][0] * scale : -INFINITY;
+        sc[kb][1] = oka ? sc[kb][1] * scale : -INFINITY;
+        sc[kb][2] = okb ? sc[kb][2] * scale : -INFINITY;
+        sc[kb][3] = okb ? sc[kb][3] * scale : -INFINITY;
         mx0 = fmaxf(mx0, fmaxf(sc[kb][0], sc[kb][2]));
         mx1 = fmaxf(mx1, fmaxf(sc[kb][1], sc[kb][3]));
       }
@@ -871,7 +902,8 @@ __global__ void __launch_bounds__(64)
   if (pos_dev || tok_pos) {
     const int t = blockIdx.y;
     const int hi = tok_pos ? tok_pos[t] : *pos_dev, lo = window > 0 ? max(0, hi - window + 1) : 0;
-    n_split = (hi - lo + keys_per_split) / keys_per_split;
+    // splits of keys_per_split / 64 cache pages, from the page holding lo
+    n_split = (page_splits(lo, hi) - 1) / (keys_per_split / kKvPage) + 1;
     if (tok_pos) {
       part += (size_t)t * part_tok;
       out += (size_t)t * Nq;
@@ -907,7 +939,8 @@ constexpr int kAttQ = 64, kAttK = 64, kAttPad = 72;
 
 __global__ void __launch_bounds__(128)
     attn_prefill_kernel(const uint16_t *__restrict__ q, int T, int nh, int G, const uint16_t *__restrict__ kc,
-                        const uint16_t *__restrict__ vc, int max_seq, int pos0, int window, float scale,
+                        const uint16_t *__restrict__ vc, int max_seq, const int32_t *__restrict__ pages,
+                        int max_pages, int seq, int pos0, int window, float scale,
                         const uint16_t *__restrict__ sinks, uint16_t *__restrict__ out) {
   __shared__ __align__(16) uint16_t Ks[2][kAttK][kAttPad];
   __shared__ __align__(16) uint16_t Vs[2][kAttK][kAttPad];
@@ -935,14 +968,15 @@ __global__ void __launch_bounds__(128)
   const size_t kvbase = (size_t)kvh * max_seq;
 
   auto load_tile = [&](int buf, int tile) {
-    const int kb = tile * kAttK;
+    const int kb = tile * kAttK;  // a key tile is one cache page
+    const size_t prow = kvbase + (size_t)kv_row(pages, max_pages, seq, kb);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int id = tid + i * 128;
       const int r = id >> 3, ch = id & 7;
       const int key = kb + r;
       const bool ok = key <= kmax;
-      const size_t off = (kvbase + (ok ? key : 0)) * 64 + ch * 8;
+      const size_t off = (prow + (ok ? r : 0)) * 64 + ch * 8;
       cp_async_16_zfill(&Ks[buf][r][ch * 8], kc + off, ok ? 16u : 0u);
       cp_async_16_zfill(&Vs[buf][r][ch * 8], vc + off, ok ? 16u : 0u);
     }
@@ -1183,29 +1217,34 @@ cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, 
 
 cudaError_t launch_qkv_post(const float *part, int S, int T, int nh, int nkv, const uint16_t *bias,
                             const float *rope_cos, const float *rope_sin, int pos0, const int32_t *pos_dev,
-                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream,
-                            const int32_t *tok_pos, const int32_t *tok_row0) {
+                            int kv_rows, const int32_t *pages, int max_pages, int seq, uint16_t *q_out,
+                            uint16_t *kc, uint16_t *vc, cudaStream_t stream, const int32_t *tok_pos,
+                            const int32_t *tok_seq) {
   if (T <= 0) return cudaSuccess;
-  if (S > kMaxSplits) return cudaErrorInvalidValue;
+  if (S > kMaxSplits || !pages || max_pages <= 0) return cudaErrorInvalidValue;
   const int items = (nh + nkv) * 32 + nkv * 64;
   qkv_post_kernel<<<dim3(T, (items + kQkvThreads - 1) / kQkvThreads), kQkvThreads, 0, stream>>>(
-      part, S, T, nh, nkv, bias, rope_cos, rope_sin, pos0, pos_dev, tok_pos, tok_row0, max_seq, q_out, kc, vc);
+      part, S, T, nh, nkv, bias, rope_cos, rope_sin, pos0, pos_dev, tok_pos, tok_seq, pages, max_pages, seq,
+      kv_rows, q_out, kc, vc);
   return cudaGetLastError();
 }
 
 int attn_decode_splits(int n_keys) { return (n_keys + kDecKeys - 1) / kDecKeys; }
+// The most 64-key pages a window of `window` keys can touch.
+int window_page_splits(int window) { return (window + 62) / kKvPage + 1; }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
   const int G = a.nh / a.nkv;
   const int Nq = a.nh * 64;
   const int rows = a.split_rows > 0 ? a.split_rows : a.max_seq;  // positions of one sequence
+  if (!a.pages || a.max_pages <= 0) return cudaErrorInvalidValue;
+  // the most pages one query's keys touch (full span: a.max_splits pages)
+  const bool windowed = a.window > 0 && a.window < rows;
   if (a.tok_pos && a.kv_map && G == 8 && a.n_sms > 0) {  // one query of each of T sequences, tensor cores
     const size_t part_tok = attn_part_floats(a.nkv, G, rows);
-    // the longest span in keys (an upper bound from the 64-key split count)
-    const int span = a.window > 0 && a.window < rows ? std::min(a.window, a.max_splits * kDecKeys)
-                                                     : a.max_splits * kDecKeys;
-    const int max_split = (span + kAdKeys - 1) / kAdKeys;
+    const int span_pages = windowed ? std::min(window_page_splits(a.window), a.max_splits) : a.max_splits;
+    const int max_split = (span_pages + kAdPages - 1) / kAdPages;
     if (max_split <= 0 || a.max_splits > attn_decode_splits(rows)) return cudaErrorInvalidValue;
     const int n_items = a.T * max_split * a.nkv;
     const int grid = std::min((n_items + kAdWarps - 1) / kAdWarps, a.n_sms);
@@ -1213,8 +1252,9 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
                                           (int)kAdSmem);
     if (st != cudaSuccess) return st;
     attn_decode_mma_kernel<<<grid, kAdWarps * 32, kAdSmem, stream>>>(
-        *reinterpret_cast<const CUtensorMap *>(a.kv_map), a.q, a.tok_pos, a.tok_row0, a.k_row, a.v_row,
-        (long long)a.max_seq, a.nkv, Nq, a.window, a.scale, max_split, n_items, a.part, part_tok, a.err);
+        *reinterpret_cast<const CUtensorMap *>(a.kv_map), a.q, a.tok_pos, a.tok_seq, a.pages, a.max_pages,
+        a.k_row, a.v_row, (long long)a.max_seq, a.nkv, Nq, a.window, a.scale, max_split, n_items, a.part,
+        part_tok, a.err);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
     attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, max_split, nullptr, a.window, a.sinks,
                                                            a.out, a.tok_pos, Nq, part_tok, kAdKeys);
@@ -1222,12 +1262,11 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
   }
   if (a.tok_pos) {  // one query of each of T sequences
     const size_t part_tok = attn_part_floats(a.nkv, G, rows);
-    const int window_splits = attn_decode_splits(a.window > 0 && a.window < rows ? a.window : rows);
-    const int grid_split = a.window > 0 && window_splits < a.max_splits ? window_splits : a.max_splits;
+    const int grid_split = windowed ? std::min(window_page_splits(a.window), a.max_splits) : a.max_splits;
     if (grid_split <= 0 || grid_split > attn_decode_splits(rows)) return cudaErrorInvalidValue;
     attn_decode_kernel<<<dim3(a.nkv, grid_split, a.T), kDecThreads, 0, stream>>>(
         a.q, a.kc, a.vc, a.max_seq, G, 0, 0, a.scale, grid_split, nullptr, a.window, a.part, a.tok_pos,
-        a.tok_row0, Nq, part_tok);
+        a.tok_seq, a.pages, a.max_pages, 0, Nq, part_tok);
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, grid_split, nullptr, a.window, a.sinks,
@@ -1238,11 +1277,12 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
     const int pos = a.pos0;
     const int lo = a.window > 0 ? (pos - a.window + 1 > 0 ? pos - a.window + 1 : 0) : 0;
     // with the position on the device the grid covers the largest split count
-    const int grid_split = a.pos_dev ? attn_decode_splits(a.window > 0 && a.window < rows ? a.window : rows)
-                                     : attn_decode_splits(pos - lo + 1);
+    const int full = attn_decode_splits(rows);
+    const int grid_split = a.pos_dev ? (windowed ? std::min(window_page_splits(a.window), full) : full)
+                                     : page_splits(lo, pos);
     attn_decode_kernel<<<dim3(a.nkv, grid_split), kDecThreads, 0, stream>>>(
         a.q, a.kc, a.vc, a.max_seq, G, lo, pos, a.scale, grid_split, a.pos_dev, a.window, a.part, nullptr, nullptr,
-        Nq, 0);
+        a.pages, a.max_pages, a.seq, Nq, 0);
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     attn_combine_kernel<<<a.nh, 64, 0, stream>>>(a.part, G, grid_split, a.pos_dev, a.window, a.sinks, a.out,
@@ -1250,7 +1290,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
     return cudaGetLastError();
   }
   attn_prefill_kernel<<<dim3((a.T + kAttQ - 1) / kAttQ, a.nh), 128, 0, stream>>>(
-      a.q, a.T, a.nh, G, a.kc, a.vc, a.max_seq, a.pos0, a.window, a.scale, a.sinks, a.out);
+      a.q, a.T, a.nh, G, a.kc, a.vc, a.max_seq, a.pages, a.max_pages, a.seq, a.pos0, a.window, a.scale, a.sinks,
+      a.out);
   return cudaGetLastError();
 }
 

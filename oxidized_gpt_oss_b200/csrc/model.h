@@ -47,24 +47,34 @@ struct ArgmaxEpilogue {
 cudaError_t launch_linear(const uint16_t *x, int T, int ldx, const uint16_t *W, int N, int K, int splits,
                           float *out, cudaStream_t stream, const ArgmaxEpilogue *am = nullptr);
 
+// Paged KV cache: each kv head's cache is a pool of kv_rows rows in pages of
+// 64; pages [B, max_pages] (device) gives the pool page of page p of
+// sequence s (positions 64p .. 64p + 63), filled by the host as sequences
+// grow. Every kernel below addresses cache rows through it.
+constexpr int kKvPageRows = 64;
+
 // q/k/v epilogue: bias, RoPE (tables [positions, 32] of cos and sin), bf16 q
-// [T, nh * 64] and K/V cache rows (a kv head's rows max_seq apart) at
-// positions pos0 + t. pos_dev, when not null, replaces pos0 by the position
-// held on the device. tok_pos / tok_row0 (device, [T]), when not null, make
-// token t one of its own sequence: position tok_pos[t], cache row
-// tok_row0[t] + tok_pos[t].
+// [T, nh * 64] and the K/V cache rows (pools of kv_rows rows per kv head) of
+// positions pos0 + t of sequence seq. pos_dev, when not null, replaces pos0
+// by the position held on the device. tok_pos / tok_seq (device, [T]), when
+// not null, make token t one of its own sequence: position tok_pos[t] of
+// sequence tok_seq[t].
 cudaError_t launch_qkv_post(const float *part, int S, int T, int nh, int nkv, const uint16_t *bias,
                             const float *rope_cos, const float *rope_sin, int pos0, const int32_t *pos_dev,
-                            int max_seq, uint16_t *q_out, uint16_t *kc, uint16_t *vc, cudaStream_t stream,
-                            const int32_t *tok_pos = nullptr, const int32_t *tok_row0 = nullptr);
+                            int kv_rows, const int32_t *pages, int max_pages, int seq, uint16_t *q_out,
+                            uint16_t *kc, uint16_t *vc, cudaStream_t stream, const int32_t *tok_pos = nullptr,
+                            const int32_t *tok_seq = nullptr);
 
 struct AttnArgs {
   const uint16_t *q = nullptr;   // [T, nh * 64] bf16
-  const uint16_t *kc = nullptr, *vc = nullptr;  // [nkv, max_seq, 64] bf16 (max_seq: rows per kv head)
+  const uint16_t *kc = nullptr, *vc = nullptr;  // [nkv, max_seq, 64] bf16 (max_seq: pool rows per kv head)
   int T = 0, nh = 0, nkv = 0, max_seq = 0, pos0 = 0;
   int split_rows = 0;            // positions of one sequence (0: max_seq); sizes the decode grid
-  const int32_t *tok_pos = nullptr, *tok_row0 = nullptr;  // [T] device: one query of each of T sequences
-  int max_splits = 0;            // with tok_pos: splits of the longest sequence's full-attention span
+  const int32_t *pages = nullptr;  // page table [B, max_pages] (see kKvPageRows)
+  int max_pages = 0;
+  int seq = 0;                   // the sequence of a one-sequence call (no tok_pos)
+  const int32_t *tok_pos = nullptr, *tok_seq = nullptr;  // [T] device: one query of each of T sequences
+  int max_splits = 0;            // with tok_pos: 64-key page splits of the longest sequence's full span
   int window = 0;                // > 0: keys p - window + 1 .. p
   float scale = 0.125f;
   const uint16_t *sinks = nullptr;  // [nh] bf16 or null
@@ -85,6 +95,8 @@ struct AttnArgs {
 cudaError_t make_kv_map(void *map, const uint16_t *kv, long long rows);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream);
 size_t attn_part_floats(int nkv, int G, int max_seq);
+// Page splits (64 keys each) the keys lo .. hi of a query touch.
+inline int attn_page_splits(int lo, int hi) { return (hi >> 6) - (lo >> 6) + 1; }
 int attn_max_group();
 
 // next[row] = greedy choice (next may be null). With state (one row): the

@@ -7,10 +7,13 @@
 //     (q rows, then k, then v, so one linear launch covers all three), their
 //     bias, o projection [H, nh 64] + bias, sinks [nh], MoE norm [H];
 //   * embeddings [V, H], LM head [V, H], final norm [H];
-//   * KV cache [layer][K|V][nkv][max_batch * max_seq][64] bf16: a kv head's
-//     keys of sequence s are the contiguous rows s * max_seq .. (both
-//     attention kernels stream one run), RoPE cos/sin tables [max_seq][32]
-//     f32 (built on the host in double precision);
+//   * KV cache [layer][K|V][nkv][pool rows][64] bf16, paged: the pool of a
+//     kv head holds kv_pages pages of 64 rows; the page table [B][max_pages]
+//     (device, with a host mirror) maps page p of sequence s (positions
+//     64p .. 64p + 63) to a pool page, taken from a free list as the sequence
+//     grows and returned by a reset. Every attention kernel reads and writes
+//     rows through the table (a 64-key tile or split is one page). RoPE
+//     cos/sin tables [max_seq][32] f32 (built on the host in double precision);
 //   * activations for max_tokens tokens: residual f32, normed bf16, linear
 //     partials f32, q and attention output bf16, MoE output f32, logits.
 // Reference interfaces replaced: GPTModel::forward (src/model.rs:713-741),
@@ -60,9 +63,16 @@ struct ModelState {
   int part_rows = 0, max_logits = 0, gen_cap = 0;
   int pos = 0;                 // sequence 0's position (the single-sequence API's)
   int B = 1;                   // sequences with a KV cache of their own
-  size_t kv_stride = 0;        // cache rows per kv head: B * max_seq
+  size_t kv_stride = 0;        // cache rows per kv head: the page pool, n_pool * 64
   std::vector<int> seq_pos;    // positions of sequences 1 .. B-1 (index 0 unused)
-  int32_t *tok_pos = nullptr, *tok_row0 = nullptr;  // batched step: [B] position, cache row base
+  int32_t *tok_pos = nullptr, *tok_seq = nullptr;  // batched step: [B] position, sequence
+  // paged KV cache: page table [B][max_pages] on the device and its host
+  // mirror (-1: no page), the free pool pages, and each sequence's page count
+  int32_t *pages = nullptr;
+  int max_pages = 0, n_pool = 0;
+  std::vector<int32_t> page_host;
+  std::vector<int32_t> free_pages;
+  std::vector<int> seq_npages;
   bool moe_reserved = false;
   bool state_ok = false;  // the device state holds the last forward's greedy token
   int32_t *route_tap = nullptr;  // oxg_model_route_tap: [n_layers][tap_tokens][k] expert ids
@@ -150,6 +160,8 @@ int check_model_dims(oxg_ctx *ctx, const oxg_model_dims *d) {
   if (d->max_batch < 0 || d->max_batch > kMaxLogits || d->max_batch > d->max_tokens)
     return mfail(ctx, OXG_ERR_SHAPE, "max_batch must be in [0, min(%d, max_tokens)], got %d", kMaxLogits,
                  d->max_batch);
+  if (d->kv_pages < 0 || d->kv_pages > (1 << 24))
+    return mfail(ctx, OXG_ERR_SHAPE, "kv_pages must be in [0, 2^24], got %d", d->kv_pages);
   if (!(d->rope_theta > 0.f)) return mfail(ctx, OXG_ERR_INVALID_ARG, "rope_theta must be positive");
   if (!(d->rms_eps >= 0.f)) return mfail(ctx, OXG_ERR_INVALID_ARG, "rms_eps must be >= 0");
   return OXG_OK;
@@ -212,13 +224,48 @@ int upload_attn(oxg_ctx *ctx, ModelState &M, int layer, const oxg_attn_weights *
 
 int &seq_pos_ref(ModelState &M, int seq) { return seq == 0 ? M.pos : M.seq_pos[seq]; }
 
+// Gives sequence seq pool pages for every position up to last_pos and copies
+// the new table entries to the device (stream order). Fails with OXG_ERR_OOM,
+// changing nothing, when the pool has too few free pages.
+int ensure_pages(oxg_ctx *ctx, ModelState &M, int seq, int last_pos) {
+  if (last_pos < 0) return OXG_OK;
+  const int need = (last_pos >> 6) + 1, have = M.seq_npages[seq];
+  if (need <= have) return OXG_OK;
+  if (need > M.max_pages)
+    return mfail(ctx, OXG_ERR_SHAPE, "position %d of sequence %d exceeds max_seq %d", last_pos, seq, M.d.max_seq);
+  if ((int)M.free_pages.size() < need - have)
+    return mfail(ctx, OXG_ERR_OOM,
+                 "KV-cache pool exhausted: sequence %d needs %d more pages of 64 positions, %d of %d are free",
+                 seq, need - have, (int)M.free_pages.size(), M.n_pool);
+  int32_t *row = M.page_host.data() + (size_t)seq * M.max_pages;
+  for (int p = have; p < need; ++p) {
+    row[p] = M.free_pages.back();
+    M.free_pages.pop_back();
+  }
+  M.seq_npages[seq] = need;
+  MCUDA(ctx, cudaMemcpyAsync(M.pages + (size_t)seq * M.max_pages + have, row + have, (size_t)(need - have) * 4,
+                             cudaMemcpyHostToDevice, ctx_stream(ctx)),
+        "page table update");
+  return OXG_OK;
+}
+
+// Returns sequence seq's pages to the pool.
+void release_pages(ModelState &M, int seq) {
+  int32_t *row = M.page_host.data() + (size_t)seq * M.max_pages;
+  for (int p = M.seq_npages[seq] - 1; p >= 0; --p) {
+    M.free_pages.push_back(row[p]);
+    row[p] = -1;
+  }
+  M.seq_npages[seq] = 0;
+}
+
 // One forward of T tokens of sequence seq at positions pos .. pos + T - 1.
 // With dstate (the decode step a graph captures: sequence 0, T = 1,
 // n_logits = 1) the token, position and output slot come from the device
 // state instead, and the argmax advances it; otherwise a forward of sequence
 // 0 that computes logits leaves the state at its end position and greedy
 // token, ready for one-token steps. With batch, token t is the next token of
-// sequence t (positions and cache rows in M.tok_pos / M.tok_row0, max_splits
+// sequence t (positions and sequences in M.tok_pos / M.tok_seq, max_splits
 // the longest one's attention splits) and the caller advances the positions.
 int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits, float *logits_out,
             int32_t *next_out, int32_t *dstate = nullptr, int seq = 0, bool batch = false, int max_splits = 0) {
@@ -251,6 +298,10 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
   }
   const bool own_state = !batch && seq == 0;  // the decode state follows sequence 0
   const int pos0 = batch ? 0 : seq_pos_ref(M, seq);
+  if (!batch && !dstate) {  // pages for the positions this call writes (steps and batches: their callers)
+    const int rcp = ensure_pages(ctx, M, seq, pos0 + T - 1);
+    if (rcp) return rcp;
+  }
   // embedding + layer 0's attention norm
   {
     NormArgs a;
@@ -268,11 +319,10 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
   }
   const float scale = 1.0f / std::sqrt((float)d.head_dim);
   const size_t kv_layer = (size_t)2 * d.n_kv_heads * M.kv_stride * 64;
-  const size_t seq_row0 = batch ? 0 : (size_t)seq * d.max_seq * 64;
-  const int32_t *tpos = batch ? M.tok_pos : nullptr, *trow = batch ? M.tok_row0 : nullptr;
+  const int32_t *tpos = batch ? M.tok_pos : nullptr, *tseq = batch ? M.tok_seq : nullptr;
   for (int l = 0; l < L; ++l) {
     const ModelState::Attn &A = M.layers[l];
-    uint16_t *kc = M.kv + (size_t)l * kv_layer + seq_row0;
+    uint16_t *kc = M.kv + (size_t)l * kv_layer;
     uint16_t *vc = kc + kv_layer / 2;
     const int s_qkv = linear_splits(M.Nqkv, H, T, n_sms, M.part_rows);
     MCUDA(ctx, ctx_launch(ctx, "linear_qkv", [&] {
@@ -281,7 +331,8 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
           "qkv launch");
     MCUDA(ctx, ctx_launch(ctx, "qkv_rope", [&] {
             return launch_qkv_post(M.part, s_qkv, T, d.n_heads, d.n_kv_heads, A.bqkv, M.rope_cos, M.rope_sin,
-                                   pos0, dstate, (int)M.kv_stride, M.qb, kc, vc, s, tpos, trow);
+                                   pos0, dstate, (int)M.kv_stride, M.pages, M.max_pages, seq, M.qb, kc, vc, s,
+                                   tpos, tseq);
           }),
           "qkv epilogue launch");
     AttnArgs at;
@@ -294,7 +345,10 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     at.max_seq = (int)M.kv_stride;
     at.split_rows = d.max_seq;
     at.tok_pos = tpos;
-    at.tok_row0 = trow;
+    at.tok_seq = tseq;
+    at.pages = M.pages;
+    at.max_pages = M.max_pages;
+    at.seq = seq;
     at.max_splits = max_splits;
     at.pos0 = pos0;
     at.window = (l % 2 == 0) ? d.sliding_window : 0;
@@ -451,6 +505,9 @@ int decode_steps(oxg_ctx *ctx, ModelState &M, int n) {
   if (M.pos + n > M.d.max_seq)
     return mfail(ctx, OXG_ERR_SHAPE, "KV cache full: position %d + %d steps exceeds max_seq %d", M.pos, n,
                  M.d.max_seq);
+  // pages for every position the steps write (replays read the table on the device)
+  int rcp = ensure_pages(ctx, M, 0, M.pos + n - 1);
+  if (rcp) return rcp;
   // step counter back to 0 (tokens land in M.gen[0 ..)), position from the host
   MCUDA(ctx, ctx_launch(ctx, "decode_state", [&] {
           return launch_set_state(M.dstate, M.pos, M.dstate + 2, ctx_stream(ctx));
@@ -531,8 +588,14 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->part_rows = d.max_tokens > 1024 ? d.max_tokens : 1024;
   M->gen_cap = d.max_seq;
   M->B = d.max_batch > 1 ? d.max_batch : 1;
-  M->kv_stride = (size_t)M->B * d.max_seq;
+  M->max_pages = (d.max_seq + oxg::kKvPageRows - 1) / oxg::kKvPageRows;
+  M->n_pool = d.kv_pages > 0 ? d.kv_pages : M->B * M->max_pages;
+  M->kv_stride = (size_t)M->n_pool * oxg::kKvPageRows;
   M->seq_pos.assign(M->B, 0);
+  M->page_host.assign((size_t)M->B * M->max_pages, -1);
+  M->seq_npages.assign(M->B, 0);
+  M->free_pages.resize(M->n_pool);
+  for (int i = 0; i < M->n_pool; ++i) M->free_pages[i] = M->n_pool - 1 - i;  // page 0 is taken first
   const size_t H = d.hidden, Tm = d.max_tokens;
   const size_t nmax = (size_t)(M->Nqkv > d.hidden ? M->Nqkv : d.hidden);
   size_t off = 0;
@@ -552,6 +615,7 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   const size_t o_ds = take(4 * 4), o_first = take(4);
   const size_t o_amk = take(8 * 8), o_amc = take(4);
   const size_t o_tp = take((size_t)M->B * 4), o_tr = take((size_t)M->B * 4);
+  const size_t o_pg = take((size_t)M->B * M->max_pages * 4);
   cudaError_t e = cudaMalloc(&M->state, off);
   if (e) {
     delete M;
@@ -577,7 +641,8 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->am_keys = (unsigned long long *)(b + o_amk);
   M->am_count = (unsigned int *)(b + o_amc);
   M->tok_pos = (int32_t *)(b + o_tp);
-  M->tok_row0 = (int32_t *)(b + o_tr);
+  M->tok_seq = (int32_t *)(b + o_tr);
+  M->pages = (int32_t *)(b + o_pg);
   // RoPE tables: angle(pos, i) = pos * theta^(-2i / head_dim), i < head_dim / 2,
   // evaluated in double and rounded once to f32.
   std::vector<float> cs((size_t)d.max_seq * 32), sn((size_t)d.max_seq * 32);
@@ -594,6 +659,7 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   if (!e) e = cudaMemset(M->dstate, 0, 16);
   if (!e) e = cudaMemset(M->am_keys, 0, 8 * 8);
   if (!e) e = cudaMemset(M->am_count, 0, 4);
+  if (!e) e = cudaMemset(M->pages, 0, (size_t)M->B * M->max_pages * 4);
   if (e) {
     oxg::free_model(M);
     return oxg::mcuda(ctx, e, "model state initialisation");
@@ -649,7 +715,30 @@ int oxg_model_reset(oxg_ctx *ctx) {
   if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
   M->pos = 0;  // positions at or beyond pos are never read before they are written again
   for (int &p : M->seq_pos) p = 0;
+  for (int q = 0; q < M->B; ++q) oxg::release_pages(*M, q);
   M->state_ok = false;
+  return OXG_OK;
+}
+
+int oxg_model_reset_seq(oxg_ctx *ctx, int seq) {
+  if (!ctx) return oxg::ctx_error(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ModelState *M = oxg::get_model(ctx);
+  if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
+  if (seq < 0 || seq >= M->B)
+    return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "seq %d out of range [0, max_batch = %d)", seq, M->B);
+  oxg::seq_pos_ref(*M, seq) = 0;
+  oxg::release_pages(*M, seq);
+  if (seq == 0) M->state_ok = false;
+  return OXG_OK;
+}
+
+int oxg_model_kv_pages(oxg_ctx *ctx, int *used, int *total) {
+  if (!ctx) return oxg::ctx_error(nullptr, OXG_ERR_INVALID_ARG, "ctx is NULL");
+  ModelState *M = oxg::get_model(ctx);
+  if (!M) return oxg::mfail(ctx, OXG_ERR_STATE, "oxg_model_init has not been called");
+  if (!used || !total) return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "used and total must be non-NULL");
+  *total = M->n_pool;
+  *used = M->n_pool - (int)M->free_pages.size();
   return OXG_OK;
 }
 
@@ -766,16 +855,20 @@ int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens, int32_
       return oxg::mfail(ctx, OXG_ERR_SHAPE, "KV cache of sequence %d full: position %d + 1 exceeds max_seq %d", i, p,
                         M->d.max_seq);
     hp[i] = p;
-    hr[i] = i * M->d.max_seq;
-    const int sp = (p + 64) / 64;  // decode splits of 64 keys over positions 0 .. p
+    hr[i] = i;
+    const int sp = oxg::attn_page_splits(0, p);  // 64-key pages over positions 0 .. p
     if (sp > max_splits) max_splits = sp;
   }
   oxg::DevGuard g(oxg::ctx_device(ctx));
+  for (int i = 0; i < n_seqs; ++i) {
+    const int rc = oxg::ensure_pages(ctx, *M, i, hp[i]);
+    if (rc) return rc;
+  }
   cudaStream_t s = oxg::ctx_stream(ctx);
   // pageable sources: each copy is staged before the call returns
   MCUDA(ctx, cudaMemcpyAsync(M->tok_pos, hp.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s), "position copy");
-  MCUDA(ctx, cudaMemcpyAsync(M->tok_row0, hr.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s),
-        "cache row copy");
+  MCUDA(ctx, cudaMemcpyAsync(M->tok_seq, hr.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s),
+        "sequence copy");
   int rc = oxg::forward(ctx, *M, tokens, n_seqs, n_seqs, logits, next, nullptr, 0, true, max_splits);
   if (rc) return rc;
   for (int i = 0; i < n_seqs; ++i) oxg::seq_pos_ref(*M, i) += 1;

@@ -52,10 +52,12 @@ class GPTModel:
     """
 
     def __init__(self, weights: dict, *, max_seq: int = 4096, max_tokens: int = 2048, max_batch: int = 1,
-                 ctx: abi.Context | None = None, experts: tuple[int, int] | None = None):
+                 ctx: abi.Context | None = None, experts: tuple[int, int] | None = None, kv_pages: int = 0):
         """experts: (begin, count) to keep only that range of every MoE
         block's experts (expert parallelism; then ``connect_expert_parallel``
-        on every process before the first forward)."""
+        on every process before the first forward). kv_pages: pages of 64
+        positions in the KV-cache pool the sequences share (0: room for every
+        sequence at max_seq)."""
         # a context of its own (its layer ids 0..n_layers-1 must not collide
         # with other MoE layers), bound to torch's current stream
         self.ctx = ctx if ctx is not None else abi.Context(torch.cuda.current_device())
@@ -68,7 +70,8 @@ class GPTModel:
         self.max_tokens = int(min(max_tokens, max_seq))
         md = abi.ModelDims(self.n_layers, int(d["hidden"]), int(d["n_heads"]), int(d["n_kv_heads"]),
                            int(d["head_dim"]), self.vocab, int(d["sliding_window"]), self.max_seq,
-                           self.max_tokens, float(d["rope_theta"]), float(d["rms_eps"]), int(max_batch))
+                           self.max_tokens, float(d["rope_theta"]), float(d["rms_eps"]), int(max_batch),
+                           int(kv_pages))
         self.max_batch = max(int(max_batch), 1)
         lib, h = self.ctx.lib, self.ctx.handle
         abi.check(lib.oxg_model_init(h, ctypes.byref(md)), h)
@@ -124,6 +127,17 @@ class GPTModel:
     # -- reference-shaped API ------------------------------------------------
     def reset_kv_cache(self) -> None:
         abi.check(self.ctx.lib.oxg_model_reset(self.ctx.handle), self.ctx.handle)
+
+    def reset_sequence(self, seq: int) -> None:
+        """Empties sequence ``seq``'s cache and returns its pages to the pool."""
+        abi.check(self.ctx.lib.oxg_model_reset_seq(self.ctx.handle, int(seq)), self.ctx.handle)
+
+    def kv_pages(self) -> tuple[int, int]:
+        """(pages in use, pages in the pool) of the paged KV cache."""
+        used, total = ctypes.c_int(), ctypes.c_int()
+        abi.check(self.ctx.lib.oxg_model_kv_pages(self.ctx.handle, ctypes.byref(used), ctypes.byref(total)),
+                  self.ctx.handle)
+        return used.value, total.value
 
     def position(self) -> int:
         p = ctypes.c_int()

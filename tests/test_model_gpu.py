@@ -343,3 +343,62 @@ def test_batched_step_errors(small_model):
     with pytest.raises(abi.OxgError, match="seq 2 out of range"):
         gb.prefill_seq(2, [1, 2, 3])
     gb.release()
+
+
+def test_paged_kv_cache_interleaved_pages_give_the_same_bits(small_model):
+    """The KV cache is paged (64 positions per page, a pool the sequences
+    share). Three sequences prefilled in interleaved 64-token chunks own
+    interleaved pool pages; the same prompts in the same chunks prefilled one
+    sequence after another own contiguous runs (same kernels, other pages). Attention reads every key through the page table, so the
+    greedy tokens and the batched steps' logits must be bit-identical between
+    the two layouts. Then a small pool: a sequence that needs a page when none
+    is free fails with OXG_ERR_OOM and changes nothing, and resetting another
+    sequence returns its pages so the prefill goes through."""
+    import torch
+    from oxidized_gpt_oss_b200 import abi
+    m, _ = small_model
+    rng = np.random.default_rng(31)
+    # 3, 3 and 4 pages; the batched steps below move sequences 0 and 2 into a new page
+    prompts = [rng.integers(0, 4096, n) for n in (190, 150, 254)]
+
+    def run(interleaved):
+        g = _gpu_model(m, max_batch=3)
+        nxt = [None] * 3
+        if interleaved:
+            for c0 in range(0, 254, 64):
+                for i, p in enumerate(prompts):
+                    if c0 < len(p):
+                        nxt[i] = int(g.prefill_seq(i, p[c0:c0 + 64]).item())
+        else:  # the same 64-token chunks (the same kernels), one sequence after another
+            for i, p in enumerate(prompts):
+                for c0 in range(0, len(p), 64):
+                    nxt[i] = int(g.prefill_seq(i, p[c0:c0 + 64]).item())
+        used, total = g.kv_pages()
+        assert used == 3 + 3 + 4 and total == 3 * 8, (used, total)  # max_seq 512: 8 pages per sequence
+        toks = torch.tensor(nxt, dtype=torch.int32, device="cuda")
+        lg = []
+        for _ in range(4):  # positions 190-193 and 254-257 cross into a new page
+            logits = torch.empty((3, 4096), dtype=torch.float32, device="cuda")
+            toks = g.step_batch(toks, logits)
+            lg.append(logits.cpu().numpy())
+        assert g.kv_pages()[0] == 4 + 3 + 5
+        g.release()
+        return nxt, np.stack(lg)
+
+    n_a, lg_a = run(False)
+    n_b, lg_b = run(True)
+    assert n_a == n_b
+    assert np.array_equal(lg_a, lg_b)
+
+    g = _gpu_model(m, max_batch=3, kv_pages=7)
+    g.prefill_seq(0, prompts[0])            # 3 pages
+    g.prefill_seq(1, prompts[1][:128])      # 2 pages: 5 of 7 in use
+    with pytest.raises(abi.OxgError) as ei:
+        g.prefill_seq(2, prompts[2][:130])  # needs 3
+    assert ei.value.status == abi.OXG_ERR_OOM and "pool exhausted" in str(ei.value)
+    assert g.kv_pages() == (5, 7)
+    g.reset_sequence(1)
+    assert g.kv_pages() == (3, 7)
+    g.prefill_seq(2, prompts[2][:130])
+    assert g.kv_pages() == (6, 7)
+    g.release()
