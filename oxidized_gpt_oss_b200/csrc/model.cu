@@ -122,6 +122,15 @@ __device__ __forceinline__ float4 norm_value4(const float *__restrict__ r, const
   return v;
 }
 
+// The norm that feeds a MoE block lets the fused router (the only kernel of
+// this file's successors launched as a programmatic dependent) start at once:
+// it loads its read-only router rows, then waits for this kernel to complete
+// before it reads anything this kernel writes. Launches without the
+// programmatic attribute ignore the release.
+__device__ __forceinline__ void release_router() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kNormThreads)
     residual_norm_kernel(float *__restrict__ res, int H, const int32_t *__restrict__ tokens,
                          const uint16_t *__restrict__ embed, int V, const float *__restrict__ add, int S,
@@ -130,6 +139,7 @@ __global__ void __launch_bounds__(kNormThreads)
                          int *__restrict__ err) {
   extern __shared__ float4 vs4[];
   __shared__ float red[kNormThreads / 32];
+  release_router();
   const int t = blockIdx.x;
   float *r = res + (size_t)t * H;
   const uint16_t *erow = nullptr;
@@ -190,6 +200,7 @@ __global__ void __cluster_dims__(kNormCl, 1, 1) __launch_bounds__(kNormClThreads
   extern __shared__ float4 vc4[];
   __shared__ float red[kNormClThreads / 32];
   __shared__ float part_ss;
+  release_router();
   const int rank = (int)cl.block_rank();
   const int t = blockIdx.y;
   float *r = res + (size_t)t * H;

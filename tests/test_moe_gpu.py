@@ -76,6 +76,8 @@ def test_small_golden_fixture(cuda_ctx):
     (128, 64, 4, 2, 13),    # full groups only
     (2880, 2880, 32, 4, 3),
     (256, 224, 16, 4, 40),  # experts with > 8 tokens: several token passes
+    (192, 128, 64, 8, 17),  # fused routing, rank-count top-8 of 64 experts
+    (256, 128, 128, 4, 64),  # fused routing at its largest batch, arg-max top-k over 128 experts
     (128, 96, 8, 4, 80),    # beyond the fused-routing batch size: separate router/permute/combine
     (256, 224, 16, 4, 200),  # tensor-core router + scatter, decode kernels (I % 64 != 0)
     (512, 512, 32, 4, 300),  # tensor-core router + scatter/gather, prefill kernels; ragged last CTA
