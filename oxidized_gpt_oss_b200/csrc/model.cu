@@ -708,13 +708,56 @@ __device__ __forceinline__ bool ad_seek(AdCursor &c, int W, int n_items, int nkv
   return false;
 }
 
+// One warp merges the n_split partials (max, sum, unnormalised output) of
+// the 8 query heads h0 .. h0 + 7 and their sinks into the bf16 output row:
+// lane = (head lane / 4, 16 dims). Same arithmetic, in the same order, as
+// attn_combine_kernel: the running max from the sink over the splits in
+// order, then L and the outputs accumulated over the splits in order.
+__device__ __forceinline__ void merge_splits(const float *p0, int n_split, int h0, const uint16_t *sinks,
+                                             uint16_t *out_row, int lane) {
+  const int h = lane >> 2, dq = lane & 3;
+  const float *ph = p0 + h * 66;
+  const size_t stride = (size_t)8 * 66;
+  const float sink = sinks ? bf16_to_f32(sinks[h0 + h]) : -INFINITY;
+  float M = sink;
+#pragma unroll 8
+  for (int s = 0; s < n_split; ++s) M = fmaxf(M, __ldcg(ph + s * stride));
+  float L = sinks ? expf(sink - M) : 0.f;
+  float acc[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < n_split; ++s) {
+    const float *p = ph + s * stride;
+    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p));
+    float2 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(reinterpret_cast<const float2 *>(p + 2 + dq * 16) + j);
+    const float f = expf(ml.x - M);
+    L = fmaf(ml.y, f, L);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[2 * j] = fmaf(v[j].x, f, acc[2 * j]);
+      acc[2 * j + 1] = fmaf(v[j].y, f, acc[2 * j + 1]);
+    }
+  }
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    w[j] = f32_to_bf16_bits(acc[2 * j] / L) | (f32_to_bf16_bits(acc[2 * j + 1] / L) << 16);
+  uint4 *o = reinterpret_cast<uint4 *>(out_row + (size_t)(h0 + h) * 64 + dq * 16);
+  o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 __global__ void __launch_bounds__(kAdWarps * 32, 1)
     attn_decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const uint16_t *__restrict__ q,
                            const int32_t *__restrict__ tok_pos, const int32_t *__restrict__ tok_seq,
                            const int32_t *__restrict__ pages, int max_pages,
                            long long k_row, long long v_row, long long kv_stride, int nkv, int Nq, int window,
                            float scale, int max_split, int n_items, float *__restrict__ part, size_t part_tok,
-                           int *err) {
+                           int *err, unsigned *__restrict__ merge_cnt, const uint16_t *__restrict__ sinks,
+                           uint16_t *__restrict__ out) {
   extern __shared__ __align__(16) uint8_t ad_raw[];
   __shared__ __align__(8) uint64_t bars[kAdWarps][kAdStages];
   uint8_t *smem = ad_raw + ((1024 - (smem_addr(ad_raw) & 1023)) & 1023);
@@ -894,6 +937,20 @@ __global__ void __launch_bounds__(kAdWarps * 32, 1)
       d0[1] = l0;
       d1[0] = m1;
       d1[1] = l1;
+    }
+    // with merge_cnt: the last split of (token, kv head) to get here merges
+    // them all (else attn_combine_kernel does)
+    unsigned prev = 0u;
+    if (merge_cnt) {
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) prev = atomicAdd(&merge_cnt[it.t * nkv + it.kvh], 1u);
+    }
+    if (merge_cnt && __shfl_sync(0xffffffffu, prev, 0) == (unsigned)it.n_split - 1u) {
+      __threadfence();
+      if (lane == 0) merge_cnt[it.t * nkv + it.kvh] = 0u;  // zero again for the next launch
+      merge_splits(part + (size_t)it.t * part_tok + (size_t)it.kvh * it.n_split * 8 * 66, it.n_split,
+                   it.kvh * 8, sinks, out + (size_t)it.t * Nq, lane);
     }
     cc.idx += W;
     c_ok = ad_seek(cc, W, n_items, nkv, max_split, tok_pos, window);
@@ -1265,8 +1322,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t stream) {
     attn_decode_mma_kernel<<<grid, kAdWarps * 32, kAdSmem, stream>>>(
         *reinterpret_cast<const CUtensorMap *>(a.kv_map), a.q, a.tok_pos, a.tok_seq, a.pages, a.max_pages,
         a.k_row, a.v_row, (long long)a.max_seq, a.nkv, Nq, a.window, a.scale, max_split, n_items, a.part,
-        part_tok, a.err);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+        part_tok, a.err, a.merge_cnt, a.sinks, a.out);
+    if ((st = cudaGetLastError()) != cudaSuccess || a.merge_cnt) return st;
     attn_combine_kernel<<<dim3(a.nh, a.T), 64, 0, stream>>>(a.part, G, max_split, nullptr, a.window, a.sinks,
                                                            a.out, a.tok_pos, Nq, part_tok, kAdKeys);
     return cudaGetLastError();

@@ -89,6 +89,11 @@ struct AttnArgs {
   long long k_row = 0, v_row = 0;
   int n_sms = 0;
   int *err = nullptr;            // timeout code of the tensor-core decode kernel
+  // tensor-core kernel: per (token, kv head) arrival counters [T * nkv], zero
+  // between launches; the last split to finish merges the splits and the sink
+  // (null: attn_combine_kernel merges them — for large batches, where the
+  // fence before each split's arrival stalls the warps' TMA streams)
+  unsigned *merge_cnt = nullptr;
 };
 // A 2-D tensor map over the KV cache `kv` of `rows` rows of 64 bf16 (128-byte
 // swizzle, 64-row boxes) into map (128 bytes, 64-byte aligned); rows < 2^31.

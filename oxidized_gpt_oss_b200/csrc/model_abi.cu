@@ -65,7 +65,8 @@ struct ModelState {
   int B = 1;                   // sequences with a KV cache of their own
   size_t kv_stride = 0;        // cache rows per kv head: the page pool, n_pool * 64
   std::vector<int> seq_pos;    // positions of sequences 1 .. B-1 (index 0 unused)
-  int32_t *tok_pos = nullptr, *tok_seq = nullptr;  // batched step: [B] position, sequence
+  unsigned *merge_cnt = nullptr;  // tensor-core decode attention: per (sequence, kv head) arrivals
+  int32_t *tok_pos = nullptr, *tok_seq = nullptr;  // batched step: [B] position; [B] sequence ids 0 .. B-1
   // paged KV cache: page table [B][max_pages] on the device and its host
   // mirror (-1: no page), the free pool pages, and each sequence's page count
   int32_t *pages = nullptr;
@@ -318,6 +319,13 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     MCUDA(ctx, ctx_launch(ctx, "embed_norm", [&] { return launch_residual_norm(a, s); }), "embed launch");
   }
   const float scale = 1.0f / std::sqrt((float)d.head_dim);
+  // A single query of one sequence runs the tensor-core decode attention of
+  // the batched step, with its position read from the device (the decode
+  // state, or M.tok_pos written here), so eager one-token forwards and graph
+  // replays compute the same bits.
+  const bool one_query = !batch && T == 1 && M.kv_map_ok && M.G == 8;
+  if (one_query && !dstate)
+    MCUDA(ctx, cudaMemcpyAsync(M.tok_pos, &pos0, 4, cudaMemcpyHostToDevice, s), "position copy");
   const size_t kv_layer = (size_t)2 * d.n_kv_heads * M.kv_stride * 64;
   const int32_t *tpos = batch ? M.tok_pos : nullptr, *tseq = batch ? M.tok_seq : nullptr;
   for (int l = 0; l < L; ++l) {
@@ -356,12 +364,18 @@ int forward(oxg_ctx *ctx, ModelState &M, const int32_t *tok, int T, int n_logits
     at.sinks = A.sinks;
     at.part = M.apart;
     at.pos_dev = dstate;
-    if (batch && M.kv_map_ok) {
+    if (one_query) {  // one query of one sequence: the batched kernel, its position on the device
+      at.tok_pos = dstate ? dstate : M.tok_pos;
+      at.tok_seq = M.tok_seq + seq;
+      at.max_splits = (d.max_seq + kKvPageRows - 1) / kKvPageRows;
+    }
+    if ((batch || one_query) && M.kv_map_ok) {
       at.kv_map = M.kv_map;
       at.k_row = (long long)l * 2 * d.n_kv_heads * (long long)M.kv_stride;
       at.v_row = at.k_row + (long long)d.n_kv_heads * (long long)M.kv_stride;
       at.n_sms = n_sms;
       at.err = M.err;
+      if (one_query) at.merge_cnt = M.merge_cnt;
     }
     at.out = M.cb;
     MCUDA(ctx, ctx_launch(ctx, "attention", [&] { return launch_attention(at, s); }), "attention launch");
@@ -555,6 +569,8 @@ int model_check_error(oxg_ctx *ctx) {
   MCUDA(ctx, cudaMemcpy(&h, M->err, sizeof(int), cudaMemcpyDeviceToHost), "read model status");
   if (h) {
     MCUDA(ctx, cudaMemset(M->err, 0, sizeof(int)), "clear model status");
+    // a split that stopped early never arrived: its counters start again at zero
+    MCUDA(ctx, cudaMemset(M->merge_cnt, 0, (size_t)M->B * M->d.n_kv_heads * 4), "clear attention counters");
     if (h == 61)
       return mfail(ctx, OXG_ERR_TIMEOUT, "a KV tile load of the decode attention did not complete (code 61)");
     return mfail(ctx, OXG_ERR_INVALID_ARG, "a token id outside [0, vocab = %d) was given (code %d)", M->d.vocab, h);
@@ -616,6 +632,7 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   const size_t o_amk = take(8 * 8), o_amc = take(4);
   const size_t o_tp = take((size_t)M->B * 4), o_tr = take((size_t)M->B * 4);
   const size_t o_pg = take((size_t)M->B * M->max_pages * 4);
+  const size_t o_mc = take((size_t)M->B * d.n_kv_heads * 4);
   cudaError_t e = cudaMalloc(&M->state, off);
   if (e) {
     delete M;
@@ -643,6 +660,7 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   M->tok_pos = (int32_t *)(b + o_tp);
   M->tok_seq = (int32_t *)(b + o_tr);
   M->pages = (int32_t *)(b + o_pg);
+  M->merge_cnt = (unsigned *)(b + o_mc);
   // RoPE tables: angle(pos, i) = pos * theta^(-2i / head_dim), i < head_dim / 2,
   // evaluated in double and rounded once to f32.
   std::vector<float> cs((size_t)d.max_seq * 32), sn((size_t)d.max_seq * 32);
@@ -660,6 +678,12 @@ int oxg_model_init(oxg_ctx *ctx, const oxg_model_dims *dims) {
   if (!e) e = cudaMemset(M->am_keys, 0, 8 * 8);
   if (!e) e = cudaMemset(M->am_count, 0, 4);
   if (!e) e = cudaMemset(M->pages, 0, (size_t)M->B * M->max_pages * 4);
+  if (!e) e = cudaMemset(M->merge_cnt, 0, (size_t)M->B * d.n_kv_heads * 4);
+  if (!e) {  // sequence ids: entry i is i (a one-sequence call reads entry seq)
+    std::vector<int32_t> ids((size_t)M->B);
+    for (int i = 0; i < M->B; ++i) ids[(size_t)i] = i;
+    e = cudaMemcpy(M->tok_seq, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice);
+  }
   if (e) {
     oxg::free_model(M);
     return oxg::mcuda(ctx, e, "model state initialisation");
@@ -847,7 +871,7 @@ int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens, int32_
   if (n_seqs <= 0 || n_seqs > M->B)
     return oxg::mfail(ctx, OXG_ERR_SHAPE, "n_seqs must be in [1, max_batch = %d], got %d", M->B, n_seqs);
   if (!tokens || !next) return oxg::mfail(ctx, OXG_ERR_INVALID_ARG, "tokens_dev and next_dev must be non-NULL");
-  std::vector<int32_t> hp(n_seqs), hr(n_seqs);
+  std::vector<int32_t> hp(n_seqs);
   int max_splits = 1;
   for (int i = 0; i < n_seqs; ++i) {
     const int p = oxg::seq_pos_ref(*M, i);
@@ -855,7 +879,6 @@ int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens, int32_
       return oxg::mfail(ctx, OXG_ERR_SHAPE, "KV cache of sequence %d full: position %d + 1 exceeds max_seq %d", i, p,
                         M->d.max_seq);
     hp[i] = p;
-    hr[i] = i;
     const int sp = oxg::attn_page_splits(0, p);  // 64-key pages over positions 0 .. p
     if (sp > max_splits) max_splits = sp;
   }
@@ -867,8 +890,6 @@ int oxg_model_step_batch(oxg_ctx *ctx, int n_seqs, const int32_t *tokens, int32_
   cudaStream_t s = oxg::ctx_stream(ctx);
   // pageable sources: each copy is staged before the call returns
   MCUDA(ctx, cudaMemcpyAsync(M->tok_pos, hp.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s), "position copy");
-  MCUDA(ctx, cudaMemcpyAsync(M->tok_seq, hr.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, s),
-        "sequence copy");
   int rc = oxg::forward(ctx, *M, tokens, n_seqs, n_seqs, logits, next, nullptr, 0, true, max_splits);
   if (rc) return rc;
   for (int i = 0; i < n_seqs; ++i) oxg::seq_pos_ref(*M, i) += 1;
