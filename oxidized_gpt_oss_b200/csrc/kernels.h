@@ -105,6 +105,10 @@ struct RouteSmallArgs {
   // consecutive slots ("virtual experts", expert order then slot order):
   // expert id, first position and slot count of each, and their number
   int32_t *v_expert, *v_pos0, *v_count, *n_virtual;
+  // optional (expert-parallel dispatch, the batched router's outputs for one
+  // CTA of <= 64 tokens): per expert the slot count [E], and per slot its
+  // rank among the earlier slots of its expert [T, k]
+  int32_t *cta_hist, *local_rank;
 };
 constexpr int kVirtualTokens = 8;
 // Upper bound on the virtual experts of T tokens routed top-k over E experts.

@@ -1711,7 +1711,34 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
   const oxg::EpLayout lay = q.lay;
   const oxg::EpPeers peers = q.peers;
   const int n_cta = oxg::router_mma_ctas(T);
-  if (T > 0) {
+  if (T > 0 && T <= oxg::kMaxRouteTokens) {
+    // a decode-sized batch: the fused per-token router, which also gives the
+    // one CTA's histogram and slot ranks the dispatch reads (and routes each
+    // token as oxg_moe_forward does on one GPU)
+    oxg::RouteSmallArgs ra{};
+    ra.x = x;
+    ra.router_w = L->router_w;
+    ra.router_b = L->router_b;
+    ra.T = T;
+    ra.H = d.hidden;
+    ra.E = d.n_experts;
+    ra.k = d.top_k;
+    ra.logits = ctx->ws.logits;
+    ra.sigma = ctx->ws.sigma;
+    ra.idx = ctx->ws.idx;
+    ra.wts = ctx->ws.wts;
+    ra.counts = ctx->ws.counts;
+    ra.offsets = ctx->ws.offsets;
+    ra.perm = ctx->ws.perm;
+    ra.slot_pos = ctx->ws.slot_pos;
+    ra.active = ctx->ws.active;
+    ra.n_active = ctx->ws.n_active;
+    ra.done = ctx->ws.done;
+    ra.cta_hist = ctx->ws.cta_hist;
+    ra.local_rank = ctx->ws.local_rank;
+    OXG_CUDA(ctx, launch(ctx, "route_small", [&] { return oxg::launch_route_small(ra, ctx->stream, true); }),
+             "route_small launch");
+  } else if (T > 0) {
     OXG_CUDA(ctx, launch(ctx, "router_mma", [&] {
                return oxg::launch_router_mma(x, L->router_w, L->router_b, T, d.hidden, d.n_experts,
                                              d.top_k, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits,

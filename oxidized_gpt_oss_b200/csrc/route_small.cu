@@ -23,8 +23,9 @@
 //      expert: counts, offsets, the active-expert list and the virtual
 //      experts by warp prefix scans, each slot's rank among the earlier
 //      slots of its expert by match_any over slot-ordered chunks of 32, the
-//      token masks of the block-scaled path, and the reset of the mlp2
-//      kernel's per-band counters. The counter is left at zero.
+//      token masks of the block-scaled path, the expert-parallel dispatch's
+//      per-expert counts and slot ranks, and the reset of the mlp2 kernel's
+//      per-band counters. The counter is left at zero.
 // A token's logits come from the same per-lane chunk order and xor reduction
 // whatever T is, so a token routes identically alone or in a batch.
 #include "common.cuh"
@@ -230,6 +231,7 @@ __device__ __forceinline__ void group_slots(const RouteSmallArgs &a, int *idx_s,
           }
         }
         if (masks) a.tok_mask[x] = mask_s[x];
+        if (a.cta_hist) a.cta_hist[x] = c;
       }
       run += __shfl_sync(0xFFFFFFFFu, cs, 31);
       n_act += __shfl_sync(0xFFFFFFFFu, as, 31);
@@ -249,9 +251,11 @@ __device__ __forceinline__ void group_slots(const RouteSmallArgs &a, int *idx_s,
       const int ex = s < S ? idx_s[s] : -1;
       const uint32_t peers = __match_any_sync(0xFFFFFFFFu, ex);
       if (s < S) {
-        const int p = off_s[ex] + run_s[ex] + __popc(peers & lt);
+        const int r = run_s[ex] + __popc(peers & lt);
+        const int p = off_s[ex] + r;
         a.perm[p] = s;
         a.slot_pos[s] = p;
+        if (a.local_rank) a.local_rank[s] = r;
       }
       __syncwarp();
       if (s < S && lane == 31 - __clz(peers)) run_s[ex] += __popc(peers);
