@@ -77,7 +77,10 @@ constexpr int kW3 = OXG_DEC_W3, kS3 = OXG_DEC_S3;  // mlp2 with at most 8 tokens
 #define OXG_DEEP_TOKENS 2
 #endif
 constexpr int kDeepTokens = OXG_DEEP_TOKENS;
-constexpr int kW1d = 28, kS1d = 5, kK1d = 4;  // mlp1: 7 groups of 4 warps splitting K
+// mlp1: 5 groups of 4 warps splitting K, 7 ring stages each. At one token
+// (4 experts x 360 tiles) 5 groups per SM take 1440 / 740 = 1.95 rounds of
+// tiles (7 groups: 1.39 rounds, the second mostly idle): 18.9 against 21.0 us.
+constexpr int kW1d = 20, kS1d = 7, kK1d = 4;
 constexpr int kW3d = 20, kS3d = 7, kK3d = 4;  // mlp2: 5 groups of 4 warps splitting K
 constexpr int kMaxAllTokActive = 128;  // active experts of an all-token mlp1 launch (T*k <= 128)
 // Flat-split kernels: warps x ring stages per CTA, one CTA per SM. mlp1
