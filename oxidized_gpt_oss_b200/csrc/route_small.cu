@@ -176,16 +176,17 @@ __device__ __forceinline__ void split_x_terms(const RouteSmallArgs &a, const uin
 }
 
 // Grouping of the S = T*k slots by expert, run by the whole (last) CTA once
-// every token's idx is in global memory: counts, offsets, the active-expert
-// list and the virtual experts by warp scans over chunks of 32 experts
-// (expert order, so the lists come out sorted), then perm / slot_pos with
-// each slot's rank among the earlier slots of its expert (slot order), and
-// the per-expert token masks of the block-scaled path (T <= 32).
-__device__ __forceinline__ void group_slots(const RouteSmallArgs &a, int *idx_s, int *cnt_s, int *off_s,
-                                            int *run_s, uint32_t *mask_s) {
+// every token's idx is in global memory (or, for one token, in idx_local):
+// counts, offsets, the active-expert list and the virtual experts by warp
+// scans over chunks of 32 experts (expert order, so the lists come out
+// sorted), then perm / slot_pos with each slot's rank among the earlier
+// slots of its expert (slot order), and the per-expert token masks of the
+// block-scaled path (T <= 32).
+__device__ __forceinline__ void group_slots(const RouteSmallArgs &a, const int *idx_local, int *idx_s,
+                                            int *cnt_s, int *off_s, int *run_s, uint32_t *mask_s) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = a.E, k = a.k, S = a.T * a.k;
-  for (int s = tid; s < S; s += blockDim.x) idx_s[s] = __ldcg(a.idx + s);
+  for (int s = tid; s < S; s += blockDim.x) idx_s[s] = idx_local ? idx_local[s] : __ldcg(a.idx + s);
   for (int x = tid; x < E; x += blockDim.x) {
     cnt_s[x] = 0;
     run_s[x] = 0;
@@ -328,19 +329,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1) route_token_kernel(RouteSmallA
       select_topk_softmax(logit_s, E, k, lane, a.idx + t * k, a.wts + t * k);
   }
 
-  // ---- hand over to the last token's rank 0 ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(a.done, 1u) == gridDim.y - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+  // ---- hand over to the last token's rank 0 (one token: this CTA) ----
+  const bool single = gridDim.y == 1;
+  if (!single) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(a.done, 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+  } else {
+    __syncthreads();
+  }
 
-  group_slots(a, idx_s, cnt_s, off_s, run_s, mask_s);
+  group_slots(a, single ? top_i_s : nullptr, idx_s, cnt_s, off_s, run_s, mask_s);
   for (int b = tid; b < a.n_bands; b += blockDim.x) a.band_done[b] = 0u;
-  if (tid == 0) *a.done = 0u;
-  __threadfence();
-  __syncthreads();
+  if (tid == 0 && !single) *a.done = 0u;
+  // the dependents read all of this after their griddepcontrol.wait, which
+  // waits for this grid to complete and its writes to be visible
   pdl_launch();
 }
 
