@@ -594,7 +594,7 @@ def run_prefill(args, ws, rank, local):
     rows_profiled = rows_done[0]
     names = ("router_topk", "router_mma", "permute", "gather_f16", "scatter_gather", "moe_mlp1_prefill",
              "moe_mlp2_prefill", "scatter_e4m3", "gather_e4m3", "mxf_gemm1", "mxf_gemm2", "combine",
-             "ep_counts", "ep_wait", "ep_scatter", "ep_signal", "ep_segments")
+             "ep_counts", "ep_scatter", "ep_signal", "ep_segments")
     k_ms = {n: ctx.profile_read(n) for n in names}
     k_ms = {n: v for n, v in k_ms.items() if v[1] > 0}
     mxf = "mxf_gemm1" in k_ms
@@ -955,7 +955,7 @@ def run_model(args, ws, rank, local):
 
 
 ZIPF_S = 1.1
-BATCH_KERNELS = MODEL_KERNELS + ("router_topk", "permute", "combine", "router_mma", "ep_counts", "ep_wait",
+BATCH_KERNELS = MODEL_KERNELS + ("router_topk", "permute", "combine", "router_mma", "ep_counts",
                                   "ep_scatter", "ep_segments", "moe_ep_decode", "ep_signal")
 
 

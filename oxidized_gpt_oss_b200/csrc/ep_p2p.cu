@@ -7,9 +7,10 @@
 // receive rows and the return rows (EpLayout, kernels.h). One forward is:
 //
 //   router_mma_kernel        idx, weights, sigma, per-CTA histograms and ranks
+//                            (route_token_kernel for batches of <= 64 tokens)
 //   ep_counts_kernel         this rank's per-expert counts into every rank's
-//                            inbox, then a counts flag to every rank
-//   ep_wait_kernel (counts)  all ranks' counts are here
+//                            inbox, then a counts flag to every rank; then it
+//                            waits until all ranks' counts are here
 //   ep_scatter_kernel        each slot's f16 operand row (x * 2^-sigma) and its
 //                            2^sigma stored straight into the destination
 //                            rank's receive rows; the last CTA raises a rows
@@ -20,8 +21,8 @@
 //                            output rows go: the source rank's return rows
 //   GEMM1, GEMM2             the resident experts (GEMM2's epilogue stores each
 //                            row into its source's return rows)
-//   ep_signal_kernel         a returns flag to every rank
-//   ep_wait_kernel (returns) every rank has sent this rank's rows back
+//   ep_signal_kernel         a returns flag to every rank, then it waits
+//                            until every rank has sent this rank's rows back
 //   combine_kernel           as on one GPU, from the return rows
 //
 // Flags carry the forward's epoch (increasing per forward), so nothing is
@@ -93,7 +94,7 @@ __device__ bool wait_flags(const EpLayout &L, const EpPeers &P, int kind, uint32
 __global__ void __launch_bounds__(256) ep_counts_kernel(EpLayout L, EpPeers P,
                                                         const int32_t *__restrict__ cta_hist,
                                                         int n_cta, int32_t *counts, int32_t *offsets,
-                                                        int *ok_word, uint32_t epoch) {
+                                                        int *ok_word, uint32_t epoch, int *err, int code) {
   __shared__ int tot_s[kEpMaxExperts], before_s[kEpMaxExperts], part_s[2 * 256];
   if (threadIdx.x == 0) *ok_word = 1;
   hist_prefix<256>(cta_hist, n_cta, L.E, n_cta, before_s, tot_s, part_s);
@@ -113,11 +114,8 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpLayout L, EpPeers P,
   __threadfence_system();  // every writer orders its own stores before the flag
   __syncthreads();
   if (threadIdx.x == 0) raise_flags(L, P, 0, epoch, true);
-}
-
-__global__ void ep_wait_kernel(EpLayout L, EpPeers P, int kind, uint32_t epoch, int *err, int code,
-                               int *ok_word) {
-  if (!wait_flags(L, P, kind, epoch, err, code) && (threadIdx.x & 31) == 0) *ok_word = 0;
+  // then every rank's counts
+  if (threadIdx.x < 32 && !wait_flags(L, P, 0, epoch, err, code) && threadIdx.x == 0) *ok_word = 0;
 }
 
 // As scatter_kernel (permute.cu) for the positions; rows go to the owner of
@@ -266,8 +264,11 @@ __global__ void __launch_bounds__(256) ep_segments_kernel(EpLayout L, EpPeers P,
   }
 }
 
-__global__ void ep_signal_kernel(EpLayout L, EpPeers P, int kind, uint32_t epoch, const int *ok_word) {
+__global__ void ep_signal_kernel(EpLayout L, EpPeers P, int kind, uint32_t epoch, int *ok_word, int *err,
+                                 int code) {
   if (threadIdx.x == 0) raise_flags(L, P, kind, epoch, *(volatile const int *)ok_word != 0);
+  __syncwarp();
+  if (err && !wait_flags(L, P, kind, epoch, err, code) && threadIdx.x == 0) *ok_word = 0;
 }
 
 }  // namespace
@@ -300,15 +301,9 @@ EpLayout ep_layout(int W, int E, int H, int k, int rank, long long max_tokens, l
 }
 
 cudaError_t launch_ep_counts(const EpLayout &L, const EpPeers &P, const int32_t *cta_hist, int n_cta,
-                             int32_t *counts, int32_t *offsets, int *ok_word, uint32_t epoch,
-                             cudaStream_t stream) {
-  ep_counts_kernel<<<1, 256, 0, stream>>>(L, P, cta_hist, n_cta, counts, offsets, ok_word, epoch);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_ep_wait(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch, int *err,
-                           int code, int *ok_word, cudaStream_t stream) {
-  ep_wait_kernel<<<1, 32, 0, stream>>>(L, P, kind, epoch, err, code, ok_word);
+                             int32_t *counts, int32_t *offsets, int *ok_word, uint32_t epoch, int *err,
+                             int code, cudaStream_t stream) {
+  ep_counts_kernel<<<1, 256, 0, stream>>>(L, P, cta_hist, n_cta, counts, offsets, ok_word, epoch, err, code);
   return cudaGetLastError();
 }
 
@@ -332,9 +327,9 @@ cudaError_t launch_ep_segments(const EpLayout &L, const EpPeers &P, uint32_t epo
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch,
-                             const int *ok_word, cudaStream_t stream) {
-  ep_signal_kernel<<<1, 32, 0, stream>>>(L, P, kind, epoch, ok_word);
+cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch, int *ok_word,
+                             int *err, int code, cudaStream_t stream) {
+  ep_signal_kernel<<<1, 32, 0, stream>>>(L, P, kind, epoch, ok_word, err, code);
   return cudaGetLastError();
 }
 

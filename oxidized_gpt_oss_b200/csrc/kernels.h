@@ -307,12 +307,11 @@ struct EpPeers {
   char *base[kEpMaxRanks];  // every rank's symmetric buffer as mapped here ([rank]: own)
 };
 EpLayout ep_layout(int W, int E, int H, int k, int rank, long long max_tokens, long long max_recv);
+// The counts into every rank's inbox, then (the same launch) the wait for
+// every rank's counts flag; a wait that runs out records `code` in err.
 cudaError_t launch_ep_counts(const EpLayout &L, const EpPeers &P, const int32_t *cta_hist, int n_cta,
-                             int32_t *counts, int32_t *offsets, int *ok_word, uint32_t epoch,
-                             cudaStream_t stream);
-// kind 0: counts, 2: returns (rows are awaited by launch_ep_segments)
-cudaError_t launch_ep_wait(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch, int *err,
-                           int code, int *ok_word, cudaStream_t stream);
+                             int32_t *counts, int32_t *offsets, int *ok_word, uint32_t epoch, int *err,
+                             int code, cudaStream_t stream);
 cudaError_t launch_ep_scatter(const EpLayout &L, const EpPeers &P, const int32_t *cta_hist, int n_cta,
                               const int32_t *idx, const int32_t *local_rank, int T, const uint16_t *x,
                               const int32_t *sigma, int32_t *slot_pos, uint32_t *done_ctr,
@@ -330,8 +329,10 @@ struct EpVirtual {
 cudaError_t launch_ep_segments(const EpLayout &L, const EpPeers &P, uint32_t epoch, int *err,
                                int *ok_word, int32_t *seg, float **seg_ptr, const EpVirtual &virt,
                                cudaStream_t stream);
-cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch,
-                             const int *ok_word, cudaStream_t stream);
+// Raises flag `kind` (1: rows, 2: returns) on every rank; with err, the same
+// launch then waits for every rank's flag of that kind (code on a timeout).
+cudaError_t launch_ep_signal(const EpLayout &L, const EpPeers &P, int kind, uint32_t epoch, int *ok_word,
+                             int *err, int code, cudaStream_t stream);
 
 // Expert-parallel decode on the receiving rank: the resident experts' MLPs
 // over the received rows (f16 x * 2^-sigma [R, H] with their 2^sigma), in the

@@ -1749,13 +1749,9 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
   }
   OXG_CUDA(ctx, launch(ctx, "ep_counts", [&] {
              return oxg::launch_ep_counts(lay, peers, ctx->ws.cta_hist, n_cta, ctx->ws.counts,
-                                          ctx->ws.offsets, q.ok_word, epoch, ctx->stream);
+                                          ctx->ws.offsets, q.ok_word, epoch, ctx->ws.err, 11, ctx->stream);
            }),
            "ep_counts launch");
-  OXG_CUDA(ctx, launch(ctx, "ep_wait", [&] {
-             return oxg::launch_ep_wait(lay, peers, 0, epoch, ctx->ws.err, 11, q.ok_word, ctx->stream);
-           }),
-           "ep_wait launch");
   if (T > 0) {
     OXG_CUDA(ctx, launch(ctx, "ep_scatter", [&] {
                return oxg::launch_ep_scatter(lay, peers, ctx->ws.cta_hist, n_cta, ctx->ws.idx,
@@ -1765,7 +1761,7 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
              "ep_scatter launch");
   } else {  // nothing to send: raise the rows flags at once
     OXG_CUDA(ctx, launch(ctx, "ep_signal", [&] {
-               return oxg::launch_ep_signal(lay, peers, 1, epoch, q.ok_word, ctx->stream);
+               return oxg::launch_ep_signal(lay, peers, 1, epoch, q.ok_word, nullptr, 0, ctx->stream);
              }),
              "ep_signal launch");
   }
@@ -1818,13 +1814,9 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
            "prefill mlp2 launch");
   }
   OXG_CUDA(ctx, launch(ctx, "ep_signal", [&] {
-             return oxg::launch_ep_signal(lay, peers, 2, epoch, q.ok_word, ctx->stream);
+             return oxg::launch_ep_signal(lay, peers, 2, epoch, q.ok_word, ctx->ws.err, 13, ctx->stream);
            }),
            "ep_signal launch");
-  OXG_CUDA(ctx, launch(ctx, "ep_wait", [&] {
-             return oxg::launch_ep_wait(lay, peers, 2, epoch, ctx->ws.err, 13, q.ok_word, ctx->stream);
-           }),
-           "ep_wait launch");
   ctx->prefill_pending = true;
   if (T == 0) return OXG_OK;
   OXG_CUDA(ctx, launch(ctx, "combine", [&] {
