@@ -40,15 +40,17 @@ cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint1
                                int32_t *sigma, cudaStream_t stream);
 
 // Batched router on the tensor cores for E a multiple of 16 (<= 64) and H a
-// multiple of 16: the same outputs as launch_router_topk plus, per CTA of
-// router_mma_ctas(T) CTAs, the expert histogram cta_hist[cta, E] and each
-// slot's rank among the CTA's slots of its expert, local_rank[T*k] (slot order).
+// multiple of 16: the same outputs as launch_router_topk plus, per unit of 64
+// tokens (router_mma_ctas(T) units), the expert histogram cta_hist[unit, E]
+// and each slot's rank among the unit's slots of its expert, local_rank[T*k]
+// (slot order). With err (a pipeline error word) and H a multiple of 64 it
+// runs on tcgen05 (TMA-fed, bounded waits), else on mma.sync.
 bool router_mma_supported(int H, int E, int k);
 int router_mma_ctas(int T);
 cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
                               int E, int k, int32_t *idx, float *wts, float *logits,
                               int32_t *sigma, int32_t *cta_hist, int32_t *local_rank,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int *err = nullptr);
 
 // ---- permutation (permute.cu) -------------------------------------------------
 // Stable counting sort of the T*k (token, j) slots by expert.

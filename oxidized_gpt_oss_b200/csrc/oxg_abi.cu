@@ -466,9 +466,10 @@ int route(oxg_ctx *ctx, Layer &L, const uint16_t *x, int T, int32_t *idx, float 
     OXG_CUDA(ctx, launch(ctx, "router_mma", [&] {
                return oxg::launch_router_mma(x, L.router_w, L.router_b, T, d.hidden, d.n_experts,
                                              d.top_k, idx, wts, logits, ctx->ws.sigma,
-                                             ctx->ws.cta_hist, ctx->ws.local_rank, ctx->stream);
+                                             ctx->ws.cta_hist, ctx->ws.local_rank, ctx->stream, ctx->ws.err);
              }),
              "router_mma launch");
+    ctx->prefill_pending = true;  // its bounded waits report a timeout in the error word
     return OXG_OK;
   }
   OXG_CUDA(ctx, launch(ctx, "router_topk", [&] {
@@ -1743,7 +1744,7 @@ int oxg_moe_forward_ep(oxg_ctx *ctx, int layer, const uint16_t *x, int T, float 
                return oxg::launch_router_mma(x, L->router_w, L->router_b, T, d.hidden, d.n_experts,
                                              d.top_k, ctx->ws.idx, ctx->ws.wts, ctx->ws.logits,
                                              ctx->ws.sigma, ctx->ws.cta_hist, ctx->ws.local_rank,
-                                             ctx->stream);
+                                             ctx->stream, ctx->ws.err);
              }),
              "router_mma launch");
   }

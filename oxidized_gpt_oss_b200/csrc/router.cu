@@ -18,8 +18,11 @@
 // value (8 significant bits) converts to f16 exactly down to 2^-17, so every
 // element of magnitude >= 2^-31 max|x| is exact; smaller ones are rounded to
 // the f16 subnormal grid with absolute error <= 2^-39 max|x|.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace oxg {
 namespace {
@@ -307,6 +310,224 @@ __global__ void __launch_bounds__(kRmThreads) router_mma_kernel(
   }
 }
 
+
+// ---- batched router on tcgen05 -------------------------------------------------
+// One CTA per 128 tokens (M = 128 of a kind::f16 MMA with bf16 operands, N =
+// E experts, f32 accumulator in TMEM), the x tile and the router rows (both
+// K-major, 64 columns per stage, 128-byte swizzle) streamed by TMA through a
+// kTcStages-deep ring:
+//   warp 0     TMA producer (one thread)
+//   warp 1     TMEM owner and MMA issuer (one thread): 4 MMAs of K 16 per stage
+//   warps 2-5  one token row per thread (the thread's TMEM lane): max|x| of
+//              its row from each stage's x tile (a stage is free once the
+//              MMAs and these four warps are done with it); then the logits
+//              from TMEM, bias, top-k and softmax of its token (the same
+//              selection and arithmetic as rank_topk_softmax), and per 64-token
+//              half of the tile the histogram and slot ranks of the counting
+//              sort (the batched router's outputs, in its 64-token units).
+// Every wait is bounded: a timeout records code 14 in *err and the pipeline
+// drains without hanging.
+constexpr int kTcTokens = 128;
+constexpr int kTcBK = 64;
+constexpr int kTcStages = 6;
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcXBytes = kTcTokens * kTcBK * 2;  // 16 KB
+
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+  return (1u << 4)                          // D format: f32
+         | (1u << 7) | (1u << 10)           // A, B format: bf16
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+template <int EMAX>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                     const uint16_t *__restrict__ b, int T, int H, int E, int k, int32_t *__restrict__ idx,
+                     float *__restrict__ wts, float *__restrict__ logits_out, int32_t *__restrict__ sigma_out,
+                     int32_t *__restrict__ cta_hist, int32_t *__restrict__ local_rank, int *err) {
+  extern __shared__ uint8_t tc_raw[];
+  uint8_t *smem = tc_raw + ((1024u - (sm100::smem_addr(tc_raw) & 1023u)) & 1023u);
+  __shared__ uint64_t full_[kTcStages], empty_[kTcStages], acc_full;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int idx_s[kTcTokens * kMaxTopK];
+  __shared__ int cnt_s[2][EMAX];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kTcTokens;
+  const uint32_t w_bytes = (uint32_t)E * kTcBK * 2;
+  const uint32_t stage_bytes = kTcXBytes + EMAX * kTcBK * 2;
+  const int KSTEPS = H / kTcBK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      sm100::mbar_init(&full_[s], 1);
+      sm100::mbar_init(&empty_[s], 1 + 4);  // the MMA commit + the four row warps
+    }
+    sm100::mbar_init(&acc_full, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(&tmem_slot, EMAX);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::prefetch_tmap(&xmap);
+      sm100::prefetch_tmap(&wmap);
+      int issued = 0;
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        const int s = ks % kTcStages, r = ks / kTcStages;
+        if (r > 0 && !sm100::mbar_wait(&empty_[s], (r - 1) & 1, err, 14)) break;
+        uint8_t *st = smem + (size_t)s * stage_bytes;
+        sm100::mbar_arrive_expect_tx(&full_[s], kTcXBytes + w_bytes);
+        sm100::tma_load_2d(st, &xmap, &full_[s], ks * kTcBK, t0);
+        sm100::tma_load_2d(st + kTcXBytes, &wmap, &full_[s], ks * kTcBK, 0);
+        issued = ks + 1;
+      }
+      // after a timeout elsewhere: the copies still in flight land before the CTA exits
+      for (int ks = issued - 1; ks >= 0 && ks >= issued - kTcStages; --ks)
+        if (!sm100::mbar_wait(&full_[ks % kTcStages], (ks / kTcStages) & 1, err, 14)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kTcTokens, E);
+      const uint64_t d0 = sm100::desc_sw128_kmajor(sm100::smem_addr(smem));
+      bool ok = true;
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        const int s = ks % kTcStages;
+        if (!(ok = sm100::mbar_wait(&full_[s], (ks / kTcStages) & 1, err, 14))) break;
+        sm100::tc_fence_after();
+        const uint64_t ad = d0 + (uint64_t)(s * (stage_bytes >> 4));
+        const uint64_t bd = ad + (uint64_t)(kTcXBytes >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kTcBK / 16; ++kk) sm100::umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+        sm100::umma_commit(&empty_[s]);
+      }
+      sm100::umma_commit(&acc_full);  // also after a timeout
+      sm100::mbar_wait(&acc_full, 0, err, 14);  // no MMA in flight when TMEM is released
+    }
+  } else {
+    // ---- row warps: thread = token row = TMEM lane
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const int t = t0 + row;
+    uint32_t amax = 0u;  // max |x| of the row as two packed bf16 magnitudes
+    bool ok = true;
+    for (int ks = 0; ks < KSTEPS && ok; ++ks) {
+      const int s = ks % kTcStages;
+      if (!(ok = sm100::mbar_wait(&full_[s], (ks / kTcStages) & 1, err, 14))) break;
+      // the row's 128 bytes (its 16-byte chunks are swizzled within the row
+      // and the maximum does not care about their order): iteration c reads
+      // chunk c ^ (row & 7), so the 8 rows of a quarter warp hit 8 distinct
+      // bank groups (all at chunk c: an 8-way conflict)
+      const uint4 *rp = reinterpret_cast<const uint4 *>(smem + (size_t)s * stage_bytes + (size_t)row * 128);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = rp[c ^ (row & 7)];
+        amax = __vmaxu2(amax, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                                       __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty_[s]);
+    }
+    sm100::mbar_wait(&acc_full, 0, err, 14);
+    sm100::tc_fence_after();
+    float v[EMAX];
+    {
+      uint32_t r[32];
+      sm100::tmem_ld_32_async(tmem + ((uint32_t)(q * 32) << 16), r);
+      sm100::tmem_wait_ld(r);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+      if constexpr (EMAX > 32) {
+        sm100::tmem_ld_32_async(tmem + ((uint32_t)(q * 32) << 16) + 32u, r);
+        sm100::tmem_wait_ld(r);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[32 + e] = __uint_as_float(r[e]);
+      }
+    }
+    sm100::tc_fence_before();
+    const bool valid = t < T;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e) {
+      if (e < E) {
+        v[e] += b ? bf16_to_f32(b[e]) : 0.f;
+        if (valid && logits_out) logits_out[(size_t)t * E + e] = v[e];
+        if (v[e] != v[e]) v[e] = -INFINITY;  // NaN ranks last, as in rank_topk_softmax
+      }
+    }
+    if (valid) {
+      const uint32_t m = max(amax & 0xFFFFu, amax >> 16);
+      sigma_out[t] = sigma_of(m >> 7);  // bf16 bits >> 7 = f32 exponent
+      // the k largest, ties to the lower expert (a stable descending sort)
+      float top_v[kMaxTopK];
+      int top_e[kMaxTopK];
+      uint64_t taken = 0ull;
+      for (int j = 0; j < k; ++j) {
+        int be = -1;
+        float bv = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < EMAX; ++e)
+          if (e < E && !((taken >> e) & 1ull) && (be < 0 || v[e] > bv)) {
+            be = e;
+            bv = v[e];
+          }
+        taken |= 1ull << be;
+        top_v[j] = bv;
+        top_e[j] = be;
+      }
+      float mx = -INFINITY;
+      for (int j = 0; j < k; ++j) mx = fmaxf(mx, top_v[j]);
+      float sum = 0.f;
+      for (int j = 0; j < k; ++j) {
+        top_v[j] = expf(top_v[j] - mx);
+        sum += top_v[j];
+      }
+      for (int j = 0; j < k; ++j) {
+        idx[(size_t)t * k + j] = top_e[j];
+        wts[(size_t)t * k + j] = sum == 0.f ? 1.0f / (float)k : top_v[j] / sum;
+        idx_s[row * k + j] = top_e[j];
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four row warps: every idx_s entry is written
+    // the counting sort's first half per 64-token unit: warp of quarter 0
+    // (rows 0-63) and of quarter 2 (rows 64-127)
+    if (q == 0 || q == 2) {
+      const int h = q >> 1, n_tok = min(64, T - (t0 + 64 * h));
+      if (n_tok > 0) {
+        int *cnt = cnt_s[h];
+        for (int e = lane; e < E; e += 32) cnt[e] = 0;
+        __syncwarp();
+        const int n_slots = n_tok * k;
+        const unsigned lt_mask = (1u << lane) - 1u;
+        for (int s0 = 0; s0 < n_slots; s0 += 32) {
+          const int sl = s0 + lane;
+          const bool sv = sl < n_slots;
+          const int e = sv ? idx_s[64 * h * k + sl] : E + lane;  // distinct dummies never match
+          const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+          const int prior = sv ? cnt[e] : 0;
+          __syncwarp();
+          if (sv) {
+            local_rank[(size_t)(t0 + 64 * h) * k + sl] = prior + __popc(peers & lt_mask);
+            if ((peers & lt_mask) == 0u) cnt[e] = prior + __popc(peers);
+          }
+          __syncwarp();
+        }
+        for (int e = lane; e < E; e += 32) cta_hist[(size_t)(2 * blockIdx.x + h) * E + e] = cnt[e];
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, EMAX);
+  }
+}
 }  // namespace
 
 cudaError_t launch_router_topk(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
@@ -330,13 +551,64 @@ bool router_mma_supported(int H, int E, int k) {
 
 int router_mma_ctas(int T) { return (T + kRmTokens - 1) / kRmTokens; }
 
+namespace {
+typedef CUresult (*RouterEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+RouterEncodeFn router_encode_fn() {
+  static RouterEncodeFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<RouterEncodeFn>(p);
+  }
+  return fn;
+}
+// [rows, cols] bf16 row-major, box [64 cols, box_rows], 128-byte swizzle (rows
+// past the end read as zeros).
+bool router_tmap(CUtensorMap *m, const void *base, int rows, int cols, int box_rows) {
+  RouterEncodeFn fn = router_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
 cudaError_t launch_router_mma(const uint16_t *x, const uint16_t *w, const uint16_t *b, int T, int H,
                               int E, int k, int32_t *idx, float *wts, float *logits,
                               int32_t *sigma, int32_t *cta_hist, int32_t *local_rank,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, int *err) {
   if (T == 0) return cudaSuccess;
   if (!router_mma_supported(H, E, k)) return cudaErrorInvalidValue;
   if ((uintptr_t)x & 15 || (uintptr_t)w & 15) return cudaErrorInvalidValue;
+  CUtensorMap xm, wm;
+  if (err && H % kTcBK == 0 && router_tmap(&xm, x, T, H, kTcTokens) && router_tmap(&wm, w, E, H, E)) {
+    // tcgen05: one CTA per 128 tokens
+    const int emax = E <= 32 ? 32 : 64;
+    const size_t smem = 1024 + (size_t)kTcStages * (kTcXBytes + (size_t)emax * kTcBK * 2);
+    const int grid = (T + kTcTokens - 1) / kTcTokens;
+    cudaError_t st;
+    if (emax == 32) {
+      st = cudaFuncSetAttribute(router_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (st != cudaSuccess) return st;
+      router_tc_kernel<32><<<grid, kTcThreads, smem, stream>>>(xm, wm, b, T, H, E, k, idx, wts, logits, sigma,
+                                                                cta_hist, local_rank, err);
+    } else {
+      st = cudaFuncSetAttribute(router_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (st != cudaSuccess) return st;
+      router_tc_kernel<64><<<grid, kTcThreads, smem, stream>>>(xm, wm, b, T, H, E, k, idx, wts, logits, sigma,
+                                                                cta_hist, local_rank, err);
+    }
+    return cudaGetLastError();
+  }
   const size_t smem = (size_t)kRmStages * (kRmTokens + E) * kRmKC * 2;
   cudaError_t st = cudaFuncSetAttribute(router_mma_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
