@@ -52,8 +52,8 @@ struct Layer {
 constexpr int kMaxBands = 1024;
 // Tokens per chunk of a host-buffer forward (oxg_moe_forward_host) when the
 // caller has not set one (a batch of T tokens runs in T / 1600 equal chunks).
-// Measured on gpt-oss-20b, 8192 tokens: 5 chunks of 1639 tokens 2.51 M
-// tokens/s, 4 of 2048 2.32 M, 8 of 1024 1.88 M — every chunk streams all the
+// Measured on gpt-oss-20b, 8192 tokens: 5 chunks of 1639 tokens 2.67 M
+// tokens/s, 4 of 2048 2.46 M, 8 of 1024 2.09 M — every chunk streams all the
 // expert weights again and below ~200 tokens per expert the prefill GEMMs'
 // 256-column tiles run half empty, while fewer chunks leave longer copies
 // that cannot overlap.
